@@ -1,0 +1,535 @@
+// Dense 1×1 and 3×3 convolutions as implicit GEMMs on the sm_100a tensor
+// cores (tcgen05.mma, TMEM accumulator, TMA-fed weights).
+//
+// GEMM view: M = output pixels (n·ho·wo, raster order), N = c_out,
+// K = taps·c_in walked in 32-channel chunks per tap (K chunk kc → tap
+// kc / cin_chunks, channels 32·(kc % cin_chunks)…). This is the reference's
+// im2col K order [ky, kx, c_in] (src/engine/conv.rs:145-165) without ever
+// materialising the patch matrix, and replaces its Winograd path
+// (src/engine/winograd.rs) for stride 1 / pad 1.
+//
+// CTA = one 128 × bn output tile; 6 warps:
+//   warps 0-3  producers: gather the A tile (128 pixels × 32 channels) from
+//              NHWC global memory — zero padding, stride, nearest-2× upsample
+//              and the optional GroupNorm prologue [SiLU](x·scale + shift)
+//              are all applied here — split each value into a TF32-exact
+//              high part and the f32 remainder, and store both into
+//              128-byte-swizzled K-major shared-memory tiles;
+//              afterwards the epilogue: TMEM → registers, + bias (+ residual),
+//              → global.
+//   warp 4     MMA issuer (one thread) + TMEM allocation.
+//   warp 5     TMA issuer (one thread) for the pre-split weight tiles.
+// Precision: f32 weights → 3×TF32 (a_hi·w_hi + a_hi·w_lo + a_lo·w_hi),
+// f16 weights (exact in TF32) → 2×TF32 (a_hi·w + a_lo·w); accumulation in
+// f32 in TMEM. Every mbarrier wait is bounded; on timeout the CTA records the
+// error in the context's device error word, skips its stores and exits.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "mbx_device.cuh"
+#include "mbx_internal.h"
+
+namespace mbx {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;                  // f32 elements per 128-byte swizzle row
+constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
+constexpr int kThreads = 192;
+constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
+constexpr int kMaxSmem = 232448;             // 227 KB opt-in limit per CTA
+
+struct ConvArgs {
+    const float* x;
+    int64_t m_total;
+    int h, w, c_in, ho, wo, stride, pad_t, pad_l, up;
+    int cin_chunks, k_chunks;
+    int c_out, bn, n_tiles, stages, tmem_cols;
+    const float* bias;
+    const float* residual;
+    float* out;
+    const float* pro_scale;
+    const float* pro_shift;
+    int pro_silu;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`. Returns false when the CTA is
+// aborting (another role gave up) or after kWaitLimit cycles, in which case
+// the error is recorded and the abort flag raised.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int site, volatile int* abort_flag,
+                                       bool honour_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (honour_abort && *abort_flag) return false;
+        if (clock64() - t0 > kWaitLimit) {
+            if (atomicCAS(err, 0, kErrWaitTimeout) == 0) {
+                err[1] = kKConvTc;
+                err[2] = site;
+            }
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_slot), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
+// 8-row groups 1024 bytes apart (SBO), LBO unused (1), sm_100 version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3ffffu) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t idesc_tf32(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xffffe000u); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+template <bool F32W, bool VEC4>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
+                   const ConvArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const int bn = args.bn;
+    const int stages = args.stages;
+    const uint32_t b_bytes = (uint32_t)bn * 128u;
+    const uint32_t stage_bytes = 2 * A_BYTES + (F32W ? 2 : 1) * b_bytes;
+    const uint32_t bars = base + (uint32_t)stages * stage_bytes;  // full[s], empty[s], done
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
+    const uint32_t done_bar = bars + 16u * stages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (done_bar + 8 - base));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (done_bar + 12 - base));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tile = blockIdx.x % args.n_tiles;
+    const int64_t m_tile = blockIdx.x / args.n_tiles;
+    const int64_t m0 = m_tile * BM;
+    const int n0 = n_tile * bn;
+    const int K = args.k_chunks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full_bar(s), 128 + 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(done_bar, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 4) {
+        tmem_alloc(smem_u32(tmem_slot), (uint32_t)args.tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 4) {
+        // ------------------------------------------------------------ producers
+        const int tid = threadIdx.x;
+        const int j = tid & 7;       // 16-byte chunk (4 channels) within the 128-byte row
+        const int rbase = tid >> 3;  // rows rbase + 16·i
+        const int hi_img = args.h << args.up, wi_img = args.w << args.up;
+        const int64_t hw_out = (int64_t)args.ho * args.wo;
+        int pb[8], iy0[8], ix0[8];
+        bool rv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t m = m0 + rbase + 16 * i;
+            rv[i] = m < args.m_total;
+            const int64_t mm = rv[i] ? m : 0;
+            const int64_t b = mm / hw_out;
+            const int64_t rem = mm - b * hw_out;
+            const int oy = (int)(rem / args.wo);
+            const int ox = (int)(rem - (int64_t)oy * args.wo);
+            pb[i] = (int)b;
+            iy0[i] = oy * args.stride - args.pad_t;
+            ix0[i] = ox * args.stride - args.pad_l;
+        }
+        const bool pro = args.pro_scale != nullptr;
+        for (int kc = 0; kc < K; ++kc) {
+            const int s = kc % stages;
+            if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
+            const int tap = kc / args.cin_chunks;
+            const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
+            const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+            float v[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int iy = iy0[i] + ky, ix = ix0[i] + kx;
+                const bool ok = rv[i] && iy >= 0 && iy < hi_img && ix >= 0 && ix < wi_img;
+                const int64_t pix = ((int64_t)pb[i] * args.h + (iy >> args.up)) * args.w + (ix >> args.up);
+                if constexpr (VEC4) {
+                    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (ok && c0 < args.c_in) {
+                        f = __ldg(reinterpret_cast<const float4*>(args.x + pix * args.c_in + c0));
+                        if (pro) {
+                            const float4 sc =
+                                __ldg(reinterpret_cast<const float4*>(args.pro_scale + (int64_t)pb[i] * args.c_in + c0));
+                            const float4 sh =
+                                __ldg(reinterpret_cast<const float4*>(args.pro_shift + (int64_t)pb[i] * args.c_in + c0));
+                            f = f4_fma(f, sc, sh);
+                            if (args.pro_silu) {
+                                f.x = dev_silu(f.x);
+                                f.y = dev_silu(f.y);
+                                f.z = dev_silu(f.z);
+                                f.w = dev_silu(f.w);
+                            }
+                        }
+                    }
+                    v[i][0] = f.x;
+                    v[i][1] = f.y;
+                    v[i][2] = f.z;
+                    v[i][3] = f.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int ch = c0 + e;
+                        float f = 0.0f;
+                        if (ok && ch < args.c_in) {
+                            f = __ldg(args.x + pix * args.c_in + ch);
+                            if (pro) {
+                                f = fmaf(f, __ldg(args.pro_scale + (int64_t)pb[i] * args.c_in + ch),
+                                         __ldg(args.pro_shift + (int64_t)pb[i] * args.c_in + ch));
+                                if (args.pro_silu) f = dev_silu(f);
+                            }
+                        }
+                        v[i][e] = f;
+                    }
+                }
+            }
+            const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
+            const uint32_t a_lo = a_hi + A_BYTES;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = rbase + 16 * i;
+                const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
+                const float h0 = tf32_hi(v[i][0]), h1 = tf32_hi(v[i][1]), h2 = tf32_hi(v[i][2]),
+                            h3 = tf32_hi(v[i][3]);
+                st_shared_v4(a_hi + off, h0, h1, h2, h3);
+                st_shared_v4(a_lo + off, v[i][0] - h0, v[i][1] - h1, v[i][2] - h2, v[i][3] - h3);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(full_bar(s));
+        }
+        // ------------------------------------------------------------ epilogue
+        const bool ok = mbar_wait(done_bar, 0, args.err, 2, abort_flag, false) && !*abort_flag;
+        tc_fence_after();
+        const int row = warp * 32 + lane;
+        const int64_t m = m0 + row;
+        const bool vec_out = (args.c_out & 3) == 0;
+        for (int cc = 0; cc < bn; cc += 32) {
+            float acc[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cc, acc);
+            if (!ok || m >= args.m_total) continue;
+            const int nb = n0 + cc;
+            if (nb >= args.c_out) continue;
+            float* dst = args.out + m * args.c_out + nb;
+            const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
+            if (vec_out && nb + 32 <= args.c_out) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + q)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (res) {
+                        const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + q);
+                        pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
+                    }
+                    reinterpret_cast<float4*>(dst)[q] = make_float4(pre.x + acc[4 * q], pre.y + acc[4 * q + 1],
+                                                                    pre.z + acc[4 * q + 2], pre.w + acc[4 * q + 3]);
+                }
+            } else {
+                const int lim = min(32, args.c_out - nb);
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                    if (q < lim) {
+                        float pre = args.bias ? __ldg(args.bias + nb + q) : 0.0f;
+                        if (res) pre = __ldg(res + q) + pre;
+                        dst[q] = pre + acc[q];
+                    }
+                }
+            }
+        }
+    } else if (warp == 4) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32(bn);
+            for (int kc = 0; kc < K; ++kc) {
+                const int s = kc % stages;
+                if (!mbar_wait(full_bar(s), (kc / stages) & 1, args.err, 3, abort_flag, true)) break;
+                tc_fence_after();
+                const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
+                const uint32_t a_lo = a_hi + A_BYTES;
+                const uint32_t b_hi = a_hi + 2 * A_BYTES;
+                const uint32_t b_lo = b_hi + b_bytes;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint32_t koff = (uint32_t)kk * 32u;
+                    const uint64_t adh = sw128_desc(a_hi + koff), adl = sw128_desc(a_lo + koff);
+                    const uint64_t bdh = sw128_desc(b_hi + koff);
+                    const uint32_t first = (kc > 0 || kk > 0) ? 1u : 0u;
+                    if constexpr (F32W) {
+                        const uint64_t bdl = sw128_desc(b_lo + koff);
+                        mma_tf32(tmem, adl, bdh, idesc, first);
+                        mma_tf32(tmem, adh, bdl, idesc, 1u);
+                        mma_tf32(tmem, adh, bdh, idesc, 1u);
+                    } else {
+                        mma_tf32(tmem, adl, bdh, idesc, first);
+                        mma_tf32(tmem, adh, bdh, idesc, 1u);
+                    }
+                }
+                mma_commit(empty_bar(s));
+            }
+            mma_commit(done_bar);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ TMA issuer
+        if (lane == 0) {
+            for (int kc = 0; kc < K; ++kc) {
+                const int s = kc % stages;
+                if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 4, abort_flag, true)) break;
+                const uint32_t b_hi = base + (uint32_t)s * stage_bytes + 2 * A_BYTES;
+                mbar_arrive_expect_tx(full_bar(s), (F32W ? 2u : 1u) * b_bytes);
+                tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, full_bar(s));
+                if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, full_bar(s));
+            }
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tmem, (uint32_t)args.tmem_cols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q),
+                   "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+        if (q != cudaDriverEntryPointSuccess || !p) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+void encode_one(CUtensorMap* map, const float* data, int64_t kdim, int64_t rows, int bn) {
+    cuuint64_t dims[2] = {(cuuint64_t)kdim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kdim * 4};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(data), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+}
+
+int stage_count(bool f32w, int bn) {
+    const int stage = 2 * (int)A_BYTES + (f32w ? 2 : 1) * bn * 128;
+    return std::min(6, (kMaxSmem - 2048) / stage);
+}
+
+template <bool F32W, bool VEC4>
+void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_tiles) {
+    auto kernel = conv_tc_kernel<F32W, VEC4>;
+    const int stage = 2 * (int)A_BYTES + (F32W ? 2 : 1) * a.bn * 128;
+    const int smem = a.stages * stage + 1024 + 256;
+    static bool configured = false;
+    if (!configured) {
+        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
+                   "conv smem attribute");
+        configured = true;
+    }
+    const int64_t blocks = m_tiles * a.n_tiles;
+    kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, a);
+}
+
+}  // namespace
+
+int choose_bn(int64_t c_out) {
+    int best = 32;
+    int64_t best_cost = INT64_MAX;
+    for (int bn = 256; bn >= 32; bn -= 32) {
+        const int64_t tiles = (c_out + bn - 1) / bn;
+        const int64_t cost = tiles * bn + 32 * tiles;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+void encode_param_tmaps(mbx_param* p) {
+    const int64_t kdim = p->taps * p->cin_pad;
+    encode_one(&p->tmap_hi, p->hi, kdim, p->cout_pad, p->bn);
+    if (p->lo)
+        encode_one(&p->tmap_lo, p->lo, kdim, p->cout_pad, p->bn);
+    else
+        p->tmap_lo = p->tmap_hi;
+}
+
+void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
+                    const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
+                    float* out) {
+    ConvArgs a{};
+    a.x = x;
+    a.m_total = s.n * s.ho * s.wo;
+    a.h = (int)s.h;
+    a.w = (int)s.w;
+    a.c_in = (int)s.c_in;
+    a.ho = (int)s.ho;
+    a.wo = (int)s.wo;
+    a.stride = s.stride;
+    a.pad_t = s.pad_t;
+    a.pad_l = s.pad_l;
+    a.up = s.up;
+    a.cin_chunks = p->cin_pad / BK;
+    a.k_chunks = (int)p->taps * a.cin_chunks;
+    a.c_out = (int)p->c_out;
+    a.bn = p->bn;
+    a.n_tiles = p->cout_pad / p->bn;
+    const bool f32w = p->lo != nullptr;
+    a.stages = stage_count(f32w, p->bn);
+    a.tmem_cols = 32;
+    while (a.tmem_cols < p->bn) a.tmem_cols <<= 1;
+    a.bias = bias;
+    a.residual = residual;
+    a.out = out;
+    a.pro_scale = pro_scale;
+    a.pro_shift = pro_shift;
+    a.pro_silu = pro_silu ? 1 : 0;
+    a.err = ctx->dev_err;
+    MBX_REQUIRE(a.m_total < (int64_t(1) << 40), "conv: too many output pixels");
+    const int64_t m_tiles = (a.m_total + BM - 1) / BM;
+    MBX_REQUIRE(m_tiles * a.n_tiles < (int64_t(1) << 31), "conv: grid too large");
+    const bool vec4 = (s.c_in & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                      (!pro_scale || ((reinterpret_cast<uintptr_t>(pro_scale) & 15) == 0 &&
+                                      (reinterpret_cast<uintptr_t>(pro_shift) & 15) == 0));
+    const bool aligned_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                             (!residual || (reinterpret_cast<uintptr_t>(residual) & 15) == 0) &&
+                             (!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+    MBX_REQUIRE(aligned_out || (p->c_out & 3) != 0,
+                "conv: out, residual and bias must be 16-byte aligned when c_out is a multiple of 4");
+    if (f32w)
+        vec4 ? run_conv<true, true>(ctx, p, a, m_tiles) : run_conv<true, false>(ctx, p, a, m_tiles);
+    else
+        vec4 ? run_conv<false, true>(ctx, p, a, m_tiles) : run_conv<false, false>(ctx, p, a, m_tiles);
+    after_launch(ctx, "conv (tcgen05)");
+}
+
+}  // namespace mbx

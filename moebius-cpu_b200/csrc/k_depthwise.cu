@@ -1,0 +1,186 @@
+// Depthwise 3×3, stride 1, zero padding 1, NHWC, bias and a fused epilogue
+// (reference src/engine/depthwise.rs:31-185).
+//
+// Each thread owns one channel vector (4 channels, or 1 for channel counts
+// that are not multiples of 4) at one x position and walks a strip of output
+// rows with a 3×3 register window: every step loads only the new input row's
+// three pixels (the left and right ones are the neighbouring threads' centre
+// pixels, so they come from L1), so DRAM traffic is about one read of the
+// input plus one write of the output. Taps are accumulated bias-first in
+// (ky, kx) order with fma(tap, x, acc) as in acc_block (:112-143); padding
+// taps contribute nothing.
+#include "mbx_device.cuh"
+#include "mbx_internal.h"
+
+namespace mbx {
+namespace {
+
+constexpr int kDwThreads = 256;
+constexpr int kDwRows = 16;  // output rows per thread strip
+
+template <int V>
+struct Vec {
+    float v[V];
+};
+
+template <int V>
+__device__ __forceinline__ Vec<V> vload(const float* p) {
+    Vec<V> r;
+    if constexpr (V == 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(p));
+        r.v[0] = f.x;
+        r.v[1] = f.y;
+        r.v[2] = f.z;
+        r.v[3] = f.w;
+    } else {
+        r.v[0] = __ldg(p);
+    }
+    return r;
+}
+
+template <int V>
+__device__ __forceinline__ Vec<V> vzero() {
+    Vec<V> r;
+#pragma unroll
+    for (int k = 0; k < V; ++k) r.v[k] = 0.0f;
+    return r;
+}
+
+template <int V>
+__device__ __forceinline__ void vstore(float* p, const Vec<V>& a) {
+    if constexpr (V == 4)
+        stg_stream(reinterpret_cast<float4*>(p), make_float4(a.v[0], a.v[1], a.v[2], a.v[3]));
+    else
+        *p = a.v[0];
+}
+
+// Loads row `iy` at columns ix-1, ix, ix+1 for channel offset `ch` (zero when padded).
+template <int V>
+__device__ __forceinline__ void load_row(const float* __restrict__ xb, int h, int w, int c, int iy, int ix, int ch,
+                                         Vec<V> (&row)[3]) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int xx = ix + k - 1;
+        row[k] = (iy >= 0 && iy < h && xx >= 0 && xx < w) ? vload<V>(xb + ((int64_t)iy * w + xx) * c + ch)
+                                                          : vzero<V>();
+    }
+}
+
+template <int V>
+__device__ __forceinline__ Vec<V> taps(const Vec<V> (&win)[3][3], const Vec<V> (&wt)[9], const Vec<V>& bias,
+                                       bool top, bool bottom, bool left, bool right) {
+    Vec<V> acc = bias;
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+        if ((ky == 0 && !top) || (ky == 2 && !bottom)) continue;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            if ((kx == 0 && !left) || (kx == 2 && !right)) continue;
+#pragma unroll
+            for (int k = 0; k < V; ++k) acc.v[k] = fmaf(wt[ky * 3 + kx].v[k], win[ky][kx].v[k], acc.v[k]);
+        }
+    }
+    return acc;
+}
+
+// grid: x = output channel-vector blocks, y = x-position blocks, z = item × strip.
+template <int V, int EPI>
+__global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restrict__ x, int h, int w, int c,
+                                                           const float* __restrict__ weight,
+                                                           const float* __restrict__ bias, float* __restrict__ out,
+                                                           int qb, int strips) {
+    constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
+    const int c_out = kGlu ? c / 2 : c;
+    const int cvo = c_out / V;
+    const int xb = kDwThreads / qb;
+    const int t = threadIdx.x;
+    if (t >= qb * xb) return;
+    const int qv = blockIdx.x * qb + t % qb;
+    const int ox = blockIdx.y * xb + t / qb;
+    if (qv >= cvo || ox >= w) return;
+    const int b = blockIdx.z / strips;
+    const int y0 = (blockIdx.z % strips) * kDwRows;
+    const int y1 = min(y0 + kDwRows, h);
+    const int ch = qv * V;
+    const float* xb_ = x + (int64_t)b * h * w * c;
+
+    Vec<V> wt[9], bs, wg[9], bg;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) wt[k] = vload<V>(weight + k * c + ch);
+    bs = vload<V>(bias + ch);
+    if constexpr (kGlu) {
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wg[k] = vload<V>(weight + k * c + c_out + ch);
+        bg = vload<V>(bias + c_out + ch);
+    }
+    Vec<V> win[3][3], gwin[3][3];
+    load_row<V>(xb_, h, w, c, y0 - 1, ox, ch, win[0]);
+    load_row<V>(xb_, h, w, c, y0, ox, ch, win[1]);
+    if constexpr (kGlu) {
+        load_row<V>(xb_, h, w, c, y0 - 1, ox, c_out + ch, gwin[0]);
+        load_row<V>(xb_, h, w, c, y0, ox, c_out + ch, gwin[1]);
+    }
+    const bool left = ox > 0, right = ox + 1 < w;
+    for (int y = y0; y < y1; ++y) {
+        load_row<V>(xb_, h, w, c, y + 1, ox, ch, win[2]);
+        if constexpr (kGlu) load_row<V>(xb_, h, w, c, y + 1, ox, c_out + ch, gwin[2]);
+        const bool top = y > 0, bottom = y + 1 < h;
+        Vec<V> acc = taps<V>(win, wt, bs, top, bottom, left, right);
+        if constexpr (EPI == MBX_EPILOGUE_RELU) {
+#pragma unroll
+            for (int k = 0; k < V; ++k) acc.v[k] = fmaxf(acc.v[k], 0.0f);
+        } else if constexpr (kGlu) {
+            const Vec<V> g = taps<V>(gwin, wg, bg, top, bottom, left, right);
+#pragma unroll
+            for (int k = 0; k < V; ++k) acc.v[k] = acc.v[k] * dev_silu(g.v[k]);
+        }
+        vstore<V>(out + (((int64_t)b * h + y) * w + ox) * c_out + ch, acc);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            win[0][k] = win[1][k];
+            win[1][k] = win[2][k];
+            if constexpr (kGlu) {
+                gwin[0][k] = gwin[1][k];
+                gwin[1][k] = gwin[2][k];
+            }
+        }
+    }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                         const float* weight, const float* bias, int epilogue, float* out) {
+    MBX_REQUIRE(h < (1 << 20) && w < (1 << 20) && c < (1 << 20), "depthwise: dimension too large");
+    const int64_t c_out = epilogue == MBX_EPILOGUE_GLU_SILU ? c / 2 : c;
+    const bool vec = c % 4 == 0 && c_out % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(weight) &&
+                     aligned16(bias);
+    const int V = vec ? 4 : 1;
+    const int64_t cvo = c_out / V;
+    const int qb = (int)std::min<int64_t>(cvo, 32);
+    const int xb = kDwThreads / qb;
+    const int64_t strips = (h + kDwRows - 1) / kDwRows;
+    MBX_REQUIRE(n * strips < (int64_t(1) << 31) && (cvo + qb - 1) / qb < (int64_t(1) << 31),
+                "depthwise: grid too large");
+    MBX_REQUIRE((w + xb - 1) / xb < 65536 && n * strips < 65536 * 32768LL, "depthwise: grid too large");
+    dim3 grid((unsigned)((cvo + qb - 1) / qb), (unsigned)((w + xb - 1) / xb), (unsigned)(n * strips));
+    MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h/16) must be <= 65535)");
+    const int hh = (int)h, ww = (int)w, cc = (int)c, st = (int)strips;
+#define MBX_DW(VV, EE) \
+    dw3x3_kernel<VV, EE><<<grid, kDwThreads, 0, ctx->stream>>>(x, hh, ww, cc, weight, bias, out, qb, st)
+    if (V == 4) {
+        if (epilogue == MBX_EPILOGUE_NONE) MBX_DW(4, MBX_EPILOGUE_NONE);
+        else if (epilogue == MBX_EPILOGUE_RELU) MBX_DW(4, MBX_EPILOGUE_RELU);
+        else MBX_DW(4, MBX_EPILOGUE_GLU_SILU);
+    } else {
+        if (epilogue == MBX_EPILOGUE_NONE) MBX_DW(1, MBX_EPILOGUE_NONE);
+        else if (epilogue == MBX_EPILOGUE_RELU) MBX_DW(1, MBX_EPILOGUE_RELU);
+        else MBX_DW(1, MBX_EPILOGUE_GLU_SILU);
+    }
+#undef MBX_DW
+    after_launch(ctx, "depthwise3x3");
+}
+
+}  // namespace mbx

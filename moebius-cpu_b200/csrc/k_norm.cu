@@ -1,0 +1,346 @@
+// GroupNorm (stats pass + fused apply) and LayerNorm for NHWC float32.
+//
+// GroupNorm follows the reference's numerics (src/engine/norm.rs:57-129):
+// per-channel f32 partial Σy, Σy² over 256-pixel chunks (y = x + add[item]),
+// folded into f64 per group, chunk partials summed in f64 in chunk order
+// (deterministic: no atomics), var = E[y²] − mean² clamped at 0. The apply
+// pass is out = [SiLU](x·scale + shift) (+ residual) with 128-bit accesses.
+#include <algorithm>
+
+#include "mbx_device.cuh"
+#include "mbx_internal.h"
+
+namespace mbx {
+namespace {
+
+constexpr int kGnChunk = 256;   // pixels per stats task (the reference's STATS_CHUNK)
+constexpr int kGnThreads = 256;
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// One CTA per (pixel chunk, item). V = 4 (float4 lanes over channels) or 1.
+template <int V, bool ADD>
+__global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __restrict__ x, int64_t hw, int c,
+                                                                 int groups, const float* __restrict__ add,
+                                                                 double* __restrict__ part) {
+    extern __shared__ float red[];  // [2][rows][c]
+    const int cv = c / V;
+    const int64_t chunk = blockIdx.x, b = blockIdx.y, chunks = gridDim.x;
+    const int64_t p0 = chunk * kGnChunk;
+    const int npx = (int)(hw - p0 < kGnChunk ? hw - p0 : kGnChunk);
+    const int t = threadIdx.x;
+    const bool narrow = cv <= kGnThreads;
+    const int rows = narrow ? kGnThreads / cv : 1;
+    const int r = narrow ? t / cv : 0;
+    float* rs = red;
+    float* rq = red + rows * c;
+    const float* xb = x + (b * hw + p0) * (int64_t)c;
+    if (r < rows) {
+        for (int j = narrow ? t % cv : t; j < cv; j += narrow ? cv : kGnThreads) {
+            float s[V], q[V], a[V];
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                s[k] = 0.0f;
+                q[k] = 0.0f;
+                a[k] = ADD ? add[b * c + j * V + k] : 0.0f;
+            }
+#pragma unroll 8
+            for (int p = r; p < npx; p += rows) {
+                float v[V];
+                if constexpr (V == 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(xb + (int64_t)p * c) + j);
+                    v[0] = f.x;
+                    v[1] = f.y;
+                    v[2] = f.z;
+                    v[3] = f.w;
+                } else {
+                    v[0] = __ldg(xb + (int64_t)p * c + j);
+                }
+#pragma unroll
+                for (int k = 0; k < V; ++k) {
+                    const float y = ADD ? v[k] + a[k] : v[k];
+                    s[k] += y;
+                    q[k] = fmaf(y, y, q[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                rs[r * c + j * V + k] = s[k];
+                rq[r * c + j * V + k] = q[k];
+            }
+        }
+    }
+    __syncthreads();
+    // Per-channel chunk partial (f32, in row order), kept in row 0.
+    for (int ch = t; ch < c; ch += kGnThreads) {
+        float s = rs[ch], q = rq[ch];
+        for (int rr = 1; rr < rows; ++rr) {
+            s += rs[rr * c + ch];
+            q += rq[rr * c + ch];
+        }
+        rs[ch] = s;
+        rq[ch] = q;
+    }
+    __syncthreads();
+    // f64 fold per group (src/engine/norm.rs:78-80).
+    const int cg = c / groups;
+    for (int g = t; g < groups; g += kGnThreads) {
+        double ss = 0.0, qq = 0.0;
+        for (int ch = g * cg; ch < (g + 1) * cg; ++ch) {
+            ss += (double)rs[ch];
+            qq += (double)rq[ch];
+        }
+        double* dst = part + ((b * chunks + chunk) * groups + g) * 2;
+        dst[0] = ss;
+        dst[1] = qq;
+    }
+}
+
+// One CTA per item: chunk partials → mean / rstd → per-channel scale, shift
+// (src/engine/norm.rs:91-102).
+__global__ void gn_finalize_kernel(const double* __restrict__ part, int64_t chunks, int64_t hw, int c, int groups,
+                                   float eps, const float* __restrict__ gamma, const float* __restrict__ beta,
+                                   const float* __restrict__ add, float* __restrict__ scale,
+                                   float* __restrict__ shift) {
+    extern __shared__ double gstat[];  // [groups][2] = mean, rstd
+    const int64_t b = blockIdx.x;
+    const int cg = c / groups;
+    const double count = (double)hw * (double)cg;
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+        double sum = 0.0, sumsq = 0.0;
+        for (int64_t ch = 0; ch < chunks; ++ch) {
+            const double* src = part + ((b * chunks + ch) * groups + g) * 2;
+            sum += src[0];
+            sumsq += src[1];
+        }
+        const double mean = sum / count;
+        const double var = fmax(sumsq / count - mean * mean, 0.0);
+        gstat[2 * g] = mean;
+        gstat[2 * g + 1] = 1.0 / sqrt(var + (double)eps);
+    }
+    __syncthreads();
+    for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+        const int g = ch / cg;
+        const double mean = gstat[2 * g], rstd = gstat[2 * g + 1];
+        const double sc = rstd * (double)gamma[ch];
+        const double pre = add ? (double)add[b * c + ch] : 0.0;
+        scale[b * c + ch] = (float)sc;
+        shift[b * c + ch] = (float)((double)beta[ch] + (pre - mean) * sc);
+    }
+}
+
+template <int V, bool SILU, bool RES>
+__global__ void gn_apply_kernel(const float* __restrict__ x, int64_t hw, int64_t c, const float* __restrict__ scale,
+                                const float* __restrict__ shift, const float* __restrict__ residual,
+                                float* __restrict__ out, int64_t total_v) {
+    const int64_t cv = c / V;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_v;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t q = i % cv;
+        const int64_t item = i / (hw * cv);
+        if constexpr (V == 4) {
+            const float4 v = ldg_stream(reinterpret_cast<const float4*>(x) + i);
+            const float4 a = __ldg(reinterpret_cast<const float4*>(scale + item * c) + q);
+            const float4 s = __ldg(reinterpret_cast<const float4*>(shift + item * c) + q);
+            float4 y = f4_fma(v, a, s);
+            if (SILU) {
+                y.x = dev_silu(y.x);
+                y.y = dev_silu(y.y);
+                y.z = dev_silu(y.z);
+                y.w = dev_silu(y.w);
+            }
+            if (RES) {
+                const float4 r = ldg_stream(reinterpret_cast<const float4*>(residual) + i);
+                y.x += r.x;
+                y.y += r.y;
+                y.z += r.z;
+                y.w += r.w;
+            }
+            stg_stream(reinterpret_cast<float4*>(out) + i, y);
+        } else {
+            float y = fmaf(x[i], scale[item * c + q], shift[item * c + q]);
+            if (SILU) y = dev_silu(y);
+            if (RES) y += residual[i];
+            out[i] = y;
+        }
+    }
+}
+
+// LayerNorm, one warp per token, NV float4 per lane held in registers.
+template <int NV>
+__global__ void ln_warp_kernel(const float* __restrict__ x, int64_t tokens, int c, const float* __restrict__ gamma,
+                               const float* __restrict__ beta, float eps, float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int cv = c / 4;
+    for (int64_t tok = warp; tok < tokens; tok += nwarps) {
+        const float4* src = reinterpret_cast<const float4*>(x + tok * c);
+        float4 v[NV];
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int j = lane + 32 * i;
+            v[i] = j < cv ? ldg_stream(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum / (float)c;
+        float vs = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int j = lane + 32 * i;
+            if (j < cv) {
+                const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+                vs += (a * a + b * b) + (cc * cc + d * d);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+        const float rstd = 1.0f / sqrtf(vs / (float)c + eps);
+        float4* dst = reinterpret_cast<float4*>(out + tok * c);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int j = lane + 32 * i;
+            if (j < cv) {
+                const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + j);
+                const float4 bb = __ldg(reinterpret_cast<const float4*>(beta) + j);
+                float4 y;
+                y.x = fmaf((v[i].x - mean) * rstd, g.x, bb.x);
+                y.y = fmaf((v[i].y - mean) * rstd, g.y, bb.y);
+                y.z = fmaf((v[i].z - mean) * rstd, g.z, bb.z);
+                y.w = fmaf((v[i].w - mean) * rstd, g.w, bb.w);
+                stg_stream(dst + j, y);
+            }
+        }
+    }
+}
+
+// Any channel count: one warp per token, three passes over the row.
+__global__ void ln_generic_kernel(const float* __restrict__ x, int64_t tokens, int c, const float* __restrict__ gamma,
+                                  const float* __restrict__ beta, float eps, float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t tok = warp; tok < tokens; tok += nwarps) {
+        const float* s = x + tok * c;
+        float sum = 0.0f;
+        for (int j = lane; j < c; j += 32) sum += s[j];
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum / (float)c;
+        float vs = 0.0f;
+        for (int j = lane; j < c; j += 32) vs += (s[j] - mean) * (s[j] - mean);
+        for (int o = 16; o > 0; o >>= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+        const float rstd = 1.0f / sqrtf(vs / (float)c + eps);
+        for (int j = lane; j < c; j += 32) out[tok * c + j] = fmaf((s[j] - mean) * rstd, gamma[j], beta[j]);
+    }
+}
+
+}  // namespace
+
+int64_t gn_chunks(int64_t hw) { return (hw + kGnChunk - 1) / kGnChunk; }
+
+void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                        const float* add, double* part) {
+    const int64_t chunks = gn_chunks(hw);
+    MBX_REQUIRE(chunks < (int64_t(1) << 31) && n < 65536, "GroupNorm tensor too large");
+    const bool vec = c % 4 == 0 && aligned16(x) && (!add || aligned16(add));
+    const int V = vec ? 4 : 1;
+    const int64_t cv = c / V;
+    const int rows = cv <= kGnThreads ? int(kGnThreads / cv) : 1;
+    const size_t smem = size_t(2) * rows * c * sizeof(float);
+    dim3 grid((unsigned)chunks, (unsigned)n);
+    auto run = [&](auto kernel) {
+        if (smem > 48 * 1024)
+            check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "gn smem attribute");
+        kernel<<<grid, kGnThreads, smem, ctx->stream>>>(x, hw, (int)c, (int)groups, add, part);
+    };
+    if (vec)
+        add ? run(gn_partials_kernel<4, true>) : run(gn_partials_kernel<4, false>);
+    else
+        add ? run(gn_partials_kernel<1, true>) : run(gn_partials_kernel<1, false>);
+    after_launch(ctx, "group_norm partials");
+}
+
+void launch_gn_finalize(mbx_ctx* ctx, const double* part, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                        float eps, const float* gamma, const float* beta, const float* add, float* scale,
+                        float* shift) {
+    gn_finalize_kernel<<<(unsigned)n, 256, groups * 2 * sizeof(double), ctx->stream>>>(
+        part, gn_chunks(hw), hw, (int)c, (int)groups, eps, gamma, beta, add, scale, shift);
+    after_launch(ctx, "group_norm finalize");
+}
+
+void launch_gn_apply(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* scale,
+                     const float* shift, bool silu, const float* residual, float* out) {
+    const int64_t total = n * hw * c;
+    const bool vec = c % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) &&
+                     (!residual || aligned16(residual));
+    const int threads = 256;
+    if (vec) {
+        const int64_t tv = total / 4;
+        const int grid = grid_for(ctx, tv, threads);
+        if (silu)
+            residual ? gn_apply_kernel<4, true, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                         residual, out, tv)
+                     : gn_apply_kernel<4, true, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                          residual, out, tv);
+        else
+            residual ? gn_apply_kernel<4, false, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                          residual, out, tv)
+                     : gn_apply_kernel<4, false, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                           residual, out, tv);
+    } else {
+        const int grid = grid_for(ctx, total, threads);
+        if (silu)
+            residual ? gn_apply_kernel<1, true, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                         residual, out, total)
+                     : gn_apply_kernel<1, true, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                          residual, out, total);
+        else
+            residual ? gn_apply_kernel<1, false, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                          residual, out, total)
+                     : gn_apply_kernel<1, false, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
+                                                                                           residual, out, total);
+    }
+    after_launch(ctx, "group_norm apply");
+}
+
+void launch_layer_norm(mbx_ctx* ctx, const float* x, int64_t tokens, int64_t c, const float* gamma,
+                       const float* beta, float eps, float* out) {
+    const int threads = 256;
+    const int grid = grid_for(ctx, tokens, threads / 32);
+    const bool vec = c % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(gamma) && aligned16(beta);
+    const int nv = (int)((c / 4 + 31) / 32);
+    if (vec && nv <= 16) {
+        switch (nv) {
+#define MBX_LN_CASE(NV)                                                                                  \
+    case NV:                                                                                             \
+        ln_warp_kernel<NV><<<grid, threads, 0, ctx->stream>>>(x, tokens, (int)c, gamma, beta, eps, out); \
+        break;
+            MBX_LN_CASE(1)
+            MBX_LN_CASE(2)
+            MBX_LN_CASE(3)
+            MBX_LN_CASE(4)
+            MBX_LN_CASE(5)
+            MBX_LN_CASE(6)
+            MBX_LN_CASE(7)
+            MBX_LN_CASE(8)
+            MBX_LN_CASE(9)
+            MBX_LN_CASE(10)
+            MBX_LN_CASE(11)
+            MBX_LN_CASE(12)
+            MBX_LN_CASE(13)
+            MBX_LN_CASE(14)
+            MBX_LN_CASE(15)
+            MBX_LN_CASE(16)
+#undef MBX_LN_CASE
+        }
+    } else {
+        ln_generic_kernel<<<grid, threads, 0, ctx->stream>>>(x, tokens, (int)c, gamma, beta, eps, out);
+    }
+    after_launch(ctx, "layer_norm");
+}
+
+}  // namespace mbx

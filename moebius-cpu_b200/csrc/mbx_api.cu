@@ -1,0 +1,627 @@
+// The C ABI of moebius-cuda: context, memory pool, params and the kernel
+// entry points. Argument checks mirror the reference engine's asserts; the
+// kernels themselves live in k_*.cu.
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "mbx_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t set_error(int32_t code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+// Runs `f`, converting exceptions into status codes (src/ffi.rs:90-103 convention).
+template <class F>
+int32_t guard(F&& f) {
+    try {
+        f();
+        return MBX_OK;
+    } catch (const mbx::Error& e) {
+        return set_error(e.code, e.what());
+    } catch (const std::bad_alloc&) {
+        return set_error(MBX_ERR_OUT_OF_MEMORY, "host allocation failed");
+    } catch (const std::exception& e) {
+        return set_error(MBX_ERR_INTERNAL, std::string("internal error: ") + e.what());
+    } catch (...) {
+        return set_error(MBX_ERR_INTERNAL, "internal error");
+    }
+}
+
+void require_ctx(const mbx_ctx* ctx) { MBX_REQUIRE(ctx != nullptr, "null context"); }
+
+void use_device(const mbx_ctx* ctx) { mbx::check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
+
+void require_ptr(const void* p, const char* what) {
+    MBX_REQUIRE(p != nullptr, std::string("null pointer: ") + what);
+}
+
+// IEEE binary16 -> binary32 (exact).
+float half_bits_to_float(uint16_t h) {
+    uint32_t sign = uint32_t(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t man = h & 0x3ffu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int e = -1;
+            do {
+                man <<= 1;
+                ++e;
+            } while (!(man & 0x400u));
+            bits = sign | uint32_t(127 - 15 - e) << 23 | (man & 0x3ffu) << 13;
+        }
+    } else if (exp == 0x1f) {
+        bits = sign | 0x7f800000u | man << 13;
+    } else {
+        bits = sign | (exp + 127 - 15) << 23 | man << 13;
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// High part exactly representable in TF32 (low 13 mantissa bits cleared).
+inline float tf32_hi(float v) {
+    uint32_t b;
+    std::memcpy(&b, &v, 4);
+    b &= 0xffffe000u;
+    float r;
+    std::memcpy(&r, &b, 4);
+    return r;
+}
+
+}  // namespace
+
+namespace mbx {
+
+Pool::~Pool() {
+    for (auto& kv : free_) cudaFree(kv.second);
+    for (auto& kv : used_) cudaFree(kv.first);
+}
+
+void* Pool::alloc(size_t bytes) {
+    std::lock_guard<std::mutex> lock(mu_);
+    if (bytes == 0) bytes = 256;
+    bytes = (bytes + 511) & ~size_t(511);
+    // Best fit (Scratch::tensor_for, src/engine/mod.rs:61-66 / best_fit :104-117):
+    // the smallest cached block that holds `bytes`, unless it wastes more than half.
+    auto it = free_.lower_bound(bytes);
+    if (it != free_.end() && it->first <= 2 * bytes + (size_t(1) << 20)) {
+        void* p = it->second;
+        size_t sz = it->first;
+        free_.erase(it);
+        cached_ -= sz;
+        used_[p] = sz;
+        in_use_ += sz;
+        return p;
+    }
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        // Give cached memory back and retry once.
+        for (auto& kv : free_) cudaFree(kv.second);
+        free_.clear();
+        cached_ = 0;
+        e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            fail(MBX_ERR_OUT_OF_MEMORY, "device allocation of " + std::to_string(bytes) + " bytes failed");
+        }
+    }
+    used_[p] = bytes;
+    in_use_ += bytes;
+    return p;
+}
+
+void Pool::free(void* p) {
+    std::lock_guard<std::mutex> lock(mu_);
+    auto it = used_.find(p);
+    if (it == used_.end()) fail(MBX_ERR_INVALID_ARGUMENT, "mbx_free: pointer not from this context's pool");
+    free_.emplace(it->second, p);
+    cached_ += it->second;
+    in_use_ -= it->second;
+    used_.erase(it);
+}
+
+void Pool::release_below(size_t min_bytes) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (auto it = free_.begin(); it != free_.end();) {
+        if (it->first < min_bytes) {
+            cudaFree(it->second);
+            cached_ -= it->first;
+            it = free_.erase(it);
+        } else {
+            ++it;
+        }
+    }
+}
+
+// Scoped pool allocation for per-call scratch (stream-ordered reuse).
+struct PoolBuf {
+    mbx_ctx* ctx;
+    void* p;
+    PoolBuf(mbx_ctx* c, size_t bytes) : ctx(c), p(c->pool->alloc(bytes)) {}
+    ~PoolBuf() {
+        try {
+            ctx->pool->free(p);
+        } catch (...) {
+        }
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(p);
+    }
+};
+
+}  // namespace mbx
+
+using mbx::check_cuda;
+
+extern "C" {
+
+uint32_t mbx_abi_version(void) { return MBX_ABI_VERSION; }
+
+const char* mbx_last_error(void) { return g_last_error.c_str(); }
+
+int32_t mbx_ctx_create(int32_t device, mbx_ctx** out) {
+    return guard([&] {
+        require_ptr(out, "out");
+        *out = nullptr;
+        int count = 0;
+        cudaError_t e = cudaGetDeviceCount(&count);
+        if (e != cudaSuccess || count == 0) {
+            (void)cudaGetLastError();
+            mbx::fail(MBX_ERR_UNSUPPORTED_DEVICE, "no CUDA device available");
+        }
+        MBX_REQUIRE(device >= 0 && device < count, "device index out of range");
+        cudaDeviceProp prop;
+        check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10 || prop.minor != 0)
+            mbx::fail(MBX_ERR_UNSUPPORTED_DEVICE, std::string("moebius-cuda needs an sm_100 GPU (B200); device is ") +
+                                                      prop.name + " sm_" + std::to_string(prop.major) +
+                                                      std::to_string(prop.minor));
+        check_cuda(cudaSetDevice(device), "cudaSetDevice");
+        auto* ctx = new mbx_ctx();
+        ctx->device = device;
+        ctx->sm_count = prop.multiProcessorCount;
+        try {
+            check_cuda(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            ctx->stream = ctx->own_stream;
+            check_cuda(cudaMalloc(&ctx->dev_err, 4 * sizeof(int)), "cudaMalloc(dev_err)");
+            check_cuda(cudaMemset(ctx->dev_err, 0, 4 * sizeof(int)), "cudaMemset(dev_err)");
+            ctx->pool = new mbx::Pool(device);
+        } catch (...) {
+            if (ctx->dev_err) cudaFree(ctx->dev_err);
+            if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+            delete ctx;
+            throw;
+        }
+        *out = ctx;
+    });
+}
+
+void mbx_ctx_destroy(mbx_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    delete ctx->pool;
+    cudaFree(ctx->dev_err);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+}
+
+int32_t mbx_ctx_set_stream(mbx_ctx* ctx, void* stream) {
+    return guard([&] {
+        require_ctx(ctx);
+        ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    });
+}
+
+void* mbx_ctx_stream(mbx_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+uint64_t mbx_ctx_launch_count(const mbx_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int32_t mbx_ctx_synchronize(mbx_ctx* ctx) {
+    return guard([&] {
+        require_ctx(ctx);
+        use_device(ctx);
+        check_cuda(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        int rec[4];
+        check_cuda(cudaMemcpy(rec, ctx->dev_err, sizeof(rec), cudaMemcpyDeviceToHost), "read device error record");
+        if (rec[0] != mbx::kErrNone) {
+            check_cuda(cudaMemset(ctx->dev_err, 0, sizeof(rec)), "clear device error record");
+            mbx::fail(MBX_ERR_TIMEOUT, "device wait timed out (kernel " + std::to_string(rec[1]) + ", site " +
+                                           std::to_string(rec[2]) + ")");
+        }
+    });
+}
+
+int32_t mbx_alloc(mbx_ctx* ctx, size_t bytes, void** out) {
+    return guard([&] {
+        require_ctx(ctx);
+        require_ptr(out, "out");
+        use_device(ctx);
+        *out = ctx->pool->alloc(bytes);
+    });
+}
+
+int32_t mbx_free(mbx_ctx* ctx, void* ptr) {
+    return guard([&] {
+        require_ctx(ctx);
+        if (ptr) ctx->pool->free(ptr);
+    });
+}
+
+int32_t mbx_pool_release_below(mbx_ctx* ctx, size_t min_bytes) {
+    return guard([&] {
+        require_ctx(ctx);
+        use_device(ctx);
+        check_cuda(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        ctx->pool->release_below(min_bytes);
+    });
+}
+
+int32_t mbx_pool_stats(const mbx_ctx* ctx, size_t* cached_bytes, size_t* in_use_bytes) {
+    return guard([&] {
+        require_ctx(ctx);
+        if (cached_bytes) *cached_bytes = ctx->pool->cached_bytes();
+        if (in_use_bytes) *in_use_bytes = ctx->pool->in_use_bytes();
+    });
+}
+
+int32_t mbx_host_alloc(size_t bytes, void** out) {
+    return guard([&] {
+        require_ptr(out, "out");
+        *out = nullptr;
+        check_cuda(cudaHostAlloc(out, bytes ? bytes : 1, cudaHostAllocDefault), "cudaHostAlloc");
+    });
+}
+
+int32_t mbx_host_free(void* ptr) {
+    return guard([&] {
+        if (ptr) check_cuda(cudaFreeHost(ptr), "cudaFreeHost");
+    });
+}
+
+static int32_t memcpy_kind(mbx_ctx* ctx, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
+    return guard([&] {
+        require_ctx(ctx);
+        if (bytes == 0) return;
+        require_ptr(dst, "dst");
+        require_ptr(src, "src");
+        use_device(ctx);
+        check_cuda(cudaMemcpyAsync(dst, src, bytes, kind, ctx->stream), "cudaMemcpyAsync");
+    });
+}
+
+int32_t mbx_memcpy_h2d(mbx_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    return memcpy_kind(ctx, dst, src, bytes, cudaMemcpyHostToDevice);
+}
+int32_t mbx_memcpy_d2h(mbx_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    return memcpy_kind(ctx, dst, src, bytes, cudaMemcpyDeviceToHost);
+}
+int32_t mbx_memcpy_d2d(mbx_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    return memcpy_kind(ctx, dst, src, bytes, cudaMemcpyDeviceToDevice);
+}
+
+int32_t mbx_param_create(mbx_ctx* ctx, const void* host_data, int32_t dtype, int64_t c_out, int64_t taps,
+                         int64_t c_in, mbx_param** out) {
+    return guard([&] {
+        require_ctx(ctx);
+        require_ptr(host_data, "host_data");
+        require_ptr(out, "out");
+        *out = nullptr;
+        MBX_REQUIRE(dtype == MBX_DTYPE_F32 || dtype == MBX_DTYPE_F16, "dtype must be MBX_DTYPE_F32 or MBX_DTYPE_F16");
+        MBX_REQUIRE(taps == 1 || taps == 9, "taps must be 1 (1x1) or 9 (3x3)");
+        MBX_REQUIRE(c_out > 0 && c_in > 0, "c_out and c_in must be positive");
+        MBX_REQUIRE(c_in <= (1 << 16) && c_out <= (1 << 16), "channel count too large");
+        use_device(ctx);
+        auto* p = new mbx_param();
+        p->dtype = dtype;
+        p->c_out = c_out;
+        p->taps = taps;
+        p->c_in = c_in;
+        p->cin_pad = int((c_in + 31) / 32 * 32);
+        p->bn = mbx::choose_bn(c_out);
+        p->cout_pad = int((c_out + p->bn - 1) / p->bn * p->bn);
+        const size_t kdim = size_t(taps) * p->cin_pad;
+        const size_t elems = size_t(p->cout_pad) * kdim;
+        std::vector<float> hi(elems, 0.0f), lo;
+        if (dtype == MBX_DTYPE_F32) lo.assign(elems, 0.0f);
+        for (int64_t o = 0; o < c_out; ++o)
+            for (int64_t t = 0; t < taps; ++t)
+                for (int64_t i = 0; i < c_in; ++i) {
+                    const size_t src = (size_t(o) * taps + t) * c_in + i;
+                    const size_t dst = size_t(o) * kdim + size_t(t) * p->cin_pad + i;
+                    if (dtype == MBX_DTYPE_F16) {
+                        hi[dst] = half_bits_to_float(static_cast<const uint16_t*>(host_data)[src]);
+                    } else {
+                        const float v = static_cast<const float*>(host_data)[src];
+                        hi[dst] = tf32_hi(v);
+                        lo[dst] = v - hi[dst];
+                    }
+                }
+        try {
+            check_cuda(cudaMalloc(&p->hi, elems * 4), "cudaMalloc(param hi)");
+            check_cuda(cudaMemcpy(p->hi, hi.data(), elems * 4, cudaMemcpyHostToDevice), "upload param hi");
+            if (!lo.empty()) {
+                check_cuda(cudaMalloc(&p->lo, elems * 4), "cudaMalloc(param lo)");
+                check_cuda(cudaMemcpy(p->lo, lo.data(), elems * 4, cudaMemcpyHostToDevice), "upload param lo");
+            }
+            mbx::encode_param_tmaps(p);
+        } catch (...) {
+            cudaFree(p->hi);
+            cudaFree(p->lo);
+            delete p;
+            throw;
+        }
+        *out = p;
+    });
+}
+
+void mbx_param_destroy(mbx_ctx* ctx, mbx_param* p) {
+    if (!p) return;
+    if (ctx) {
+        cudaSetDevice(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    cudaFree(p->hi);
+    cudaFree(p->lo);
+    delete p;
+}
+
+int32_t mbx_param_info(const mbx_param* p, int64_t* c_out, int64_t* taps, int64_t* c_in, int32_t* dtype) {
+    return guard([&] {
+        MBX_REQUIRE(p != nullptr, "null param");
+        if (c_out) *c_out = p->c_out;
+        if (taps) *taps = p->taps;
+        if (c_in) *c_in = p->c_in;
+        if (dtype) *dtype = p->dtype;
+    });
+}
+
+int32_t mbx_silu_inplace(mbx_ctx* ctx, float* x, int64_t len) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(len >= 0, "negative length");
+        if (len == 0) return;
+        require_ptr(x, "x");
+        use_device(ctx);
+        mbx::launch_silu_inplace(ctx, x, len);
+    });
+}
+
+int32_t mbx_add_inplace(mbx_ctx* ctx, float* a, const float* b, int64_t len) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(len >= 0, "negative length");
+        if (len == 0) return;
+        require_ptr(a, "a");
+        require_ptr(b, "b");
+        use_device(ctx);
+        mbx::launch_add(ctx, a, b, a, len);
+    });
+}
+
+int32_t mbx_bias_temb_add(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* bias,
+                          const float* temb, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0 && c > 0, "bad shape");
+        if (n * hw == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::launch_bias_temb_add(ctx, x, n, hw, c, bias, temb, out);
+    });
+}
+
+int32_t mbx_concat_channels(mbx_ctx* ctx, const float* a, int64_t ca, const float* b, int64_t cb, int64_t pixels,
+                            float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(ca >= 0 && cb >= 0 && pixels >= 0, "bad shape");
+        if (pixels == 0 || ca + cb == 0) return;
+        require_ptr(out, "out");
+        MBX_REQUIRE(ca == 0 || a, "null a");
+        MBX_REQUIRE(cb == 0 || b, "null b");
+        MBX_REQUIRE(out != a && out != b, "concat_channels: out must alias neither input");
+        use_device(ctx);
+        mbx::launch_concat(ctx, a, ca, b, cb, pixels, out);
+    });
+}
+
+static void check_gn(int64_t n, int64_t h, int64_t w, int64_t c, int64_t groups) {
+    MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0 && c > 0, "bad shape");
+    MBX_REQUIRE(groups > 0 && c % groups == 0, "channels not divisible by groups");
+    MBX_REQUIRE(c <= 8192, "GroupNorm supports at most 8192 channels");
+    MBX_REQUIRE(groups <= 1024, "GroupNorm supports at most 1024 groups");
+}
+
+static void gn_affine_impl(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t groups,
+                           float eps, const float* gamma, const float* beta, const float* add, float* scale,
+                           float* shift) {
+    const int64_t hw = h * w;
+    mbx::PoolBuf part(ctx, size_t(n) * mbx::gn_chunks(hw) * groups * 2 * sizeof(double));
+    mbx::launch_gn_partials(ctx, x, n, hw, c, groups, add, part.as<double>());
+    mbx::launch_gn_finalize(ctx, part.as<double>(), n, hw, c, groups, eps, gamma, beta, add, scale, shift);
+}
+
+int32_t mbx_group_norm_affine(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                              int64_t groups, float eps, const float* gamma, const float* beta, const float* add,
+                              float* scale_out, float* shift_out) {
+    return guard([&] {
+        require_ctx(ctx);
+        check_gn(n, h, w, c, groups);
+        if (n == 0) return;
+        MBX_REQUIRE(h * w > 0, "GroupNorm over an empty image");
+        require_ptr(x, "x");
+        require_ptr(gamma, "gamma");
+        require_ptr(beta, "beta");
+        require_ptr(scale_out, "scale_out");
+        require_ptr(shift_out, "shift_out");
+        use_device(ctx);
+        gn_affine_impl(ctx, x, n, h, w, c, groups, eps, gamma, beta, add, scale_out, shift_out);
+    });
+}
+
+int32_t mbx_group_norm_apply(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* scale,
+                             const float* shift, int32_t silu, const float* residual, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0 && c > 0, "bad shape");
+        if (n * hw == 0) return;
+        require_ptr(x, "x");
+        require_ptr(scale, "scale");
+        require_ptr(shift, "shift");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::launch_gn_apply(ctx, x, n, hw, c, scale, shift, silu != 0, residual, out);
+    });
+}
+
+int32_t mbx_group_norm_forward(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                               int64_t groups, float eps, const float* gamma, const float* beta, const float* add,
+                               int32_t silu, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        check_gn(n, h, w, c, groups);
+        if (n == 0) return;
+        MBX_REQUIRE(h * w > 0, "GroupNorm over an empty image");
+        require_ptr(x, "x");
+        require_ptr(gamma, "gamma");
+        require_ptr(beta, "beta");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::PoolBuf ss(ctx, size_t(n) * c * 2 * sizeof(float));
+        float* scale = ss.as<float>();
+        float* shift = scale + n * c;
+        gn_affine_impl(ctx, x, n, h, w, c, groups, eps, gamma, beta, add, scale, shift);
+        mbx::launch_gn_apply(ctx, x, n, h * w, c, scale, shift, silu != 0, nullptr, out);
+    });
+}
+
+int32_t mbx_layer_norm(mbx_ctx* ctx, const float* x, int64_t tokens, int64_t c, const float* gamma,
+                       const float* beta, float eps, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(tokens >= 0 && c > 0, "bad shape");
+        MBX_REQUIRE(c <= 8192, "LayerNorm supports at most 8192 channels");
+        if (tokens == 0) return;
+        require_ptr(x, "x");
+        require_ptr(gamma, "gamma");
+        require_ptr(beta, "beta");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::launch_layer_norm(ctx, x, tokens, c, gamma, beta, eps, out);
+    });
+}
+
+int32_t mbx_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                         const float* weight, const float* bias, int32_t epilogue, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0 && c > 0, "bad shape");
+        MBX_REQUIRE(epilogue == MBX_EPILOGUE_NONE || epilogue == MBX_EPILOGUE_RELU ||
+                        epilogue == MBX_EPILOGUE_GLU_SILU,
+                    "unknown epilogue");
+        MBX_REQUIRE(epilogue != MBX_EPILOGUE_GLU_SILU || c % 2 == 0, "GLU needs an even channel count");
+        if (n * h * w == 0) return;
+        require_ptr(x, "x");
+        require_ptr(weight, "weight");
+        require_ptr(bias, "bias");
+        require_ptr(out, "out");
+        MBX_REQUIRE(out != x, "depthwise3x3: out must not alias x");
+        use_device(ctx);
+        mbx::launch_depthwise3x3(ctx, x, n, h, w, c, weight, bias, epilogue, out);
+    });
+}
+
+int32_t mbx_conv1x1(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                    const mbx_param* weight, const float* bias, const float* residual, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(weight != nullptr, "null weight");
+        MBX_REQUIRE(weight->taps == 1, "Conv1x1 needs a 1x1 (taps = 1) weight");
+        MBX_REQUIRE(weight->c_in == c_in, "Conv1x1 input channels");
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0, "bad shape");
+        if (n * h * w == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        MBX_REQUIRE(out != x, "conv1x1: out must not alias x");
+        use_device(ctx);
+        mbx::ConvShape s{n, h, w, c_in, h, w, 1, 0, 0, 0};
+        mbx::launch_conv_tc(ctx, x, s, weight, bias, nullptr, nullptr, false, residual, out);
+    });
+}
+
+int32_t mbx_conv3x3_output_hw(int64_t h, int64_t w, int64_t stride, const int64_t pad[4], int32_t upsample2x,
+                              int64_t* ho, int64_t* wo) {
+    return guard([&] {
+        require_ptr(pad, "pad");
+        require_ptr(ho, "ho");
+        require_ptr(wo, "wo");
+        MBX_REQUIRE(stride >= 1 && stride <= 2, "stride must be 1 or 2");
+        for (int i = 0; i < 4; ++i) MBX_REQUIRE(pad[i] >= 0 && pad[i] <= 2, "padding must be in [0, 2]");
+        const int64_t up = upsample2x ? 2 : 1;
+        const int64_t hh = h * up + pad[0] + pad[2] - 3, ww = w * up + pad[1] + pad[3] - 3;
+        MBX_REQUIRE(hh >= 0 && ww >= 0, "input smaller than the 3x3 window");
+        *ho = hh / stride + 1;
+        *wo = ww / stride + 1;
+    });
+}
+
+int32_t mbx_conv3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                    const mbx_param* weight, const float* bias, int64_t stride, const int64_t pad[4],
+                    int32_t upsample2x, const float* pro_scale, const float* pro_shift, int32_t pro_silu,
+                    const float* residual, float* out) {
+    int64_t ho = 0, wo = 0;
+    int32_t st = mbx_conv3x3_output_hw(h, w, stride, pad, upsample2x, &ho, &wo);
+    if (st != MBX_OK) return st;
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(weight != nullptr, "null weight");
+        MBX_REQUIRE(weight->taps == 9, "Conv3x3 needs a 3x3 (taps = 9) weight");
+        MBX_REQUIRE(weight->c_in == c_in, "Conv3x3 input channels");
+        MBX_REQUIRE(n >= 0 && h >= 1 && w >= 1, "bad shape");
+        MBX_REQUIRE((pro_scale == nullptr) == (pro_shift == nullptr), "prologue needs both scale and shift");
+        if (n == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        MBX_REQUIRE(out != x, "conv3x3: out must not alias x");
+        MBX_REQUIRE((h << (upsample2x ? 1 : 0)) < (1 << 20) && (w << (upsample2x ? 1 : 0)) < (1 << 20),
+                    "image too large");
+        use_device(ctx);
+        mbx::ConvShape s{n, h, w, c_in, ho, wo, int(stride), int(pad[0]), int(pad[1]), upsample2x ? 1 : 0};
+        mbx::launch_conv_tc(ctx, x, s, weight, bias, pro_scale, pro_shift, pro_silu != 0, residual, out);
+    });
+}
+
+int32_t mbx_matmul(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, int64_t a_row_stride,
+                   int64_t a_col_stride, const float* b, int64_t n, int64_t b_row_stride, int64_t b_col_stride,
+                   int32_t accumulate) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(m >= 0 && n >= 0 && k >= 0, "bad shape");
+        MBX_REQUIRE(a_row_stride >= 0 && a_col_stride >= 0 && b_row_stride >= 0 && b_col_stride >= 0,
+                    "negative stride");
+        if (m == 0 || n == 0) return;
+        require_ptr(c, "c");
+        MBX_REQUIRE(k == 0 || (a && b), "null operand");
+        use_device(ctx);
+        mbx::launch_matmul_simt(ctx, c, a, m, k, a_row_stride, a_col_stride, b, n, b_row_stride, b_col_stride,
+                                accumulate != 0);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+// Internal declarations shared by the moebius-cuda translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/moebius_cuda.h"
+
+namespace mbx {
+
+// Error raised inside the library; converted to a status code at the C ABI.
+struct Error : std::runtime_error {
+    int32_t code;
+    Error(int32_t c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] inline void fail(int32_t code, const std::string& msg) { throw Error(code, msg); }
+
+inline void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        int32_t code = e == cudaErrorMemoryAllocation ? MBX_ERR_OUT_OF_MEMORY : MBX_ERR_CUDA;
+        fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+#define MBX_REQUIRE(cond, msg)                                     \
+    do {                                                           \
+        if (!(cond)) ::mbx::fail(MBX_ERR_INVALID_ARGUMENT, (msg)); \
+    } while (0)
+
+// Device-side error record written by kernels whose bounded waits gave up:
+// [0] = code (0 = none), [1] = kernel id, [2] = detail (barrier / stage).
+enum DeviceErr : int { kErrNone = 0, kErrWaitTimeout = 1 };
+enum KernelId : int { kKConvTc = 1, kKGnSlab = 2 };
+
+// Stream-ordered best-fit caching allocator (device analogue of the
+// reference's Scratch pool). All blocks are used on the context stream, so a
+// block freed by one call can be handed to the next call without a sync.
+class Pool {
+public:
+    explicit Pool(int device) : device_(device) {}
+    ~Pool();
+    void* alloc(size_t bytes);
+    void free(void* p);
+    void release_below(size_t min_bytes);
+    size_t cached_bytes() const { return cached_; }
+    size_t in_use_bytes() const { return in_use_; }
+
+private:
+    int device_;
+    std::multimap<size_t, void*> free_;        // size -> block
+    std::unordered_map<void*, size_t> used_;   // block -> size
+    size_t cached_ = 0, in_use_ = 0;
+    mutable std::mutex mu_;
+};
+
+}  // namespace mbx
+
+struct mbx_ctx {
+    int device = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0;
+    int* dev_err = nullptr;       // 4 ints, device memory, zeroed at create
+    mbx::Pool* pool = nullptr;
+    uint64_t launches = 0;
+};
+
+struct mbx_param {
+    int32_t dtype = MBX_DTYPE_F32;
+    int64_t c_out = 0, taps = 0, c_in = 0;
+    int cin_pad = 0;   // c_in rounded up to the 32-channel K chunk
+    int bn = 0;        // N tile (output channels per CTA tile)
+    int cout_pad = 0;  // c_out rounded up to bn
+    float* hi = nullptr;  // [cout_pad][taps][cin_pad] tf32-exact high part (or the f16 values)
+    float* lo = nullptr;  // same layout, f32 - hi; null for f16 weights (exact in tf32)
+    CUtensorMap tmap_hi;
+    CUtensorMap tmap_lo;
+};
+
+namespace mbx {
+
+// Kernel launchers (each returns after enqueueing on ctx->stream).
+void launch_silu_inplace(mbx_ctx* ctx, float* x, int64_t len);
+void launch_add(mbx_ctx* ctx, const float* a, const float* b, float* out, int64_t len);
+void launch_bias_temb_add(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* bias,
+                          const float* temb, float* out);
+void launch_concat(mbx_ctx* ctx, const float* a, int64_t ca, const float* b, int64_t cb, int64_t pixels,
+                   float* out);
+
+// GroupNorm: partial sums per (item, pixel chunk, group) into `part`
+// (f64 [n][chunks][groups][2]), then the fold into scale/shift.
+int64_t gn_chunks(int64_t hw);
+void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                        const float* add, double* part);
+void launch_gn_finalize(mbx_ctx* ctx, const double* part, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                        float eps, const float* gamma, const float* beta, const float* add, float* scale,
+                        float* shift);
+void launch_gn_apply(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* scale,
+                     const float* shift, bool silu, const float* residual, float* out);
+void launch_layer_norm(mbx_ctx* ctx, const float* x, int64_t tokens, int64_t c, const float* gamma,
+                       const float* beta, float eps, float* out);
+
+void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                         const float* weight, const float* bias, int epilogue, float* out);
+
+struct ConvShape {
+    int64_t n, h, w, c_in;
+    int64_t ho, wo;
+    int stride, pad_t, pad_l, up;
+};
+void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
+                    const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
+                    float* out);
+// Tensor maps for a param's hi / lo arrays (TMA, 128-byte swizzle).
+void encode_param_tmaps(mbx_param* p);
+int choose_bn(int64_t c_out);
+
+void launch_matmul_simt(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, int64_t a_rs, int64_t a_cs,
+                        const float* b, int64_t n, int64_t b_rs, int64_t b_cs, bool accumulate);
+
+// Launch-configuration helpers.
+inline int grid_for(mbx_ctx* ctx, int64_t work_items, int per_block, int max_waves = 8) {
+    int64_t blocks = (work_items + per_block - 1) / per_block;
+    int64_t cap = (int64_t)ctx->sm_count * max_waves;
+    if (blocks > cap) blocks = cap;
+    return (int)(blocks < 1 ? 1 : blocks);
+}
+
+inline void after_launch(mbx_ctx* ctx, const char* what) {
+    check_cuda(cudaGetLastError(), what);
+    ctx->launches++;
+}
+
+}  // namespace mbx

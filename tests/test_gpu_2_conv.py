@@ -1,0 +1,217 @@
+"""GPU parity of the tensor-core convolutions (tcgen05 implicit GEMM) through
+the C ABI: every conv case of the reference's tests/kernels.rs at its
+tolerances, the fused GroupNorm prologue, and BASELINE-shaped single-block /
+conv-sweep inputs against the CPU oracle with the per-kernel gates
+(max relative error ≤ 1e-3 for f32 weights (3×TF32), ≤ 5e-3 for f16 weights).
+"""
+import numpy as np
+import pytest
+
+from conftest import max_rel_err, rel_l2, scaled_err
+
+pytestmark = pytest.mark.gpu
+
+REF_TOL = 1e-5
+GATE_F32 = 1e-3
+GATE_F16 = 5e-3
+
+
+def up(ctx, a):
+    return ctx.upload(a)
+
+
+def test_conv1x1_bias_and_residual(mbx, ctx, ref_fixture):
+    f = ref_fixture
+    w = mbx.Param(ctx, f["c1.w"])
+    x, b = up(ctx, f["c1.x"]), up(ctx, f["c1.b"])
+    assert scaled_err(mbx.conv1x1(x, w, b).numpy(), f["c1.y"]) <= REF_TOL
+    assert scaled_err(mbx.conv1x1(x, w, b, residual=up(ctx, f["c1.r"])).numpy(), f["c1.yr"]) <= REF_TOL
+    w.close()
+
+
+def test_conv1x1_f16_weights_match_rounded_f32(mbx, ctx, ref_fixture):
+    # tests/kernels.rs:54-63
+    f = ref_fixture
+    x = up(ctx, f["c1.x"])
+    w16 = mbx.Param(ctx, f["c1.w"], "f16")
+    w32 = mbx.Param(ctx, f["c1.w"].astype(np.float16).astype(np.float32))
+    assert scaled_err(mbx.conv1x1(x, w16).numpy(), mbx.conv1x1(x, w32).numpy()) <= 1e-6
+
+
+@pytest.mark.parametrize("name,stride,pad,upx", [
+    ("c3.same", 1, (1, 1, 1, 1), False),
+    ("c3.s2p1", 2, (1, 1, 1, 1), False),
+    ("c3.s2vae", 2, (0, 0, 1, 1), False),
+    ("c3.up", 1, (1, 1, 1, 1), True),
+])
+def test_conv3x3_variants(mbx, ctx, ref_fixture, name, stride, pad, upx):
+    f = ref_fixture
+    w = mbx.Param(ctx, f["c3.w"])
+    got = mbx.conv3x3(up(ctx, f["c3.x"]), w, up(ctx, f["c3.b"]), stride, pad, upx).numpy()
+    assert scaled_err(got, f[name]) <= REF_TOL
+
+
+def test_extra_fixture_convs(mbx, ctx, extra_fixture):
+    f = extra_fixture
+    w = mbx.Param(ctx, f["c1o.w"])
+    got = mbx.conv1x1(up(ctx, f["c1o.x"]), w, up(ctx, f["c1o.b"]), residual=up(ctx, f["c1o.r"])).numpy()
+    assert scaled_err(got, f["c1o.y"]) <= REF_TOL
+    w = mbx.Param(ctx, f["c3n.w"])
+    assert scaled_err(mbx.conv3x3(up(ctx, f["c3n.x"]), w, up(ctx, f["c3n.b"])).numpy(), f["c3n.y"]) <= REF_TOL
+    # GN(+SiLU) prologue fused into the conv, plain and upsampled; padding stays zero.
+    x = up(ctx, f["pro.x"])
+    sc, sh = mbx.group_norm_affine(x, 8, 1e-6, up(ctx, f["pro.gamma"]), up(ctx, f["pro.beta"]))
+    w = mbx.Param(ctx, f["pro.w"])
+    b = up(ctx, f["pro.b"])
+    for key, upx in (("pro.y", False), ("pro.yup", True)):
+        got = mbx.conv3x3(x, w, b, upsample2x=upx, prologue=(sc, sh, True)).numpy()
+        assert scaled_err(got, f[key]) <= REF_TOL
+
+
+def naive_conv3x3_same(x, wt):
+    n, h, w, c = x.shape
+    xp = np.zeros((n, h + 2, w + 2, c))
+    xp[:, 1:-1, 1:-1] = x
+    out = np.zeros((n, h, w, wt.shape[0]))
+    for ky in range(3):
+        for kx in range(3):
+            out += np.einsum("nhwc,oc->nhwo", xp[:, ky:ky + h, kx:kx + w], wt[:, ky, kx].astype(np.float64))
+    return out
+
+
+def test_conv3x3_band_boundaries(mbx, ctx):
+    # tests/kernels.rs:87-116 (c_in = 1024: many K chunks; 1200 output pixels = 10 M tiles)
+    n, h, w, c = 1, 40, 30, 1024
+    i = np.arange(n * h * w * c, dtype=np.int64)
+    x = (((i * 7919) % 211) / 211.0 - 0.5).astype(np.float32).reshape(n, h, w, c)
+    j = np.arange(2 * 9 * c, dtype=np.int64)
+    wt = (((j * 104_729) % 97) / 970.0 - 0.05).astype(np.float32).reshape(2, 3, 3, c)
+    got = mbx.conv3x3(up(ctx, x), mbx.Param(ctx, wt)).numpy()
+    assert scaled_err(got, naive_conv3x3_same(x.astype(np.float64), wt)) <= 2e-5
+
+
+@pytest.mark.parametrize("n,h,w,ci,co,upx", [(2, 37, 23, 24, 40, False), (1, 9, 13, 16, 8, True),
+                                             (1, 6, 5, 768, 720, False)])
+def test_f16_weights_match_direct_on_odd_sizes(mbx, ctx, oracle, n, h, w, ci, co, upx):
+    # tests/kernels.rs:154-170: the GPU direct conv with f16 weights vs the oracle's im2col path.
+    i = np.arange(n * h * w * ci, dtype=np.int64)
+    x = (((i * 7919) % 401) / 401.0 - 0.5).astype(np.float32).reshape(n, h, w, ci)
+    j = np.arange(co * 9 * ci, dtype=np.int64)
+    wt = (((j * 104_729) % 113) / 1130.0 - 0.05).astype(np.float32).reshape(co, 3, 3, ci)
+    b = (np.arange(co) * 0.01).astype(np.float32)
+    got = mbx.conv3x3(up(ctx, x), mbx.Param(ctx, wt, "f16"), up(ctx, b), upsample2x=upx).numpy()
+    want = oracle.conv3x3(x, wt.astype(np.float16).astype(np.float32), b, upsample2x=upx, im2col=True)
+    assert scaled_err(got, want) <= 2e-5
+
+
+def lcg(seed):
+    s = seed
+
+    def nxt(k):
+        nonlocal s
+        out = np.empty(k, np.float32)
+        for i in range(k):
+            s = (s * 6364136223846793005 + 1442695040888963407) % (1 << 64)
+            out[i] = ((s >> 40) / float(1 << 24)) * 2.0 - 1.0
+        return out
+    return nxt
+
+
+@pytest.mark.parametrize("n,h,w,ci,groups,co", [(2, 7, 9, 40, 8, 24), (2, 37, 23, 768, 32, 16)])
+@pytest.mark.parametrize("upx", [False, True])
+def test_prologue_matches_group_norm_then_conv(mbx, ctx, n, h, w, ci, groups, co, upx):
+    # tests/kernels.rs:233-264, both sides on the GPU.
+    rng = np.random.default_rng(7 + ci)
+    x = (rng.uniform(-1, 1, (n, h, w, ci)) * 3.0 + 0.7).astype(np.float32)
+    gamma = (1.0 + 0.5 * rng.uniform(-1, 1, ci)).astype(np.float32)
+    beta = rng.uniform(-1, 1, ci).astype(np.float32)
+    wt = (rng.uniform(-1, 1, (co, 3, 3, ci)) * 0.05).astype(np.float32)
+    bias = (np.arange(co) * 0.01).astype(np.float32)
+    xd, g, b = up(ctx, x), up(ctx, gamma), up(ctx, beta)
+    wp, bd = mbx.Param(ctx, wt, "f16"), up(ctx, bias)
+    a = mbx.group_norm(xd, groups, 1e-6, g, b, silu=True)
+    want = mbx.conv3x3(a, wp, bd, upsample2x=upx).numpy()
+    sc, sh = mbx.group_norm_affine(xd, groups, 1e-6, g, b)
+    got = mbx.conv3x3(xd, wp, bd, upsample2x=upx, prologue=(sc, sh, True)).numpy()
+    assert rel_l2(got, want) <= 1e-6
+
+
+def test_single_block_config(mbx, ctx, oracle):
+    """x [1,64,64,256] ~N(0,1); GN(32, eps 1e-6, γ~N(1,0.02), β~N(0,0.02)) + SiLU;
+    3×3 conv 256→256 (w ~N(0, 1/√2304), bias ~N(0, 0.01)); + x. Fused on the GPU as GN stats →
+    conv with the GN prologue and the residual in the epilogue."""
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1, 64, 64, 256)).astype(np.float32)
+    gamma = rng.normal(1.0, 0.02, 256).astype(np.float32)
+    beta = rng.normal(0.0, 0.02, 256).astype(np.float32)
+    wt = rng.normal(0.0, 1.0 / np.sqrt(2304.0), (256, 3, 3, 256)).astype(np.float32)
+    bias = rng.normal(0.0, 0.01, 256).astype(np.float32)
+    want = oracle.conv3x3(oracle.group_norm(x, 32, 1e-6, gamma, beta, silu=True), wt, bias)
+    want = oracle.add(want, x)
+    for dtype, gate in (("f32", GATE_F32), ("f16", GATE_F16)):
+        wref = wt if dtype == "f32" else wt.astype(np.float16).astype(np.float32)
+        want_d = want if dtype == "f32" else oracle.add(
+            oracle.conv3x3(oracle.group_norm(x, 32, 1e-6, gamma, beta, silu=True), wref, bias), x)
+        xd = up(ctx, x)
+        sc, sh = mbx.group_norm_affine(xd, 32, 1e-6, up(ctx, gamma), up(ctx, beta))
+        got = mbx.conv3x3(xd, mbx.Param(ctx, wt, dtype), up(ctx, bias), prologue=(sc, sh, True),
+                          residual=xd).numpy()
+        assert max_rel_err(got, want_d) <= gate
+        assert scaled_err(got, want_d) <= 1e-4
+
+
+@pytest.mark.parametrize("k", [1, 3])
+@pytest.mark.parametrize("hw,ci,co", [(64, 128, 128), (64, 256, 512), (64, 512, 256), (128, 128, 256)])
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_conv_sweep_matches_oracle(mbx, ctx, oracle, k, hw, ci, co, dtype):
+    """BASELINE config 3 shapes (B = 1; the largest sizes are covered by the bench's
+    property checks): w ~N(0, 1/√fan_in), fused bias + residual epilogue."""
+    rng = np.random.default_rng(hw + ci + co + k)
+    x = rng.standard_normal((1, hw, hw, ci)).astype(np.float32)
+    shape = (co, ci) if k == 1 else (co, 3, 3, ci)
+    wt = rng.normal(0.0, 1.0 / np.sqrt(ci * k * k), shape).astype(np.float32)
+    bias = rng.normal(0.0, 0.01, co).astype(np.float32)
+    res = rng.standard_normal((1, hw, hw, co)).astype(np.float32)
+    wref = wt if dtype == "f32" else wt.astype(np.float16).astype(np.float32)
+    if k == 1:
+        want = oracle.conv1x1(x, wref, bias, res)
+        got = mbx.conv1x1(up(ctx, x), mbx.Param(ctx, wt, dtype), up(ctx, bias), up(ctx, res)).numpy()
+    else:
+        want = oracle.add(oracle.conv3x3(x, wref, bias), res)
+        got = mbx.conv3x3(up(ctx, x), mbx.Param(ctx, wt, dtype), up(ctx, bias), residual=up(ctx, res)).numpy()
+    assert max_rel_err(got, want) <= (GATE_F32 if dtype == "f32" else GATE_F16)
+    assert scaled_err(got, want) <= 2e-5
+
+
+@pytest.mark.parametrize("shape,stride,pad,upx,co", [
+    ((2, 64, 64, 320), 2, (1, 1, 1, 1), False, 320),     # UNet Downsample2D, level 0
+    ((1, 128, 128, 128), 2, (0, 0, 1, 1), False, 128),   # VAE encoder Downsample2D
+    ((2, 16, 16, 1280), 1, (1, 1, 1, 1), True, 1280),    # UNet Upsample2D, level 2
+    ((1, 64, 64, 4), 1, (1, 1, 1, 1), False, 512),       # VAE decoder conv_in (4 channels)
+    ((1, 64, 64, 128), 1, (1, 1, 1, 1), False, 3),       # VAE conv_out (3 channels)
+])
+def test_unet_vae_conv_shapes(mbx, ctx, oracle, shape, stride, pad, upx, co):
+    rng = np.random.default_rng(shape[-1] + co)
+    ci = shape[-1]
+    x = rng.standard_normal(shape).astype(np.float32)
+    wt = rng.normal(0.0, 1.0 / np.sqrt(9 * ci), (co, 3, 3, ci)).astype(np.float32)
+    bias = rng.normal(0.0, 0.01, co).astype(np.float32)
+    want = oracle.conv3x3(x, wt, bias, stride, pad, upx)
+    got = mbx.conv3x3(up(ctx, x), mbx.Param(ctx, wt), up(ctx, bias), stride, pad, upx).numpy()
+    assert max_rel_err(got, want) <= GATE_F32
+    assert scaled_err(got, want) <= 2e-5
+
+
+def test_conv_errors(mbx, ctx):
+    w = mbx.Param(ctx, np.zeros((8, 3, 3, 16), np.float32))
+    with pytest.raises(mbx.MbxError) as e:
+        mbx.conv3x3(up(ctx, np.zeros((1, 4, 4, 12), np.float32)), w)  # wrong c_in
+    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+    with pytest.raises(mbx.MbxError):
+        mbx.conv1x1(up(ctx, np.zeros((1, 4, 4, 16), np.float32)), w)  # 3×3 weight given to a 1×1 conv
+    ctx.synchronize()
+
+
+def test_device_error_word_is_clear(mbx, ctx):
+    """No bounded wait gave up during the tests above (mbx_ctx_synchronize reports MBX_ERR_TIMEOUT otherwise)."""
+    ctx.synchronize()
