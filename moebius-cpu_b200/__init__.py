@@ -92,6 +92,23 @@ class Context:
     def free(self, ptr: int) -> None:
         check(lib().mbx_free(self.handle, ctypes.c_void_p(ptr)))
 
+    def copy_h2d(self, dst: int, src_host: int, nbytes: int) -> None:
+        check(lib().mbx_memcpy_h2d(self.handle, ctypes.c_void_p(dst), ctypes.c_void_p(src_host), nbytes))
+
+    def copy_d2h(self, dst_host: int, src: int, nbytes: int) -> None:
+        check(lib().mbx_memcpy_d2h(self.handle, ctypes.c_void_p(dst_host), ctypes.c_void_p(src), nbytes))
+
+    @staticmethod
+    def host_alloc(nbytes: int) -> int:
+        """Page-locked host memory (mbx_host_alloc); release with host_free."""
+        p = ctypes.c_void_p()
+        check(lib().mbx_host_alloc(nbytes, ctypes.byref(p)))
+        return p.value
+
+    @staticmethod
+    def host_free(ptr: int) -> None:
+        check(lib().mbx_host_free(ctypes.c_void_p(ptr)))
+
     def empty(self, shape: Sequence[int]) -> "DeviceTensor":
         return DeviceTensor(self, tuple(int(s) for s in shape))
 
@@ -107,12 +124,18 @@ class Context:
 class DeviceTensor:
     """A float32 device buffer from the context's pool, with an NHWC shape."""
 
-    def __init__(self, ctx: Context, shape: tuple):
+    def __init__(self, ctx: Context, shape: tuple, ptr: Optional[int] = None):
         self.ctx = ctx
         self.shape = tuple(shape)
         self.size = int(np.prod(self.shape)) if self.shape else 1
         self.nbytes = 4 * self.size
-        self.ptr = ctx.alloc(self.nbytes)
+        self.owned = ptr is None
+        self.ptr = ctx.alloc(self.nbytes) if ptr is None else int(ptr)
+
+    @classmethod
+    def wrap(cls, ctx: Context, ptr: int, shape: Sequence[int]) -> "DeviceTensor":
+        """A view of caller-owned device memory (e.g. a torch tensor's data_ptr()); never freed here."""
+        return cls(ctx, tuple(int(s) for s in shape), ptr=ptr)
 
     def numpy(self) -> np.ndarray:
         out = np.empty(self.shape, np.float32)
@@ -123,9 +146,9 @@ class DeviceTensor:
         return out
 
     def free(self) -> None:
-        if self.ptr:
+        if self.ptr and self.owned:
             self.ctx.free(self.ptr)
-            self.ptr = 0
+        self.ptr = 0
 
     @property
     def vp(self) -> ctypes.c_void_p:

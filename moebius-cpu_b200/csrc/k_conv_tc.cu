@@ -8,20 +8,26 @@
 // materialising the patch matrix, and replaces its Winograd path
 // (src/engine/winograd.rs) for stride 1 / pad 1.
 //
-// CTA = one 128 × bn output tile; 6 warps:
+// CTA = one 128 × bn output tile (bn ≤ 160); 10 warps:
 //   warps 0-3  producers: gather the A tile (128 pixels × 32 channels) from
 //              NHWC global memory — zero padding, stride, nearest-2× upsample
 //              and the optional GroupNorm prologue [SiLU](x·scale + shift)
-//              are all applied here — split each value into a TF32-exact
-//              high part and the f32 remainder, and store both into
-//              128-byte-swizzled K-major shared-memory tiles;
-//              afterwards the epilogue: TMEM → registers, + bias (+ residual),
-//              → global.
+//              are all applied here — split each value into a TF32-rounded
+//              high part and a TF32-rounded remainder, and store both into
+//              128-byte-swizzled K-major shared-memory tiles.
 //   warp 4     MMA issuer (one thread) + TMEM allocation.
 //   warp 5     TMA issuer (one thread) for the pre-split weight tiles.
-// Precision: f32 weights → 3×TF32 (a_hi·w_hi + a_hi·w_lo + a_lo·w_hi),
-// f16 weights (exact in TF32) → 2×TF32 (a_hi·w + a_lo·w); accumulation in
-// f32 in TMEM. Every mbarrier wait is bounded; on timeout the CTA records the
+//   warps 6-9  accumulator drain + epilogue (TMEM lane quadrant = warp % 4).
+// Precision: f32 weights → 3×TF32 (a_lo·w_hi + a_hi·w_lo + a_hi·w_hi),
+// f16 weights (exact in TF32) → 2×TF32 (a_lo·w + a_hi·w). The tensor core
+// adds each MMA's products into its f32 accumulator with truncation, which
+// biases long sums toward zero (about 1e-4 relative at K = 11520). So K is
+// cut into segments of kSegChunks chunks (256 K-elements): the MMA warp
+// alternates between two TMEM accumulators, and the drain warps fold each
+// finished segment into a TMEM-resident running sum with round-to-nearest
+// f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).
+// The last segment is folded straight into the epilogue: + bias (+ residual)
+// → global. Every mbarrier wait is bounded; on timeout the CTA records the
 // error in the context's device error word, skips its stores and exits.
 #include <cudaTypedefs.h>
 
@@ -36,7 +42,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;                  // f32 elements per 128-byte swizzle row
 constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kSegChunks = 8;  // K chunks (of 32) per accumulator segment
+constexpr int kMaxBn = 160;    // 3 · bn TMEM columns (two accumulators + the running sum) ≤ 512
 constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
 constexpr int kMaxSmem = 232448;             // 227 KB opt-in limit per CTA
 
@@ -182,7 +190,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ float tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xffffe000u); }
+// Round to the nearest TF32 value (ties to even), returned as an f32 whose low
+// 13 mantissa bits are zero, so the tensor core reads it exactly. Rounding (not
+// truncation) keeps the split errors unbiased; truncation biases every
+// product toward zero and the bias grows linearly with K.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
+        "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
+        "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float tf32_rn(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return __uint_as_float((u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u);
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
@@ -201,12 +230,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stages = args.stages;
     const uint32_t b_bytes = (uint32_t)bn * 128u;
     const uint32_t stage_bytes = 2 * A_BYTES + (F32W ? 2 : 1) * b_bytes;
-    const uint32_t bars = base + (uint32_t)stages * stage_bytes;  // full[s], empty[s], done
+    // Barriers: full[s], empty[s] per smem stage; acc_full[b], acc_empty[b] per TMEM accumulator.
+    const uint32_t bars = base + (uint32_t)stages * stage_bytes;
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
-    const uint32_t done_bar = bars + 16u * stages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (done_bar + 8 - base));
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (done_bar + 12 - base));
+    auto acc_full_bar = [&](int b) { return bars + 16u * stages + 8u * b; };
+    auto acc_empty_bar = [&](int b) { return bars + 16u * stages + 16u + 8u * b; };
+    const uint32_t final_bar = bars + 16u * stages + 32u;  // abort path: all issued MMAs retired
+    const uint32_t misc = final_bar + 8u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (misc - base));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tile = blockIdx.x % args.n_tiles;
@@ -214,13 +247,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t m0 = m_tile * BM;
     const int n0 = n_tile * bn;
     const int K = args.k_chunks;
+    const int nseg = (K + kSegChunks - 1) / kSegChunks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(full_bar(s), 128 + 1);
             mbar_init(empty_bar(s), 1);
         }
-        mbar_init(done_bar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full_bar(b), 1);
+            mbar_init(acc_empty_bar(b), 128);
+        }
+        mbar_init(final_bar, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -313,51 +351,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 8; ++i) {
                 const int r = rbase + 16 * i;
                 const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
-                const float h0 = tf32_hi(v[i][0]), h1 = tf32_hi(v[i][1]), h2 = tf32_hi(v[i][2]),
-                            h3 = tf32_hi(v[i][3]);
+                const float h0 = tf32_rn(v[i][0]), h1 = tf32_rn(v[i][1]), h2 = tf32_rn(v[i][2]),
+                            h3 = tf32_rn(v[i][3]);
                 st_shared_v4(a_hi + off, h0, h1, h2, h3);
-                st_shared_v4(a_lo + off, v[i][0] - h0, v[i][1] - h1, v[i][2] - h2, v[i][3] - h3);
+                st_shared_v4(a_lo + off, tf32_rn(v[i][0] - h0), tf32_rn(v[i][1] - h1), tf32_rn(v[i][2] - h2),
+                             tf32_rn(v[i][3] - h3));
             }
             fence_proxy_async_smem();
             mbar_arrive(full_bar(s));
-        }
-        // ------------------------------------------------------------ epilogue
-        const bool ok = mbar_wait(done_bar, 0, args.err, 2, abort_flag, false) && !*abort_flag;
-        tc_fence_after();
-        const int row = warp * 32 + lane;
-        const int64_t m = m0 + row;
-        const bool vec_out = (args.c_out & 3) == 0;
-        for (int cc = 0; cc < bn; cc += 32) {
-            float acc[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cc, acc);
-            if (!ok || m >= args.m_total) continue;
-            const int nb = n0 + cc;
-            if (nb >= args.c_out) continue;
-            float* dst = args.out + m * args.c_out + nb;
-            const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
-            if (vec_out && nb + 32 <= args.c_out) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + q)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (res) {
-                        const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + q);
-                        pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
-                    }
-                    reinterpret_cast<float4*>(dst)[q] = make_float4(pre.x + acc[4 * q], pre.y + acc[4 * q + 1],
-                                                                    pre.z + acc[4 * q + 2], pre.w + acc[4 * q + 3]);
-                }
-            } else {
-                const int lim = min(32, args.c_out - nb);
-#pragma unroll
-                for (int q = 0; q < 32; ++q) {
-                    if (q < lim) {
-                        float pre = args.bias ? __ldg(args.bias + nb + q) : 0.0f;
-                        if (res) pre = __ldg(res + q) + pre;
-                        dst[q] = pre + acc[q];
-                    }
-                }
-            }
         }
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
@@ -365,8 +366,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = idesc_tf32(bn);
             for (int kc = 0; kc < K; ++kc) {
                 const int s = kc % stages;
+                const int seg = kc / kSegChunks, b = seg & 1;
+                const bool seg_first = kc % kSegChunks == 0;
+                const bool seg_last = (kc + 1) % kSegChunks == 0 || kc + 1 == K;
+                if (seg_first &&
+                    !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true))
+                    break;
                 if (!mbar_wait(full_bar(s), (kc / stages) & 1, args.err, 3, abort_flag, true)) break;
                 tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(b * bn);
                 const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
                 const uint32_t a_lo = a_hi + A_BYTES;
                 const uint32_t b_hi = a_hi + 2 * A_BYTES;
@@ -376,23 +384,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t koff = (uint32_t)kk * 32u;
                     const uint64_t adh = sw128_desc(a_hi + koff), adl = sw128_desc(a_lo + koff);
                     const uint64_t bdh = sw128_desc(b_hi + koff);
-                    const uint32_t first = (kc > 0 || kk > 0) ? 1u : 0u;
+                    const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
                     if constexpr (F32W) {
                         const uint64_t bdl = sw128_desc(b_lo + koff);
-                        mma_tf32(tmem, adl, bdh, idesc, first);
-                        mma_tf32(tmem, adh, bdl, idesc, 1u);
-                        mma_tf32(tmem, adh, bdh, idesc, 1u);
+                        mma_tf32(d, adl, bdh, idesc, acc);
+                        mma_tf32(d, adh, bdl, idesc, 1u);
+                        mma_tf32(d, adh, bdh, idesc, 1u);
                     } else {
-                        mma_tf32(tmem, adl, bdh, idesc, first);
-                        mma_tf32(tmem, adh, bdh, idesc, 1u);
+                        mma_tf32(d, adl, bdh, idesc, acc);
+                        mma_tf32(d, adh, bdh, idesc, 1u);
                     }
                 }
                 mma_commit(empty_bar(s));
+                if (seg_last) mma_commit(acc_full_bar(b));
             }
-            mma_commit(done_bar);
+            if (*abort_flag) {
+                // Do not let TMEM be freed under MMAs that are still running.
+                mma_commit(final_bar);
+                mbar_wait(final_bar, 0, args.err, 7, abort_flag, false);
+            }
         }
         __syncwarp();
-    } else {
+    } else if (warp == 5) {
         // ------------------------------------------------------------ TMA issuer
         if (lane == 0) {
             for (int kc = 0; kc < K; ++kc) {
@@ -405,6 +418,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
+    } else {
+        // ------------------------------------------------------------ drain + epilogue
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row = q * 32 + lane;
+        const int64_t m = m0 + row;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const uint32_t sum_col = (uint32_t)(2 * bn);
+        const bool vec_out = (args.c_out & 3) == 0;
+        bool ok = true;
+        for (int seg = 0; seg < nseg; ++seg) {
+            const int b = seg & 1;
+            if (!mbar_wait(acc_full_bar(b), (seg >> 1) & 1, args.err, 6, abort_flag, true)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const bool last = seg + 1 == nseg;
+            for (int cc = 0; cc < bn; cc += 32) {
+                float acc[32];
+                tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
+                if (seg > 0) {
+                    float run[32];
+                    tmem_ld32(lane_base + sum_col + (uint32_t)cc, run);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = run[i] + acc[i];
+                }
+                if (!last) {
+                    tmem_st32(lane_base + sum_col + (uint32_t)cc, acc);
+                    continue;
+                }
+                if (m >= args.m_total) continue;
+                const int nb = n0 + cc;
+                if (nb >= args.c_out) continue;
+                float* dst = args.out + m * args.c_out + nb;
+                const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
+                if (vec_out && nb + 32 <= args.c_out) {
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) {
+                        float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + v)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (res) {
+                            const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
+                            pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
+                        }
+                        reinterpret_cast<float4*>(dst)[v] =
+                            make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
+                                        pre.w + acc[4 * v + 3]);
+                    }
+                } else {
+                    const int lim = min(32, args.c_out - nb);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (i < lim) {
+                            float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
+                            if (res) pre = __ldg(res + i) + pre;
+                            dst[i] = pre + acc[i];
+                        }
+                    }
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(acc_empty_bar(b));
+        }
+        (void)ok;
     }
     tc_fence_before();
     __syncthreads();
@@ -463,7 +541,7 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_til
 int choose_bn(int64_t c_out) {
     int best = 32;
     int64_t best_cost = INT64_MAX;
-    for (int bn = 256; bn >= 32; bn -= 32) {
+    for (int bn = kMaxBn; bn >= 32; bn -= 32) {
         const int64_t tiles = (c_out + bn - 1) / bn;
         const int64_t cost = tiles * bn + 32 * tiles;
         if (cost < best_cost) {
@@ -506,7 +584,7 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     const bool f32w = p->lo != nullptr;
     a.stages = stage_count(f32w, p->bn);
     a.tmem_cols = 32;
-    while (a.tmem_cols < p->bn) a.tmem_cols <<= 1;
+    while (a.tmem_cols < 3 * p->bn) a.tmem_cols <<= 1;
     a.bias = bias;
     a.residual = residual;
     a.out = out;

@@ -69,11 +69,13 @@ float half_bits_to_float(uint16_t h) {
     return f;
 }
 
-// High part exactly representable in TF32 (low 13 mantissa bits cleared).
-inline float tf32_hi(float v) {
+// Nearest TF32 value (ties to even) as an f32 with the low 13 mantissa bits
+// clear: the tensor core reads it exactly, and rounding keeps the 3xTF32
+// split unbiased (the same rule as the kernel's A-operand split).
+inline float tf32_rn(float v) {
     uint32_t b;
     std::memcpy(&b, &v, 4);
-    b &= 0xffffe000u;
+    b = (b + 0xfffu + ((b >> 13) & 1u)) & 0xffffe000u;
     float r;
     std::memcpy(&r, &b, 4);
     return r;
@@ -347,8 +349,8 @@ int32_t mbx_param_create(mbx_ctx* ctx, const void* host_data, int32_t dtype, int
                         hi[dst] = half_bits_to_float(static_cast<const uint16_t*>(host_data)[src]);
                     } else {
                         const float v = static_cast<const float*>(host_data)[src];
-                        hi[dst] = tf32_hi(v);
-                        lo[dst] = v - hi[dst];
+                        hi[dst] = tf32_rn(v);
+                        lo[dst] = tf32_rn(v - hi[dst]);
                     }
                 }
         try {

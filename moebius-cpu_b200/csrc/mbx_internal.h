@@ -80,8 +80,8 @@ struct mbx_param {
     int cin_pad = 0;   // c_in rounded up to the 32-channel K chunk
     int bn = 0;        // N tile (output channels per CTA tile)
     int cout_pad = 0;  // c_out rounded up to bn
-    float* hi = nullptr;  // [cout_pad][taps][cin_pad] tf32-exact high part (or the f16 values)
-    float* lo = nullptr;  // same layout, f32 - hi; null for f16 weights (exact in tf32)
+    float* hi = nullptr;  // [cout_pad][taps][cin_pad] TF32-rounded high part (or the f16 values)
+    float* lo = nullptr;  // same layout, TF32-rounded (w - hi); null for f16 weights (exact in TF32)
     CUtensorMap tmap_hi;
     CUtensorMap tmap_lo;
 };
