@@ -135,6 +135,21 @@ int32_t mbx_group_norm_apply(mbx_ctx *ctx, const float *x, int64_t n, int64_t hw
 int32_t mbx_group_norm_forward(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c,
                                int64_t groups, float eps, const float *gamma, const float *beta, const float *add,
                                int32_t silu, float *out);
+/* GroupNorm forward for callers that cannot allocate device memory. No
+ * counterpart in the reference: the Rust engine's scratch is plain host memory.
+ * Same inputs, outputs and results as mbx_group_norm_forward, but it takes the
+ * caller's cudaStream_t (NULL = the legacy default stream) on the current
+ * device instead of a context, and never calls cudaMalloc/cudaFree or any
+ * other allocator: its scratch (n * ceil(h*w/256) * groups * 16 + n * c * 8
+ * bytes) is one fixed 8 MiB array inside the library, held by every GPU that
+ * loads it until the process exits. Larger problems are rejected with
+ * MBX_ERR_INVALID_ARGUMENT. The first call on a device resolves that array's
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture. All calls share the one array, so calls that overlap on the GPU
+ * (other streams, other host threads) race: serialise them. */
+int32_t mbx_group_norm_forward_noalloc(void *stream, const float *x, int64_t n, int64_t h, int64_t w, int64_t c,
+                                       int64_t groups, float eps, const float *gamma, const float *beta,
+                                       const float *add, int32_t silu, float *out);
 /* LayerNorm over the channels of every token. Reference: layer_norm, src/engine/norm.rs:151-172. */
 int32_t mbx_layer_norm(mbx_ctx *ctx, const float *x, int64_t tokens, int64_t c, const float *gamma,
                        const float *beta, float eps, float *out);

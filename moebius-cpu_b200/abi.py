@@ -72,6 +72,8 @@ SIGNATURES = {
     "mbx_group_norm_affine": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _vp]),
     "mbx_group_norm_apply": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp]),
     "mbx_group_norm_forward": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _i32, _vp]),
+    "mbx_group_norm_forward_noalloc": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _i32,
+                                              _vp]),
     "mbx_layer_norm": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _f32, _vp]),
     "mbx_depthwise3x3": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp]),
     "mbx_conv1x1": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),

@@ -148,6 +148,8 @@ void Pool::release_below(size_t min_bytes) {
     }
 }
 
+void record_error(int32_t code, const char* msg) { set_error(code, msg); }
+
 // Scoped pool allocation for per-call scratch (stream-ordered reuse).
 struct PoolBuf {
     mbx_ctx* ctx;

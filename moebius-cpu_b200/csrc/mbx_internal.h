@@ -88,6 +88,10 @@ struct mbx_param {
 
 namespace mbx {
 
+// Sets the calling thread's mbx_last_error() message (for entry points that
+// catch their own exceptions).
+void record_error(int32_t code, const char* msg);
+
 // Kernel launchers (each returns after enqueueing on ctx->stream).
 void launch_silu_inplace(mbx_ctx* ctx, float* x, int64_t len);
 void launch_add(mbx_ctx* ctx, const float* a, const float* b, float* out, int64_t len);
