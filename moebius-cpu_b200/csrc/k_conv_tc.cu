@@ -8,16 +8,21 @@
 // materialising the patch matrix, and replaces its Winograd path
 // (src/engine/winograd.rs) for stride 1 / pad 1.
 //
-// CTA = one 128 × bn output tile (bn ≤ 160); 10 warps:
-//   warps 0-3  producers: gather the A tile (128 pixels × 32 channels) from
-//              NHWC global memory — zero padding, stride, nearest-2× upsample
-//              and the optional GroupNorm prologue [SiLU](x·scale + shift)
-//              are all applied here — split each value into a TF32-rounded
-//              high part and a TF32-rounded remainder, and store both into
-//              128-byte-swizzled K-major shared-memory tiles.
-//   warp 4     MMA issuer (one thread) + TMEM allocation.
-//   warp 5     TMA issuer (one thread) for the pre-split weight tiles.
-//   warps 6-9  accumulator drain + epilogue (TMEM lane quadrant = warp % 4).
+// CTA = one 128 × bn output tile (bn ≤ 160); 14 warps:
+//   warps 0-3   loaders: gather the A tile (128 output pixels × 32 channels of
+//               one tap) from NHWC global memory with 16-byte cp.async into a
+//               raw staging ring; zero padding (src-size 0), stride and the
+//               nearest-2× upsample are all address arithmetic here.
+//   warps 10-13 converters: apply the optional GroupNorm prologue
+//               [SiLU](x·scale + shift) at spatially valid taps, split each value
+//               into a TF32-rounded high part and a TF32-rounded remainder, and
+//               store both into 128-byte-swizzled K-major MMA tiles.
+//   warp 4      MMA issuer (one thread) + TMEM allocation.
+//   warp 5      TMA issuer (one thread) for the pre-split weight tiles.
+//   warps 6-9   accumulator drain + epilogue (TMEM lane quadrant = warp % 4).
+// Loading and converting are separate warps because the converters' proxy
+// fence (generic smem writes → tensor-core reads) would otherwise wait for
+// every global load still in flight.
 // Precision: f32 weights → 3×TF32 (a_lo·w_hi + a_hi·w_lo + a_hi·w_hi),
 // f16 weights (exact in TF32) → 2×TF32 (a_lo·w + a_hi·w). The tensor core
 // adds each MMA's products into its f32 accumulator with truncation, which
@@ -42,7 +47,8 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;                  // f32 elements per 128-byte swizzle row
 constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;  // 14 warps; see the role map above
+constexpr int kStgSlots = 4;   // raw A staging slots (16 KB each)
 constexpr int kSegChunks = 8;  // K chunks (of 32) per accumulator segment
 constexpr int kMaxBn = 160;    // 3 · bn TMEM columns (two accumulators + the running sum) ≤ 512
 constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
@@ -53,6 +59,7 @@ struct ConvArgs {
     int64_t m_total;
     int h, w, c_in, ho, wo, stride, pad_t, pad_l, up;
     int cin_chunks, k_chunks;
+    int flat;  // 1×1 conv: input pixel = output pixel (no padding, stride or upsample)
     int c_out, bn, n_tiles, stages, tmem_cols;
     const float* bias;
     const float* residual;
@@ -92,7 +99,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for phase `parity` of `bar`. Returns false when the CTA is
 // aborting (another role gave up) or after kWaitLimit cycles, in which case
 // the error is recorded and the abort flag raised.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int site, volatile int* abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int site, volatile int* abort_flag,
                                        bool honour_abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -213,13 +220,33 @@ __device__ __forceinline__ float tf32_rn(float v) {
     return __uint_as_float((u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u);
 }
 
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                  : "memory");
 }
 
-template <bool F32W, bool VEC4>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool F32W, bool VEC4, bool FLAT>
+__global__ void __maxnreg__(128)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
                    const ConvArgs args) {
     extern __shared__ uint8_t smem_raw[];
@@ -230,13 +257,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stages = args.stages;
     const uint32_t b_bytes = (uint32_t)bn * 128u;
     const uint32_t stage_bytes = 2 * A_BYTES + (F32W ? 2 : 1) * b_bytes;
-    // Barriers: full[s], empty[s] per smem stage; acc_full[b], acc_empty[b] per TMEM accumulator.
-    const uint32_t bars = base + (uint32_t)stages * stage_bytes;
+    const uint32_t stg_base = base + (uint32_t)stages * stage_bytes;  // raw A staging ring
+    // Barriers: full[s], empty[s] per MMA stage; sfull[q], sempty[q] per staging slot;
+    // acc_full[b], acc_empty[b] per TMEM accumulator; final (abort path).
+    const uint32_t bars = stg_base + (uint32_t)kStgSlots * A_BYTES;
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
-    auto acc_full_bar = [&](int b) { return bars + 16u * stages + 8u * b; };
-    auto acc_empty_bar = [&](int b) { return bars + 16u * stages + 16u + 8u * b; };
-    const uint32_t final_bar = bars + 16u * stages + 32u;  // abort path: all issued MMAs retired
+    const uint32_t sbars = bars + 16u * stages;
+    auto sfull_bar = [&](int q) { return sbars + 8u * q; };
+    auto sempty_bar = [&](int q) { return sbars + 8u * (kStgSlots + q); };
+    const uint32_t abars = sbars + 16u * kStgSlots;
+    auto acc_full_bar = [&](int b) { return abars + 8u * b; };
+    auto acc_empty_bar = [&](int b) { return abars + 16u + 8u * b; };
+    const uint32_t final_bar = abars + 32u;  // abort path: all issued MMAs retired
     const uint32_t misc = final_bar + 8u;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (misc - base));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
@@ -253,6 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < stages; ++s) {
             mbar_init(full_bar(s), 128 + 1);
             mbar_init(empty_bar(s), 1);
+        }
+        for (int q = 0; q < kStgSlots; ++q) {
+            mbar_init(sfull_bar(q), 128);
+            mbar_init(sempty_bar(q), 128);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full_bar(b), 1);
@@ -271,94 +308,145 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {
-        // ------------------------------------------------------------ producers
-        const int tid = threadIdx.x;
-        const int j = tid & 7;       // 16-byte chunk (4 channels) within the 128-byte row
-        const int rbase = tid >> 3;  // rows rbase + 16·i
+    // Loader / converter thread mapping: 16-byte chunk j (4 channels) of rows rbase + 16·i.
+    const bool loader = warp < 4, converter = warp >= 10;
+    if (loader || converter) {
+        const int tid = threadIdx.x - (converter ? 320 : 0);
+        const int j = tid & 7;
+        const int rbase = tid >> 3;
         const int hi_img = args.h << args.up, wi_img = args.w << args.up;
         const int64_t hw_out = (int64_t)args.ho * args.wo;
-        int pb[8], iy0[8], ix0[8];
-        bool rv[8];
+        // Per row: item index, and the top-left input tap packed as (iy0 << 16) | (ix0 & 0xffff);
+        // rows past the end get an iy0 far outside the image, so every tap reads as padding.
+        int pb[8], geo[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int64_t m = m0 + rbase + 16 * i;
-            rv[i] = m < args.m_total;
-            const int64_t mm = rv[i] ? m : 0;
-            const int64_t b = mm / hw_out;
-            const int64_t rem = mm - b * hw_out;
-            const int oy = (int)(rem / args.wo);
-            const int ox = (int)(rem - (int64_t)oy * args.wo);
-            pb[i] = (int)b;
-            iy0[i] = oy * args.stride - args.pad_t;
-            ix0[i] = ox * args.stride - args.pad_l;
+            pb[i] = 0;
+            geo[i] = 0;
+            if constexpr (!FLAT) {
+                const int64_t m = m0 + rbase + 16 * i;
+                const bool valid = m < args.m_total;
+                const int64_t mm = valid ? m : 0;
+                const int64_t b = mm / hw_out;
+                const int64_t rem = mm - b * hw_out;
+                const int oy = (int)(rem / args.wo);
+                const int ox = (int)(rem - (int64_t)oy * args.wo);
+                pb[i] = (int)b;
+                const int iy0 = valid ? oy * args.stride - args.pad_t : -30000;
+                const int ix0 = ox * args.stride - args.pad_l;
+                geo[i] = (int)(((uint32_t)iy0 << 16) | ((uint32_t)ix0 & 0xffffu));
+            }
         }
-        const bool pro = args.pro_scale != nullptr;
-        for (int kc = 0; kc < K; ++kc) {
-            const int s = kc % stages;
-            if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
-            const int tap = kc / args.cin_chunks;
-            const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
-            const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-            float v[8][4];
+        // Spatial validity of row i's tap and its pixel index.
+        auto tap_pixel = [&](int i, int ky, int kx, bool& ok) -> int64_t {
+            if constexpr (FLAT) {
+                const int64_t pix = m0 + rbase + 16 * i;
+                ok = pix < args.m_total;
+                return pix;
+            } else {
+                const int iy = (geo[i] >> 16) + ky, ix = (int)(int16_t)(geo[i] & 0xffff) + kx;
+                ok = iy >= 0 && iy < hi_img && ix >= 0 && ix < wi_img;
+                return ((int64_t)pb[i] * args.h + (iy >> args.up)) * args.w + (ix >> args.up);
+            }
+        };
+        if (loader) {
+            // ------------------------------------------------------------ loaders
+            // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
+            // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
+            // never waits on its data and keeps up to kStgSlots chunks in flight.
+            for (int kc = 0; kc < K; ++kc) {
+                const int q = kc % kStgSlots;
+                if (!mbar_wait(sempty_bar(q), ((kc / kStgSlots) & 1) ^ 1, args.err, 8, abort_flag, true)) break;
+                const int tap = kc / args.cin_chunks;
+                const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
+                const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int iy = iy0[i] + ky, ix = ix0[i] + kx;
-                const bool ok = rv[i] && iy >= 0 && iy < hi_img && ix >= 0 && ix < wi_img;
-                const int64_t pix = ((int64_t)pb[i] * args.h + (iy >> args.up)) * args.w + (ix >> args.up);
-                if constexpr (VEC4) {
-                    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (ok && c0 < args.c_in) {
-                        f = __ldg(reinterpret_cast<const float4*>(args.x + pix * args.c_in + c0));
-                        if (pro) {
-                            const float4 sc =
-                                __ldg(reinterpret_cast<const float4*>(args.pro_scale + (int64_t)pb[i] * args.c_in + c0));
-                            const float4 sh =
-                                __ldg(reinterpret_cast<const float4*>(args.pro_shift + (int64_t)pb[i] * args.c_in + c0));
-                            f = f4_fma(f, sc, sh);
-                            if (args.pro_silu) {
-                                f.x = dev_silu(f.x);
-                                f.y = dev_silu(f.y);
-                                f.z = dev_silu(f.z);
-                                f.w = dev_silu(f.w);
-                            }
-                        }
-                    }
-                    v[i][0] = f.x;
-                    v[i][1] = f.y;
-                    v[i][2] = f.z;
-                    v[i][3] = f.w;
-                } else {
+                for (int i = 0; i < 8; ++i) {
+                    const int r = rbase + 16 * i;
+                    const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
+                    bool ok;
+                    const int64_t pix = tap_pixel(i, ky, kx, ok);
+                    if constexpr (VEC4) {
+                        const bool in = ok && c0 < args.c_in;
+                        cp_async_16(stg + off, in ? (const void*)(args.x + pix * args.c_in + c0) : (const void*)args.x,
+                                    in ? 16u : 0u);
+                    } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int ch = c0 + e;
-                        float f = 0.0f;
-                        if (ok && ch < args.c_in) {
-                            f = __ldg(args.x + pix * args.c_in + ch);
-                            if (pro) {
-                                f = fmaf(f, __ldg(args.pro_scale + (int64_t)pb[i] * args.c_in + ch),
-                                         __ldg(args.pro_shift + (int64_t)pb[i] * args.c_in + ch));
-                                if (args.pro_silu) f = dev_silu(f);
-                            }
+                        for (int e = 0; e < 4; ++e) {
+                            const bool in = ok && c0 + e < args.c_in;
+                            cp_async_4(stg + off + 4u * e,
+                                       in ? (const void*)(args.x + pix * args.c_in + c0 + e) : (const void*)args.x,
+                                       in ? 4u : 0u);
                         }
-                        v[i][e] = f;
                     }
                 }
+                cp_async_mbar_arrive(sfull_bar(q));
             }
-            const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
-            const uint32_t a_lo = a_hi + A_BYTES;
+            asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
+        } else {
+            // ------------------------------------------------------------ converters
+            // Staging tile → [SiLU](x·scale + shift) at spatially valid taps (padding stays
+            // zero; channel padding beyond c_in meets zero weights) → TF32-rounded hi and lo
+            // tiles of the MMA stage. These warps hold no outstanding global loads, so their
+            // proxy fence before releasing the stage is cheap.
+            const bool pro = args.pro_scale != nullptr;
+            for (int kc = 0; kc < K; ++kc) {
+                const int q = kc % kStgSlots, s = kc % stages;
+                if (!mbar_wait(sfull_bar(q), (kc / kStgSlots) & 1, args.err, 9, abort_flag, true)) break;
+                if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
+                const int tap = kc / args.cin_chunks;
+                const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
+                const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+                const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
+                const uint32_t a_lo = a_hi + A_BYTES;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = rbase + 16 * i;
-                const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
-                const float h0 = tf32_rn(v[i][0]), h1 = tf32_rn(v[i][1]), h2 = tf32_rn(v[i][2]),
-                            h3 = tf32_rn(v[i][3]);
-                st_shared_v4(a_hi + off, h0, h1, h2, h3);
-                st_shared_v4(a_lo + off, tf32_rn(v[i][0] - h0), tf32_rn(v[i][1] - h1), tf32_rn(v[i][2] - h2),
-                             tf32_rn(v[i][3] - h3));
+                for (int i = 0; i < 8; ++i) {
+                    const int r = rbase + 16 * i;
+                    const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
+                    float4 v = ld_shared_v4(stg + off);
+                    if (pro && c0 < args.c_in) {
+                        bool ok;
+                        (void)tap_pixel(i, ky, kx, ok);
+                        if (ok) {
+                            const float* sc = args.pro_scale + (int64_t)pb[i] * args.c_in + c0;
+                            const float* sh = args.pro_shift + (int64_t)pb[i] * args.c_in + c0;
+                            float a[4], b[4];
+                            if constexpr (VEC4) {
+                                const float4 sc4 = __ldg(reinterpret_cast<const float4*>(sc));
+                                const float4 sh4 = __ldg(reinterpret_cast<const float4*>(sh));
+                                a[0] = sc4.x; a[1] = sc4.y; a[2] = sc4.z; a[3] = sc4.w;
+                                b[0] = sh4.x; b[1] = sh4.y; b[2] = sh4.z; b[3] = sh4.w;
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const bool in = c0 + e < args.c_in;
+                                    a[e] = in ? __ldg(sc + e) : 0.0f;
+                                    b[e] = in ? __ldg(sh + e) : 0.0f;
+                                }
+                            }
+                            v.x = fmaf(v.x, a[0], b[0]);
+                            v.y = fmaf(v.y, a[1], b[1]);
+                            v.z = fmaf(v.z, a[2], b[2]);
+                            v.w = fmaf(v.w, a[3], b[3]);
+                            if (args.pro_silu) {
+                                v.x = dev_silu(v.x);
+                                v.y = dev_silu(v.y);
+                                v.z = dev_silu(v.z);
+                                v.w = dev_silu(v.w);
+                            }
+                        }
+                    }
+                    const float h0 = tf32_rn(v.x), h1 = tf32_rn(v.y), h2 = tf32_rn(v.z), h3 = tf32_rn(v.w);
+                    st_shared_v4(a_hi + off, h0, h1, h2, h3);
+                    st_shared_v4(a_lo + off, tf32_rn(v.x - h0), tf32_rn(v.y - h1), tf32_rn(v.z - h2),
+                                 tf32_rn(v.w - h3));
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(full_bar(s));
+                mbar_arrive(sempty_bar(q));
             }
-            fence_proxy_async_smem();
-            mbar_arrive(full_bar(s));
         }
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
@@ -418,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp >= 6 && warp < 10) {
         // ------------------------------------------------------------ drain + epilogue
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = q * 32 + lane;
@@ -518,18 +606,24 @@ void encode_one(CUtensorMap* map, const float* data, int64_t kdim, int64_t rows,
 
 int stage_count(bool f32w, int bn) {
     const int stage = 2 * (int)A_BYTES + (f32w ? 2 : 1) * bn * 128;
-    return std::min(6, (kMaxSmem - 2048) / stage);
+    return std::min(4, (kMaxSmem - 2048 - kStgSlots * (int)A_BYTES) / stage);
 }
 
-template <bool F32W, bool VEC4>
+template <bool F32W, bool VEC4, bool FLAT>
 void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_tiles) {
-    auto kernel = conv_tc_kernel<F32W, VEC4>;
+    auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
     const int stage = 2 * (int)A_BYTES + (F32W ? 2 : 1) * a.bn * 128;
-    const int smem = a.stages * stage + 1024 + 256;
+    const int smem = a.stages * stage + kStgSlots * (int)A_BYTES + 1024 + 512;
     static bool configured = false;
     if (!configured) {
         check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
                    "conv smem attribute");
+        cudaFuncAttributes fa;
+        check_cuda(cudaFuncGetAttributes(&fa, kernel), "conv attributes");
+        if (fa.maxThreadsPerBlock < kThreads)
+            fail(MBX_ERR_INTERNAL, "conv kernel built with " + std::to_string(fa.numRegs) +
+                                       " registers per thread cannot launch " + std::to_string(kThreads) +
+                                       " threads");
         configured = true;
     }
     const int64_t blocks = m_tiles * a.n_tiles;
@@ -578,6 +672,7 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.up = s.up;
     a.cin_chunks = p->cin_pad / BK;
     a.k_chunks = (int)p->taps * a.cin_chunks;
+    a.flat = p->taps == 1 ? 1 : 0;
     a.c_out = (int)p->c_out;
     a.bn = p->bn;
     a.n_tiles = p->cout_pad / p->bn;
@@ -603,10 +698,18 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
                              (!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
     MBX_REQUIRE(aligned_out || (p->c_out & 3) != 0,
                 "conv: out, residual and bias must be 16-byte aligned when c_out is a multiple of 4");
-    if (f32w)
-        vec4 ? run_conv<true, true>(ctx, p, a, m_tiles) : run_conv<true, false>(ctx, p, a, m_tiles);
-    else
-        vec4 ? run_conv<false, true>(ctx, p, a, m_tiles) : run_conv<false, false>(ctx, p, a, m_tiles);
+    if (a.flat) {
+        if (f32w)
+            vec4 ? run_conv<true, true, true>(ctx, p, a, m_tiles) : run_conv<true, false, true>(ctx, p, a, m_tiles);
+        else
+            vec4 ? run_conv<false, true, true>(ctx, p, a, m_tiles) : run_conv<false, false, true>(ctx, p, a, m_tiles);
+    } else {
+        if (f32w)
+            vec4 ? run_conv<true, true, false>(ctx, p, a, m_tiles) : run_conv<true, false, false>(ctx, p, a, m_tiles);
+        else
+            vec4 ? run_conv<false, true, false>(ctx, p, a, m_tiles)
+                 : run_conv<false, false, false>(ctx, p, a, m_tiles);
+    }
     after_launch(ctx, "conv (tcgen05)");
 }
 

@@ -563,6 +563,7 @@ int32_t mbx_conv1x1(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t 
         require_ptr(x, "x");
         require_ptr(out, "out");
         MBX_REQUIRE(out != x, "conv1x1: out must not alias x");
+
         use_device(ctx);
         mbx::ConvShape s{n, h, w, c_in, h, w, 1, 0, 0, 0};
         mbx::launch_conv_tc(ctx, x, s, weight, bias, nullptr, nullptr, false, residual, out);
@@ -603,8 +604,8 @@ int32_t mbx_conv3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t 
         require_ptr(x, "x");
         require_ptr(out, "out");
         MBX_REQUIRE(out != x, "conv3x3: out must not alias x");
-        MBX_REQUIRE((h << (upsample2x ? 1 : 0)) < (1 << 20) && (w << (upsample2x ? 1 : 0)) < (1 << 20),
-                    "image too large");
+        MBX_REQUIRE((h << (upsample2x ? 1 : 0)) < (1 << 14) && (w << (upsample2x ? 1 : 0)) < (1 << 14),
+                    "conv3x3: image side must be below 16384 (after the optional upsample)");
         use_device(ctx);
         mbx::ConvShape s{n, h, w, c_in, ho, wo, int(stride), int(pad[0]), int(pad[1]), upsample2x ? 1 : 0};
         mbx::launch_conv_tc(ctx, x, s, weight, bias, pro_scale, pro_shift, pro_silu != 0, residual, out);
