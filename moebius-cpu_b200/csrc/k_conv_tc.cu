@@ -29,8 +29,12 @@
 // biases long sums toward zero (about 1e-4 relative at K = 11520). So K is
 // cut into segments of kSegChunks chunks (256 K-elements): the MMA warp
 // alternates between two TMEM accumulators, and the drain warps fold each
-// finished segment into a TMEM-resident running sum with round-to-nearest
+// finished segment into a running sum in shared memory with round-to-nearest
 // f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).
+// TMEM (512 columns) holds the two accumulators (2·bn) and a ring of A stages
+// (64 columns each: TF32 high parts, then low parts; lane = tile row) that the
+// MMA reads directly (A from tensor memory), so the converted activations never
+// pass through shared memory.
 // The last segment is folded straight into the epilogue: + bias (+ residual)
 // → global. Every mbarrier wait is bounded; on timeout the CTA records the
 // error in the context's device error word, skips its stores and exits.
@@ -48,9 +52,10 @@ constexpr int BM = 128;
 constexpr int BK = 32;                  // f32 elements per 128-byte swizzle row
 constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int kThreads = 448;  // 14 warps; see the role map above
-constexpr int kStgSlots = 4;   // raw A staging slots (16 KB each)
+constexpr int kStgSlots = 3;   // raw A staging slots (16 KB each)
 constexpr int kSegChunks = 8;  // K chunks (of 32) per accumulator segment
-constexpr int kMaxBn = 160;    // 3 · bn TMEM columns (two accumulators + the running sum) ≤ 512
+constexpr int kMaxBn = 128;       // 2 · bn accumulator columns + 4 A stages of 64 columns ≤ 512
+constexpr int kMaxAStages = 4;
 constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
 constexpr int kMaxSmem = 232448;             // 227 KB opt-in limit per CTA
 
@@ -60,7 +65,7 @@ struct ConvArgs {
     int h, w, c_in, ho, wo, stride, pad_t, pad_l, up;
     int cin_chunks, k_chunks;
     int flat;  // 1×1 conv: input pixel = output pixel (no padding, stride or upsample)
-    int c_out, bn, n_tiles, stages, tmem_cols;
+    int c_out, bn, n_tiles, stages, a_stages, tmem_cols;
     const float* bias;
     const float* residual;
     float* out;
@@ -175,6 +180,16 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// D (+)= A · Bᵀ with A (128 rows × 8 TF32, lane = row, one column per element) in TMEM.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
@@ -197,10 +212,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Round to the nearest TF32 value (ties to even), returned as an f32 whose low
-// 13 mantissa bits are zero, so the tensor core reads it exactly. Rounding (not
-// truncation) keeps the split errors unbiased; truncation biases every
-// product toward zero and the bias grows linearly with K.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -215,9 +226,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Nearest TF32 value (ties away from zero: cvt.rna), returned as an f32 whose
+// low 13 mantissa bits are zero, so the tensor core reads it exactly. Rounding
+// (not truncation) keeps the split errors unbiased; truncation biases every
+// product toward zero and the bias grows linearly with K.
 __device__ __forceinline__ float tf32_rn(float v) {
-    const uint32_t u = __float_as_uint(v);
-    return __uint_as_float((u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u);
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
 }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -254,19 +270,27 @@ __global__ void __maxnreg__(128)
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
     const int bn = args.bn;
-    const int stages = args.stages;
+    const int bstages = args.stages;    // weight-tile ring (shared memory)
+    const int astages = args.a_stages;  // A-operand ring (TMEM)
     const uint32_t b_bytes = (uint32_t)bn * 128u;
-    const uint32_t stage_bytes = 2 * A_BYTES + (F32W ? 2 : 1) * b_bytes;
-    const uint32_t stg_base = base + (uint32_t)stages * stage_bytes;  // raw A staging ring
-    // Barriers: full[s], empty[s] per MMA stage; sfull[q], sempty[q] per staging slot;
-    // acc_full[b], acc_empty[b] per TMEM accumulator; final (abort path).
-    const uint32_t bars = stg_base + (uint32_t)kStgSlots * A_BYTES;
-    auto full_bar = [&](int s) { return bars + 8u * s; };
-    auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
-    const uint32_t sbars = bars + 16u * stages;
+    const uint32_t bstage_bytes = (F32W ? 2 : 1) * b_bytes;
+    const uint32_t stg_base = base + (uint32_t)bstages * bstage_bytes;  // raw A staging ring
+    // Barriers: b_full/b_empty per weight stage, sfull/sempty per staging slot, a_full/a_empty per
+    // TMEM A stage, acc_full/acc_empty per accumulator, final (abort path).
+    // Running sums of the finished K segments: 128 rows × (bn + 4) floats (the 4-float pad
+    // staggers rows across banks for the row-per-thread float4 accesses of the drain warps).
+    const uint32_t sum_stride = (uint32_t)(bn + 4) * 4u;
+    const uint32_t sum_base = stg_base + (uint32_t)kStgSlots * A_BYTES;
+    const uint32_t bars = sum_base + 128u * sum_stride;
+    auto b_full_bar = [&](int s) { return bars + 8u * s; };
+    auto b_empty_bar = [&](int s) { return bars + 8u * (bstages + s); };
+    const uint32_t sbars = bars + 16u * bstages;
     auto sfull_bar = [&](int q) { return sbars + 8u * q; };
     auto sempty_bar = [&](int q) { return sbars + 8u * (kStgSlots + q); };
-    const uint32_t abars = sbars + 16u * kStgSlots;
+    const uint32_t tbars = sbars + 16u * kStgSlots;
+    auto a_full_bar = [&](int a) { return tbars + 8u * a; };
+    auto a_empty_bar = [&](int a) { return tbars + 8u * (kMaxAStages + a); };
+    const uint32_t abars = tbars + 16u * kMaxAStages;
     auto acc_full_bar = [&](int b) { return abars + 8u * b; };
     auto acc_empty_bar = [&](int b) { return abars + 16u + 8u * b; };
     const uint32_t final_bar = abars + 32u;  // abort path: all issued MMAs retired
@@ -281,15 +305,22 @@ __global__ void __maxnreg__(128)
     const int n0 = n_tile * bn;
     const int K = args.k_chunks;
     const int nseg = (K + kSegChunks - 1) / kSegChunks;
+    // TMEM columns: accumulators [0, 2·bn), A stage a at 2·bn + 64·a (32 columns of TF32
+    // high parts, then 32 of low parts; lane = tile row).
+    auto a_col = [&](int a) { return (uint32_t)(2 * bn + 64 * a); };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) {
-            mbar_init(full_bar(s), 128 + 1);
-            mbar_init(empty_bar(s), 1);
+        for (int s = 0; s < bstages; ++s) {
+            mbar_init(b_full_bar(s), 1);
+            mbar_init(b_empty_bar(s), 1);
         }
         for (int q = 0; q < kStgSlots; ++q) {
             mbar_init(sfull_bar(q), 128);
             mbar_init(sempty_bar(q), 128);
+        }
+        for (int a = 0; a < kMaxAStages; ++a) {
+            mbar_init(a_full_bar(a), 128);
+            mbar_init(a_empty_bar(a), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full_bar(b), 1);
@@ -300,7 +331,7 @@ __global__ void __maxnreg__(128)
         fence_mbarrier_init();
     }
     if (warp == 4) {
-        tmem_alloc(smem_u32(tmem_slot), (uint32_t)args.tmem_cols);
+        tmem_alloc(smem_u32(tmem_slot), 512u);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -308,182 +339,172 @@ __global__ void __maxnreg__(128)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Loader / converter thread mapping: 16-byte chunk j (4 channels) of rows rbase + 16·i.
-    const bool loader = warp < 4, converter = warp >= 10;
-    if (loader || converter) {
-        const int tid = threadIdx.x - (converter ? 320 : 0);
-        const int j = tid & 7;
-        const int rbase = tid >> 3;
-        const int hi_img = args.h << args.up, wi_img = args.w << args.up;
-        const int64_t hw_out = (int64_t)args.ho * args.wo;
-        // Per row: item index, and the top-left input tap packed as (iy0 << 16) | (ix0 & 0xffff);
-        // rows past the end get an iy0 far outside the image, so every tap reads as padding.
+    const int hi_img = args.h << args.up, wi_img = args.w << args.up;
+    const int64_t hw_out = (int64_t)args.ho * args.wo;
+    // Row geometry: item index and the top-left input tap packed as (iy0 << 16) | (ix0 & 0xffff);
+    // rows past the end get an iy0 far outside the image, so every tap reads as padding.
+    auto row_geo = [&](int r, int& pb, int& geo) {
+        const int64_t m = m0 + r;
+        const bool valid = m < args.m_total;
+        const int64_t mm = valid ? m : 0;
+        const int64_t b = mm / hw_out;
+        const int64_t rem = mm - b * hw_out;
+        const int oy = (int)(rem / args.wo);
+        const int ox = (int)(rem - (int64_t)oy * args.wo);
+        pb = (int)b;
+        const int iy0 = valid ? oy * args.stride - args.pad_t : -30000;
+        const int ix0 = ox * args.stride - args.pad_l;
+        geo = (int)(((uint32_t)iy0 << 16) | ((uint32_t)ix0 & 0xffffu));
+    };
+    // Spatial validity and input pixel index of row r's tap (ky, kx).
+    auto tap_pixel = [&](int r, int pb, int geo, int ky, int kx, bool& ok) -> int64_t {
+        if constexpr (FLAT) {
+            const int64_t pix = m0 + r;
+            ok = pix < args.m_total;
+            return pix;
+        } else {
+            const int iy = (geo >> 16) + ky, ix = (int)(int16_t)(geo & 0xffff) + kx;
+            ok = iy >= 0 && iy < hi_img && ix >= 0 && ix < wi_img;
+            return ((int64_t)pb * args.h + (iy >> args.up)) * args.w + (ix >> args.up);
+        }
+    };
+
+    if (warp < 4) {
+        // ------------------------------------------------------------ loaders
+        // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
+        // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
+        // never waits on its data and keeps up to kStgSlots chunks in flight.
+        const int tid = threadIdx.x;
+        const int j = tid & 7;       // 16-byte chunk (4 channels) of the 128-byte row
+        const int rbase = tid >> 3;  // rows rbase + 16·i
         int pb[8], geo[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             pb[i] = 0;
             geo[i] = 0;
-            if constexpr (!FLAT) {
-                const int64_t m = m0 + rbase + 16 * i;
-                const bool valid = m < args.m_total;
-                const int64_t mm = valid ? m : 0;
-                const int64_t b = mm / hw_out;
-                const int64_t rem = mm - b * hw_out;
-                const int oy = (int)(rem / args.wo);
-                const int ox = (int)(rem - (int64_t)oy * args.wo);
-                pb[i] = (int)b;
-                const int iy0 = valid ? oy * args.stride - args.pad_t : -30000;
-                const int ix0 = ox * args.stride - args.pad_l;
-                geo[i] = (int)(((uint32_t)iy0 << 16) | ((uint32_t)ix0 & 0xffffu));
-            }
+            if constexpr (!FLAT) row_geo(rbase + 16 * i, pb[i], geo[i]);
         }
-        // Spatial validity of row i's tap and its pixel index.
-        auto tap_pixel = [&](int i, int ky, int kx, bool& ok) -> int64_t {
-            if constexpr (FLAT) {
-                const int64_t pix = m0 + rbase + 16 * i;
-                ok = pix < args.m_total;
-                return pix;
-            } else {
-                const int iy = (geo[i] >> 16) + ky, ix = (int)(int16_t)(geo[i] & 0xffff) + kx;
-                ok = iy >= 0 && iy < hi_img && ix >= 0 && ix < wi_img;
-                return ((int64_t)pb[i] * args.h + (iy >> args.up)) * args.w + (ix >> args.up);
+        for (int kc = 0; kc < K; ++kc) {
+            const int q = kc % kStgSlots;
+            if (!mbar_wait(sempty_bar(q), ((kc / kStgSlots) & 1) ^ 1, args.err, 8, abort_flag, true)) break;
+            const int tap = kc / args.cin_chunks;
+            const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
+            const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+            const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = rbase + 16 * i;
+                const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
+                bool ok;
+                const int64_t pix = tap_pixel(r, pb[i], geo[i], ky, kx, ok);
+                if constexpr (VEC4) {
+                    const bool in = ok && c0 < args.c_in;
+                    cp_async_16(stg + off, in ? (const void*)(args.x + pix * args.c_in + c0) : (const void*)args.x,
+                                in ? 16u : 0u);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const bool in = ok && c0 + e < args.c_in;
+                        cp_async_4(stg + off + 4u * e,
+                                   in ? (const void*)(args.x + pix * args.c_in + c0 + e) : (const void*)args.x,
+                                   in ? 4u : 0u);
+                    }
+                }
             }
-        };
-        if (loader) {
-            // ------------------------------------------------------------ loaders
-            // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
-            // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
-            // never waits on its data and keeps up to kStgSlots chunks in flight.
-            for (int kc = 0; kc < K; ++kc) {
-                const int q = kc % kStgSlots;
-                if (!mbar_wait(sempty_bar(q), ((kc / kStgSlots) & 1) ^ 1, args.err, 8, abort_flag, true)) break;
+            cp_async_mbar_arrive(sfull_bar(q));
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
+    } else if (warp >= 10) {
+        // ------------------------------------------------------------ converters
+        // One tile row per thread (its TMEM lane): staging row → [SiLU](x·scale + shift) at a
+        // spatially valid tap (padding stays zero; channel padding beyond c_in meets zero
+        // weights) → TF32-rounded high and low parts written to the A stage in TMEM.
+        const int qd = warp & 3;
+        const int r = qd * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+        int pb = 0, geo = 0;
+        if constexpr (!FLAT) row_geo(r, pb, geo);
+        const bool pro = args.pro_scale != nullptr;
+        for (int kc = 0; kc < K; ++kc) {
+            const int q = kc % kStgSlots, a = kc % astages;
+            if (!mbar_wait(sfull_bar(q), (kc / kStgSlots) & 1, args.err, 9, abort_flag, true)) break;
+            if (!mbar_wait(a_empty_bar(a), ((kc / astages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
+            const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
+            float v[32];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const float4 f = ld_shared_v4(stg + ((uint32_t)(jj ^ (r & 7)) << 4));
+                v[4 * jj] = f.x;
+                v[4 * jj + 1] = f.y;
+                v[4 * jj + 2] = f.z;
+                v[4 * jj + 3] = f.w;
+            }
+            mbar_arrive(sempty_bar(q));  // the staging row is in registers
+            if (pro) {
                 const int tap = kc / args.cin_chunks;
-                const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
-                const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+                const int cb = (kc - tap * args.cin_chunks) * BK;
+                bool ok;
+                (void)tap_pixel(r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
+                if (ok) {
+                    const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
+                    const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int r = rbase + 16 * i;
-                    const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
-                    bool ok;
-                    const int64_t pix = tap_pixel(i, ky, kx, ok);
-                    if constexpr (VEC4) {
-                        const bool in = ok && c0 < args.c_in;
-                        cp_async_16(stg + off, in ? (const void*)(args.x + pix * args.c_in + c0) : (const void*)args.x,
-                                    in ? 16u : 0u);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const bool in = ok && c0 + e < args.c_in;
-                            cp_async_4(stg + off + 4u * e,
-                                       in ? (const void*)(args.x + pix * args.c_in + c0 + e) : (const void*)args.x,
-                                       in ? 4u : 0u);
+                    for (int e = 0; e < 32; ++e) {
+                        if (cb + e < args.c_in) {
+                            float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
+                            if (args.pro_silu) y = dev_silu(y);
+                            v[e] = y;
                         }
                     }
                 }
-                cp_async_mbar_arrive(sfull_bar(q));
             }
-            asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
-        } else {
-            // ------------------------------------------------------------ converters
-            // Staging tile → [SiLU](x·scale + shift) at spatially valid taps (padding stays
-            // zero; channel padding beyond c_in meets zero weights) → TF32-rounded hi and lo
-            // tiles of the MMA stage. These warps hold no outstanding global loads, so their
-            // proxy fence before releasing the stage is cheap.
-            const bool pro = args.pro_scale != nullptr;
-            for (int kc = 0; kc < K; ++kc) {
-                const int q = kc % kStgSlots, s = kc % stages;
-                if (!mbar_wait(sfull_bar(q), (kc / kStgSlots) & 1, args.err, 9, abort_flag, true)) break;
-                if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
-                const int tap = kc / args.cin_chunks;
-                const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
-                const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
-                const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
-                const uint32_t a_lo = a_hi + A_BYTES;
+            float h[32];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int r = rbase + 16 * i;
-                    const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
-                    float4 v = ld_shared_v4(stg + off);
-                    if (pro && c0 < args.c_in) {
-                        bool ok;
-                        (void)tap_pixel(i, ky, kx, ok);
-                        if (ok) {
-                            const float* sc = args.pro_scale + (int64_t)pb[i] * args.c_in + c0;
-                            const float* sh = args.pro_shift + (int64_t)pb[i] * args.c_in + c0;
-                            float a[4], b[4];
-                            if constexpr (VEC4) {
-                                const float4 sc4 = __ldg(reinterpret_cast<const float4*>(sc));
-                                const float4 sh4 = __ldg(reinterpret_cast<const float4*>(sh));
-                                a[0] = sc4.x; a[1] = sc4.y; a[2] = sc4.z; a[3] = sc4.w;
-                                b[0] = sh4.x; b[1] = sh4.y; b[2] = sh4.z; b[3] = sh4.w;
-                            } else {
+            for (int e = 0; e < 32; ++e) h[e] = tf32_rn(v[e]);
+            tmem_st32(lane_base + a_col(a), h);  // h stays untouched until the wait below
 #pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    const bool in = c0 + e < args.c_in;
-                                    a[e] = in ? __ldg(sc + e) : 0.0f;
-                                    b[e] = in ? __ldg(sh + e) : 0.0f;
-                                }
-                            }
-                            v.x = fmaf(v.x, a[0], b[0]);
-                            v.y = fmaf(v.y, a[1], b[1]);
-                            v.z = fmaf(v.z, a[2], b[2]);
-                            v.w = fmaf(v.w, a[3], b[3]);
-                            if (args.pro_silu) {
-                                v.x = dev_silu(v.x);
-                                v.y = dev_silu(v.y);
-                                v.z = dev_silu(v.z);
-                                v.w = dev_silu(v.w);
-                            }
-                        }
-                    }
-                    const float h0 = tf32_rn(v.x), h1 = tf32_rn(v.y), h2 = tf32_rn(v.z), h3 = tf32_rn(v.w);
-                    st_shared_v4(a_hi + off, h0, h1, h2, h3);
-                    st_shared_v4(a_lo + off, tf32_rn(v.x - h0), tf32_rn(v.y - h1), tf32_rn(v.z - h2),
-                                 tf32_rn(v.w - h3));
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(full_bar(s));
-                mbar_arrive(sempty_bar(q));
-            }
+            for (int e = 0; e < 32; ++e) v[e] = tf32_rn(v[e] - h[e]);
+            tmem_st32(lane_base + a_col(a) + 32u, v);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(a_full_bar(a));
         }
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(bn);
             for (int kc = 0; kc < K; ++kc) {
-                const int s = kc % stages;
+                const int s = kc % bstages, a = kc % astages;
                 const int seg = kc / kSegChunks, b = seg & 1;
                 const bool seg_first = kc % kSegChunks == 0;
                 const bool seg_last = (kc + 1) % kSegChunks == 0 || kc + 1 == K;
                 if (seg_first &&
                     !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true))
                     break;
-                if (!mbar_wait(full_bar(s), (kc / stages) & 1, args.err, 3, abort_flag, true)) break;
+                if (!mbar_wait(b_full_bar(s), (kc / bstages) & 1, args.err, 3, abort_flag, true)) break;
+                if (!mbar_wait(a_full_bar(a), (kc / astages) & 1, args.err, 10, abort_flag, true)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * bn);
-                const uint32_t a_hi = base + (uint32_t)s * stage_bytes;
-                const uint32_t a_lo = a_hi + A_BYTES;
-                const uint32_t b_hi = a_hi + 2 * A_BYTES;
+                const uint32_t ah = tmem + a_col(a), al = ah + 32u;
+                const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
                 const uint32_t b_lo = b_hi + b_bytes;
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t koff = (uint32_t)kk * 32u;
-                    const uint64_t adh = sw128_desc(a_hi + koff), adl = sw128_desc(a_lo + koff);
-                    const uint64_t bdh = sw128_desc(b_hi + koff);
+                    const uint64_t bdh = sw128_desc(b_hi + (uint32_t)kk * 32u);
                     const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
+                    const uint32_t ko = (uint32_t)kk * 8u;
                     if constexpr (F32W) {
-                        const uint64_t bdl = sw128_desc(b_lo + koff);
-                        mma_tf32(d, adl, bdh, idesc, acc);
-                        mma_tf32(d, adh, bdl, idesc, 1u);
-                        mma_tf32(d, adh, bdh, idesc, 1u);
+                        const uint64_t bdl = sw128_desc(b_lo + (uint32_t)kk * 32u);
+                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                        mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
+                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
                     } else {
-                        mma_tf32(d, adl, bdh, idesc, acc);
-                        mma_tf32(d, adh, bdh, idesc, 1u);
+                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
                     }
                 }
-                mma_commit(empty_bar(s));
+                mma_commit(b_empty_bar(s));
+                mma_commit(a_empty_bar(a));
                 if (seg_last) mma_commit(acc_full_bar(b));
             }
             if (*abort_flag) {
@@ -497,12 +518,12 @@ __global__ void __maxnreg__(128)
         // ------------------------------------------------------------ TMA issuer
         if (lane == 0) {
             for (int kc = 0; kc < K; ++kc) {
-                const int s = kc % stages;
-                if (!mbar_wait(empty_bar(s), ((kc / stages) & 1) ^ 1, args.err, 4, abort_flag, true)) break;
-                const uint32_t b_hi = base + (uint32_t)s * stage_bytes + 2 * A_BYTES;
-                mbar_arrive_expect_tx(full_bar(s), (F32W ? 2u : 1u) * b_bytes);
-                tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, full_bar(s));
-                if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, full_bar(s));
+                const int s = kc % bstages;
+                if (!mbar_wait(b_empty_bar(s), ((kc / bstages) & 1) ^ 1, args.err, 4, abort_flag, true)) break;
+                const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
+                mbar_arrive_expect_tx(b_full_bar(s), bstage_bytes);
+                tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, b_full_bar(s));
+                if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, b_full_bar(s));
             }
         }
         __syncwarp();
@@ -512,28 +533,31 @@ __global__ void __maxnreg__(128)
         const int row = q * 32 + lane;
         const int64_t m = m0 + row;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        const uint32_t sum_col = (uint32_t)(2 * bn);
+        const uint32_t srow = sum_base + (uint32_t)row * sum_stride;
         const bool vec_out = (args.c_out & 3) == 0;
-        bool ok = true;
         for (int seg = 0; seg < nseg; ++seg) {
             const int b = seg & 1;
-            if (!mbar_wait(acc_full_bar(b), (seg >> 1) & 1, args.err, 6, abort_flag, true)) {
-                ok = false;
-                break;
-            }
+            if (!mbar_wait(acc_full_bar(b), (seg >> 1) & 1, args.err, 6, abort_flag, true)) break;
             tc_fence_after();
             const bool last = seg + 1 == nseg;
             for (int cc = 0; cc < bn; cc += 32) {
                 float acc[32];
                 tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
                 if (seg > 0) {
-                    float run[32];
-                    tmem_ld32(lane_base + sum_col + (uint32_t)cc, run);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = run[i] + acc[i];
+                    for (int v = 0; v < 8; ++v) {
+                        const float4 r4 = ld_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u);
+                        acc[4 * v] = r4.x + acc[4 * v];
+                        acc[4 * v + 1] = r4.y + acc[4 * v + 1];
+                        acc[4 * v + 2] = r4.z + acc[4 * v + 2];
+                        acc[4 * v + 3] = r4.w + acc[4 * v + 3];
+                    }
                 }
                 if (!last) {
-                    tmem_st32(lane_base + sum_col + (uint32_t)cc, acc);
+#pragma unroll
+                    for (int v = 0; v < 8; ++v)
+                        st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1], acc[4 * v + 2],
+                                     acc[4 * v + 3]);
                     continue;
                 }
                 if (m >= args.m_total) continue;
@@ -566,11 +590,9 @@ __global__ void __maxnreg__(128)
                     }
                 }
             }
-            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(acc_empty_bar(b));
+            mbar_arrive(acc_empty_bar(b));  // the accumulator has been read into registers
         }
-        (void)ok;
     }
     tc_fence_before();
     __syncthreads();
@@ -604,16 +626,18 @@ void encode_one(CUtensorMap* map, const float* data, int64_t kdim, int64_t rows,
     if (r != CUDA_SUCCESS) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
 }
 
+int sum_bytes(int bn) { return 128 * (bn + 4) * 4; }
+
 int stage_count(bool f32w, int bn) {
-    const int stage = 2 * (int)A_BYTES + (f32w ? 2 : 1) * bn * 128;
-    return std::min(4, (kMaxSmem - 2048 - kStgSlots * (int)A_BYTES) / stage);
+    const int stage = (f32w ? 2 : 1) * bn * 128;
+    return std::min(8, (kMaxSmem - 2048 - kStgSlots * (int)A_BYTES - sum_bytes(bn)) / stage);
 }
 
 template <bool F32W, bool VEC4, bool FLAT>
 void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_tiles) {
     auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
-    const int stage = 2 * (int)A_BYTES + (F32W ? 2 : 1) * a.bn * 128;
-    const int smem = a.stages * stage + kStgSlots * (int)A_BYTES + 1024 + 512;
+    const int stage = (F32W ? 2 : 1) * a.bn * 128;
+    const int smem = a.stages * stage + kStgSlots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
     static bool configured = false;
     if (!configured) {
         check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
@@ -678,8 +702,8 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.n_tiles = p->cout_pad / p->bn;
     const bool f32w = p->lo != nullptr;
     a.stages = stage_count(f32w, p->bn);
-    a.tmem_cols = 32;
-    while (a.tmem_cols < 3 * p->bn) a.tmem_cols <<= 1;
+    a.tmem_cols = 512;
+    a.a_stages = std::min(kMaxAStages, (512 - 2 * p->bn) / 64);
     a.bias = bias;
     a.residual = residual;
     a.out = out;
