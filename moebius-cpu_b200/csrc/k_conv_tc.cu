@@ -122,9 +122,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     }
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ void fence_mbarrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -169,15 +166,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
 __device__ __forceinline__ uint32_t idesc_tf32(int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
 }
 
 // D (+)= A · Bᵀ with A (128 rows × 8 TF32, lane = row, one column per element) in TMEM.

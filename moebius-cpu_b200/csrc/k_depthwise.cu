@@ -2,11 +2,13 @@
 // (reference src/engine/depthwise.rs:31-185).
 //
 // Each thread owns one channel vector (4 channels, or 1 for channel counts
-// that are not multiples of 4) at one x position and walks a strip of output
-// rows with a 3×3 register window: every step loads only the new input row's
-// three pixels (the left and right ones are the neighbouring threads' centre
-// pixels, so they come from L1), so DRAM traffic is about one read of the
-// input plus one write of the output. Taps are accumulated bias-first in
+// that are not multiples of 4) at one x position and walks a 64-row strip of
+// output rows with a 3×3 register window, keeping the next three input rows in
+// flight: every step loads only one new input row's three pixels (the left
+// and right ones are the neighbouring threads' centre pixels, so they come
+// from L1). A CTA covers 8 channel vectors × 16 x-positions; the x-halo columns
+// belong to neighbouring CTAs that run at the same time, so they come from L2,
+// and DRAM traffic is about one read of the input (+3% y-halo) plus one write. Taps are accumulated bias-first in
 // (ky, kx) order with fma(tap, x, acc) as in acc_block (:112-143); padding
 // taps contribute nothing.
 #include "mbx_device.cuh"
@@ -15,8 +17,9 @@
 namespace mbx {
 namespace {
 
-constexpr int kDwThreads = 256;
-constexpr int kDwRows = 16;  // output rows per thread strip
+constexpr int kDwThreads = 128;
+constexpr int kDwRows = 64;  // output rows per thread strip (y-halo re-read: 2/64)
+constexpr int kDwQuads = 8;  // channel vectors per CTA row (16 x-positions per CTA)
 
 template <int V>
 struct Vec {
@@ -84,18 +87,37 @@ __device__ __forceinline__ Vec<V> taps(const Vec<V> (&win)[3][3], const Vec<V> (
 }
 
 // grid: x = output channel-vector blocks, y = x-position blocks, z = item × strip.
-template <int V, int EPI>
+// The CTA's taps and bias sit in shared memory (read with warp broadcasts); the
+// registers hold the 3×3 window plus a queue of DEPTH input rows in flight.
+template <int V, int EPI, int DEPTH>
 __global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restrict__ x, int h, int w, int c,
                                                            const float* __restrict__ weight,
                                                            const float* __restrict__ bias, float* __restrict__ out,
                                                            int qb, int strips) {
     constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
+    constexpr int kSets = kGlu ? 2 : 1;  // value (and gate) channel sets
+    __shared__ Vec<V> s_w[kSets][9][kDwQuads];
+    __shared__ Vec<V> s_b[kSets][kDwQuads];
     const int c_out = kGlu ? c / 2 : c;
     const int cvo = c_out / V;
     const int xb = kDwThreads / qb;
     const int t = threadIdx.x;
+    // Stage the taps of this CTA's channel vectors.
+    for (int e = t; e < kSets * 10 * qb; e += kDwThreads) {
+        const int set = e / (10 * qb), rem = e % (10 * qb), tap = rem / qb, qq = rem % qb;
+        const int qv = blockIdx.x * qb + qq;
+        if (qv < cvo) {
+            const int ch = set * c_out + qv * V;
+            if (tap < 9)
+                s_w[set][tap][qq] = vload<V>(weight + tap * c + ch);
+            else
+                s_b[set][qq] = vload<V>(bias + ch);
+        }
+    }
+    __syncthreads();
     if (t >= qb * xb) return;
-    const int qv = blockIdx.x * qb + t % qb;
+    const int qq = t % qb;
+    const int qv = blockIdx.x * qb + qq;
     const int ox = blockIdx.y * xb + t / qb;
     if (qv >= cvo || ox >= w) return;
     const int b = blockIdx.z / strips;
@@ -104,46 +126,52 @@ __global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restri
     const int ch = qv * V;
     const float* xb_ = x + (int64_t)b * h * w * c;
 
-    Vec<V> wt[9], bs, wg[9], bg;
+    Vec<V> win[kSets][3][3];
+    Vec<V> q[kSets][DEPTH][3];  // rows y+1 … y+DEPTH, loaded ahead
 #pragma unroll
-    for (int k = 0; k < 9; ++k) wt[k] = vload<V>(weight + k * c + ch);
-    bs = vload<V>(bias + ch);
-    if constexpr (kGlu) {
+    for (int set = 0; set < kSets; ++set) {
+        load_row<V>(xb_, h, w, c, y0 - 1, ox, set * c_out + ch, win[set][0]);
+        load_row<V>(xb_, h, w, c, y0, ox, set * c_out + ch, win[set][1]);
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wg[k] = vload<V>(weight + k * c + c_out + ch);
-        bg = vload<V>(bias + c_out + ch);
-    }
-    Vec<V> win[3][3], gwin[3][3];
-    load_row<V>(xb_, h, w, c, y0 - 1, ox, ch, win[0]);
-    load_row<V>(xb_, h, w, c, y0, ox, ch, win[1]);
-    if constexpr (kGlu) {
-        load_row<V>(xb_, h, w, c, y0 - 1, ox, c_out + ch, gwin[0]);
-        load_row<V>(xb_, h, w, c, y0, ox, c_out + ch, gwin[1]);
+        for (int d = 0; d < DEPTH; ++d) load_row<V>(xb_, h, w, c, y0 + 1 + d, ox, set * c_out + ch, q[set][d]);
     }
     const bool left = ox > 0, right = ox + 1 < w;
     for (int y = y0; y < y1; ++y) {
-        load_row<V>(xb_, h, w, c, y + 1, ox, ch, win[2]);
-        if constexpr (kGlu) load_row<V>(xb_, h, w, c, y + 1, ox, c_out + ch, gwin[2]);
+#pragma unroll
+        for (int set = 0; set < kSets; ++set) {
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                win[set][2][k] = q[set][0][k];
+#pragma unroll
+                for (int d = 0; d + 1 < DEPTH; ++d) q[set][d][k] = q[set][d + 1][k];
+            }
+            if (y + DEPTH < y1) load_row<V>(xb_, h, w, c, y + 1 + DEPTH, ox, set * c_out + ch, q[set][DEPTH - 1]);
+        }
         const bool top = y > 0, bottom = y + 1 < h;
-        Vec<V> acc = taps<V>(win, wt, bs, top, bottom, left, right);
+        Vec<V> acc[kSets];
+#pragma unroll
+        for (int set = 0; set < kSets; ++set) {
+            Vec<V> wt[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) wt[k] = s_w[set][k][qq];
+            acc[set] = taps<V>(win[set], wt, s_b[set][qq], top, bottom, left, right);
+        }
+        Vec<V> res = acc[0];
         if constexpr (EPI == MBX_EPILOGUE_RELU) {
 #pragma unroll
-            for (int k = 0; k < V; ++k) acc.v[k] = fmaxf(acc.v[k], 0.0f);
+            for (int k = 0; k < V; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
         } else if constexpr (kGlu) {
-            const Vec<V> g = taps<V>(gwin, wg, bg, top, bottom, left, right);
 #pragma unroll
-            for (int k = 0; k < V; ++k) acc.v[k] = acc.v[k] * dev_silu(g.v[k]);
+            for (int k = 0; k < V; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
         }
-        vstore<V>(out + (((int64_t)b * h + y) * w + ox) * c_out + ch, acc);
+        vstore<V>(out + (((int64_t)b * h + y) * w + ox) * c_out + ch, res);
 #pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            win[0][k] = win[1][k];
-            win[1][k] = win[2][k];
-            if constexpr (kGlu) {
-                gwin[0][k] = gwin[1][k];
-                gwin[1][k] = gwin[2][k];
+        for (int set = 0; set < kSets; ++set)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                win[set][0][k] = win[set][1][k];
+                win[set][1][k] = win[set][2][k];
             }
-        }
     }
 }
 
@@ -159,17 +187,18 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
                      aligned16(bias);
     const int V = vec ? 4 : 1;
     const int64_t cvo = c_out / V;
-    const int qb = (int)std::min<int64_t>(cvo, 32);
+    const int qb = (int)std::min<int64_t>(cvo, kDwQuads);
     const int xb = kDwThreads / qb;
     const int64_t strips = (h + kDwRows - 1) / kDwRows;
     MBX_REQUIRE(n * strips < (int64_t(1) << 31) && (cvo + qb - 1) / qb < (int64_t(1) << 31),
                 "depthwise: grid too large");
     MBX_REQUIRE((w + xb - 1) / xb < 65536 && n * strips < 65536 * 32768LL, "depthwise: grid too large");
     dim3 grid((unsigned)((cvo + qb - 1) / qb), (unsigned)((w + xb - 1) / xb), (unsigned)(n * strips));
-    MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h/16) must be <= 65535)");
+    MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h/64) must be <= 65535)");
     const int hh = (int)h, ww = (int)w, cc = (int)c, st = (int)strips;
-#define MBX_DW(VV, EE) \
-    dw3x3_kernel<VV, EE><<<grid, kDwThreads, 0, ctx->stream>>>(x, hh, ww, cc, weight, bias, out, qb, st)
+#define MBX_DW(VV, EE)                                                                                      \
+    dw3x3_kernel<VV, EE, EE == MBX_EPILOGUE_GLU_SILU ? 1 : 3><<<grid, kDwThreads, 0, ctx->stream>>>( \
+        x, hh, ww, cc, weight, bias, out, qb, st)
     if (V == 4) {
         if (epilogue == MBX_EPILOGUE_NONE) MBX_DW(4, MBX_EPILOGUE_NONE);
         else if (epilogue == MBX_EPILOGUE_RELU) MBX_DW(4, MBX_EPILOGUE_RELU);

@@ -2,6 +2,8 @@
 // broadcast add, channel concat. HBM-bound; 128-bit loads/stores whenever the
 // pointers are 16-byte aligned and the channel counts are multiples of 4,
 // grid-stride loops sized to a few waves of the 148 SMs.
+#include <algorithm>
+
 #include "mbx_device.cuh"
 #include "mbx_internal.h"
 
@@ -45,37 +47,50 @@ __global__ void add_scalar(const float* a, const float* b, float* out, int64_t n
 }
 
 // out = (x + bias[c]) + temb[item, c]; V = 4 (float4 over channels) or 1.
+// grid.y = item; each thread keeps one channel vector and walks pixels.
 template <int V>
-__global__ void bias_temb_kernel(const float* __restrict__ x, int64_t hw, int64_t c, const float* __restrict__ bias,
-                                 const float* __restrict__ temb, float* out, int64_t total_v) {
-    const int64_t cv = c / V;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_v;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t q = i % cv;
-        const int64_t item = i / (hw * cv);
-        if constexpr (V == 4) {
-            float4 v = ldg_stream(reinterpret_cast<const float4*>(x) + i);
-            if (bias) {
-                const float4 bb = __ldg(reinterpret_cast<const float4*>(bias) + q);
-                v.x = v.x + bb.x;
-                v.y = v.y + bb.y;
-                v.z = v.z + bb.z;
-                v.w = v.w + bb.w;
-            }
-            if (temb) {
-                const float4 t = __ldg(reinterpret_cast<const float4*>(temb) + item * cv + q);
-                v.x = v.x + t.x;
-                v.y = v.y + t.y;
-                v.z = v.z + t.z;
-                v.w = v.w + t.w;
-            }
-            stg_stream(reinterpret_cast<float4*>(out) + i, v);
-        } else {
-            float v = x[i];
-            if (bias) v = v + bias[q];
-            if (temb) v = v + temb[item * c + q];
-            out[i] = v;
+__global__ void __launch_bounds__(256) bias_temb_kernel(const float* __restrict__ x, int64_t hw, int c,
+                                                        const float* __restrict__ bias,
+                                                        const float* __restrict__ temb, float* out) {
+    const int cv = c / V;
+    const int64_t item = blockIdx.y;
+    ChanStationary m;
+    if (!m.init(cv)) return;
+    for (int j = m.j; j < cv; j += blockDim.x) {
+        // (x + bias) + temb, in that order: keep both addends separate.
+        float bv[V], tv[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            bv[k] = bias ? __ldg(bias + j * V + k) : 0.0f;
+            tv[k] = temb ? __ldg(temb + item * c + j * V + k) : 0.0f;
         }
+        const float* xi = x + item * hw * c + (int64_t)j * V;
+        float* oi = out + item * hw * c + (int64_t)j * V;
+#pragma unroll 4
+        for (int64_t p = m.p0; p < hw; p += m.step) {
+            if constexpr (V == 4) {
+                float4 v = ldg_stream(reinterpret_cast<const float4*>(xi + p * c));
+                if (bias) {
+                    v.x = v.x + bv[0];
+                    v.y = v.y + bv[1];
+                    v.z = v.z + bv[2];
+                    v.w = v.w + bv[3];
+                }
+                if (temb) {
+                    v.x = v.x + tv[0];
+                    v.y = v.y + tv[1];
+                    v.z = v.z + tv[2];
+                    v.w = v.w + tv[3];
+                }
+                stg_stream(reinterpret_cast<float4*>(oi + p * c), v);
+            } else {
+                float v = xi[p * c];
+                if (bias) v = v + bv[0];
+                if (temb) v = v + tv[0];
+                oi[p * c] = v;
+            }
+        }
+        if (cv <= (int)blockDim.x) break;
     }
 }
 
@@ -121,16 +136,18 @@ void launch_add(mbx_ctx* ctx, const float* a, const float* b, float* out, int64_
 
 void launch_bias_temb_add(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* bias,
                           const float* temb, float* out) {
-    const int64_t total = n * hw * c;
+    MBX_REQUIRE(n < 65536 && c < (1 << 24), "bias_temb_add: too many items or channels");
     const bool vec = c % 4 == 0 && aligned16(x) && aligned16(out) && (!bias || aligned16(bias)) &&
                      (!temb || aligned16(temb));
-    if (vec) {
-        bias_temb_kernel<4><<<grid_for(ctx, total / 4, kThreads), kThreads, 0, ctx->stream>>>(x, hw, c, bias, temb,
-                                                                                              out, total / 4);
-    } else {
-        bias_temb_kernel<1><<<grid_for(ctx, total, kThreads), kThreads, 0, ctx->stream>>>(x, hw, c, bias, temb, out,
-                                                                                          total);
-    }
+    const int cv = (int)(vec ? c / 4 : c);
+    const int rows = cv <= kThreads ? kThreads / cv : 1;
+    const int64_t per_item = (hw + rows - 1) / rows;
+    const int64_t want = std::max<int64_t>(1, (int64_t)ctx->sm_count * 8 / n);
+    dim3 grid((unsigned)std::min<int64_t>(per_item, want), (unsigned)n);
+    if (vec)
+        bias_temb_kernel<4><<<grid, kThreads, 0, ctx->stream>>>(x, hw, (int)c, bias, temb, out);
+    else
+        bias_temb_kernel<1><<<grid, kThreads, 0, ctx->stream>>>(x, hw, (int)c, bias, temb, out);
     after_launch(ctx, "bias_temb_add");
 }
 

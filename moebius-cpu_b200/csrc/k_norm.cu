@@ -97,26 +97,37 @@ __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __
 }
 
 // One CTA per item: chunk partials → mean / rstd → per-channel scale, shift
-// (src/engine/norm.rs:91-102).
-__global__ void gn_finalize_kernel(const double* __restrict__ part, int64_t chunks, int64_t hw, int c, int groups,
-                                   float eps, const float* __restrict__ gamma, const float* __restrict__ beta,
-                                   const float* __restrict__ add, float* __restrict__ scale,
-                                   float* __restrict__ shift) {
+// (src/engine/norm.rs:91-102). One warp per group: lanes sum strided chunks in
+// f64, then a fixed shuffle tree (deterministic).
+__global__ void __launch_bounds__(1024) gn_finalize_kernel(const double* __restrict__ part, int64_t chunks,
+                                                           int64_t hw, int c, int groups, float eps,
+                                                           const float* __restrict__ gamma,
+                                                           const float* __restrict__ beta,
+                                                           const float* __restrict__ add, float* __restrict__ scale,
+                                                           float* __restrict__ shift) {
     extern __shared__ double gstat[];  // [groups][2] = mean, rstd
     const int64_t b = blockIdx.x;
     const int cg = c / groups;
     const double count = (double)hw * (double)cg;
-    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int g = warp; g < groups; g += nwarps) {
         double sum = 0.0, sumsq = 0.0;
-        for (int64_t ch = 0; ch < chunks; ++ch) {
+        for (int64_t ch = lane; ch < chunks; ch += 32) {
             const double* src = part + ((b * chunks + ch) * groups + g) * 2;
             sum += src[0];
             sumsq += src[1];
         }
-        const double mean = sum / count;
-        const double var = fmax(sumsq / count - mean * mean, 0.0);
-        gstat[2 * g] = mean;
-        gstat[2 * g + 1] = 1.0 / sqrt(var + (double)eps);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            sumsq += __shfl_xor_sync(0xffffffffu, sumsq, o);
+        }
+        if (lane == 0) {
+            const double mean = sum / count;
+            const double var = fmax(sumsq / count - mean * mean, 0.0);
+            gstat[2 * g] = mean;
+            gstat[2 * g + 1] = 1.0 / sqrt(var + (double)eps);
+        }
     }
     __syncthreads();
     for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
@@ -129,40 +140,53 @@ __global__ void gn_finalize_kernel(const double* __restrict__ part, int64_t chun
     }
 }
 
+// grid.y = item; each thread keeps one channel vector's scale/shift in registers.
 template <int V, bool SILU, bool RES>
-__global__ void gn_apply_kernel(const float* __restrict__ x, int64_t hw, int64_t c, const float* __restrict__ scale,
-                                const float* __restrict__ shift, const float* __restrict__ residual,
-                                float* __restrict__ out, int64_t total_v) {
-    const int64_t cv = c / V;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_v;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t q = i % cv;
-        const int64_t item = i / (hw * cv);
-        if constexpr (V == 4) {
-            const float4 v = ldg_stream(reinterpret_cast<const float4*>(x) + i);
-            const float4 a = __ldg(reinterpret_cast<const float4*>(scale + item * c) + q);
-            const float4 s = __ldg(reinterpret_cast<const float4*>(shift + item * c) + q);
-            float4 y = f4_fma(v, a, s);
-            if (SILU) {
-                y.x = dev_silu(y.x);
-                y.y = dev_silu(y.y);
-                y.z = dev_silu(y.z);
-                y.w = dev_silu(y.w);
-            }
-            if (RES) {
-                const float4 r = ldg_stream(reinterpret_cast<const float4*>(residual) + i);
-                y.x += r.x;
-                y.y += r.y;
-                y.z += r.z;
-                y.w += r.w;
-            }
-            stg_stream(reinterpret_cast<float4*>(out) + i, y);
-        } else {
-            float y = fmaf(x[i], scale[item * c + q], shift[item * c + q]);
-            if (SILU) y = dev_silu(y);
-            if (RES) y += residual[i];
-            out[i] = y;
+__global__ void __launch_bounds__(256) gn_apply_kernel(const float* __restrict__ x, int64_t hw, int c,
+                                                       const float* __restrict__ scale,
+                                                       const float* __restrict__ shift,
+                                                       const float* __restrict__ residual, float* __restrict__ out) {
+    const int cv = c / V;
+    const int64_t item = blockIdx.y;
+    ChanStationary m;
+    if (!m.init(cv)) return;
+    for (int j = m.j; j < cv; j += blockDim.x) {
+        float a[V], b[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            a[k] = __ldg(scale + item * c + j * V + k);
+            b[k] = __ldg(shift + item * c + j * V + k);
         }
+        const int64_t base = item * hw * c + (int64_t)j * V;
+#pragma unroll 4
+        for (int64_t p = m.p0; p < hw; p += m.step) {
+            const int64_t i = base + p * c;
+            if constexpr (V == 4) {
+                const float4 v = ldg_stream(reinterpret_cast<const float4*>(x + i));
+                float4 y = make_float4(fmaf(v.x, a[0], b[0]), fmaf(v.y, a[1], b[1]), fmaf(v.z, a[2], b[2]),
+                                       fmaf(v.w, a[3], b[3]));
+                if (SILU) {
+                    y.x = dev_silu(y.x);
+                    y.y = dev_silu(y.y);
+                    y.z = dev_silu(y.z);
+                    y.w = dev_silu(y.w);
+                }
+                if (RES) {
+                    const float4 r = ldg_stream(reinterpret_cast<const float4*>(residual + i));
+                    y.x += r.x;
+                    y.y += r.y;
+                    y.z += r.z;
+                    y.w += r.w;
+                }
+                stg_stream(reinterpret_cast<float4*>(out + i), y);
+            } else {
+                float y = fmaf(x[i], a[0], b[0]);
+                if (SILU) y = dev_silu(y);
+                if (RES) y += residual[i];
+                out[i] = y;
+            }
+        }
+        if (cv <= (int)blockDim.x) break;
     }
 }
 
@@ -267,43 +291,39 @@ void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int
 void launch_gn_finalize(mbx_ctx* ctx, const double* part, int64_t n, int64_t hw, int64_t c, int64_t groups,
                         float eps, const float* gamma, const float* beta, const float* add, float* scale,
                         float* shift) {
-    gn_finalize_kernel<<<(unsigned)n, 256, groups * 2 * sizeof(double), ctx->stream>>>(
+    gn_finalize_kernel<<<(unsigned)n, 1024, groups * 2 * sizeof(double), ctx->stream>>>(
         part, gn_chunks(hw), hw, (int)c, (int)groups, eps, gamma, beta, add, scale, shift);
     after_launch(ctx, "group_norm finalize");
 }
 
 void launch_gn_apply(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int64_t c, const float* scale,
                      const float* shift, bool silu, const float* residual, float* out) {
-    const int64_t total = n * hw * c;
+    MBX_REQUIRE(n < 65536, "group_norm apply: too many items");
     const bool vec = c % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) &&
                      (!residual || aligned16(residual));
     const int threads = 256;
+    const int cv = (int)(vec ? c / 4 : c);
+    const int rows = cv <= threads ? threads / cv : 1;
+    const int64_t per_item = (hw + rows - 1) / rows;
+    const int64_t want = std::max<int64_t>(1, (int64_t)ctx->sm_count * 8 / n);
+    dim3 grid((unsigned)std::min<int64_t>(per_item, want), (unsigned)n);
+    const int ci = (int)c;
+#define MBX_GN_APPLY(VV, S, R) \
+    gn_apply_kernel<VV, S, R><<<grid, threads, 0, ctx->stream>>>(x, hw, ci, scale, shift, residual, out)
     if (vec) {
-        const int64_t tv = total / 4;
-        const int grid = grid_for(ctx, tv, threads);
-        if (silu)
-            residual ? gn_apply_kernel<4, true, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                         residual, out, tv)
-                     : gn_apply_kernel<4, true, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                          residual, out, tv);
-        else
-            residual ? gn_apply_kernel<4, false, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                          residual, out, tv)
-                     : gn_apply_kernel<4, false, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                           residual, out, tv);
+        if (silu) {
+            if (residual) MBX_GN_APPLY(4, true, true); else MBX_GN_APPLY(4, true, false);
+        } else {
+            if (residual) MBX_GN_APPLY(4, false, true); else MBX_GN_APPLY(4, false, false);
+        }
     } else {
-        const int grid = grid_for(ctx, total, threads);
-        if (silu)
-            residual ? gn_apply_kernel<1, true, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                         residual, out, total)
-                     : gn_apply_kernel<1, true, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                          residual, out, total);
-        else
-            residual ? gn_apply_kernel<1, false, true><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                          residual, out, total)
-                     : gn_apply_kernel<1, false, false><<<grid, threads, 0, ctx->stream>>>(x, hw, c, scale, shift,
-                                                                                           residual, out, total);
+        if (silu) {
+            if (residual) MBX_GN_APPLY(1, true, true); else MBX_GN_APPLY(1, true, false);
+        } else {
+            if (residual) MBX_GN_APPLY(1, false, true); else MBX_GN_APPLY(1, false, false);
+        }
     }
+#undef MBX_GN_APPLY
     after_launch(ctx, "group_norm apply");
 }
 

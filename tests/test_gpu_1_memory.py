@@ -220,3 +220,20 @@ def test_pool_reuses_blocks(mbx, ctx):
     ctx.release_below(1 << 40)
     cached, _ = ctx.pool_stats()
     assert cached == 0
+
+
+@pytest.mark.parametrize("shape,add,silu", [((8, 128, 128, 256), False, True), ((2, 256, 256, 512), True, True),
+                                            ((4, 512, 512, 64), False, False)])
+def test_group_norm_large_tensors(mbx, ctx, oracle, shape, add, silu):
+    """Tensors larger than L2 (the statistics pass and the apply pass both stream from DRAM)."""
+    rng = np.random.default_rng(shape[-1] * 7 + shape[0])
+    n, h, w, c = shape
+    x = (rng.standard_normal(shape, dtype=np.float32) * 1.5 + 0.2).astype(np.float32)
+    gamma = rng.normal(1, 0.02, c).astype(np.float32)
+    beta = rng.normal(0, 0.02, c).astype(np.float32)
+    a = rng.standard_normal((n, c)).astype(np.float32) if add else None
+    got = mbx.group_norm(up(ctx, x), 32, 1e-6, up(ctx, gamma), up(ctx, beta), add=up(ctx, a) if add else None,
+                         silu=silu).numpy()
+    want = oracle.group_norm(x, 32, 1e-6, gamma, beta, a, silu=silu)
+    assert max_rel_err(got, want) <= GATE
+    assert scaled_err(got, want) <= REF_TOL
