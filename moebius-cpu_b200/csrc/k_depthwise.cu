@@ -3,10 +3,10 @@
 //
 // Each thread owns one channel vector (4 channels, or 1 for channel counts
 // that are not multiples of 4) at one x position and walks a 64-row strip of
-// output rows with a 3×3 register window, keeping the next three input rows in
-// flight: every step loads only one new input row's three pixels (the left
-// and right ones are the neighbouring threads' centre pixels, so they come
-// from L1). A CTA covers 8 channel vectors × 16 x-positions; the x-halo columns
+// output rows in blocks of 4 (2 for GLU): each block loads its 6 (4) input rows
+// at once, so many loads are in flight per thread (the left and right pixels
+// are the neighbouring threads' centre pixels and the block-overlap rows were
+// loaded by the previous block, so both come from L1). A CTA covers 8 channel vectors × 16 x-positions; the x-halo columns
 // belong to neighbouring CTAs that run at the same time, so they come from L2,
 // and DRAM traffic is about one read of the input (+3% y-halo) plus one write. Taps are accumulated bias-first in
 // (ky, kx) order with fma(tap, x, acc) as in acc_block (:112-143); padding
@@ -87,9 +87,8 @@ __device__ __forceinline__ Vec<V> taps(const Vec<V> (&win)[3][3], const Vec<V> (
 }
 
 // grid: x = output channel-vector blocks, y = x-position blocks, z = item × strip.
-// The CTA's taps and bias sit in shared memory (read with warp broadcasts); the
-// registers hold the 3×3 window plus a queue of DEPTH input rows in flight.
-template <int V, int EPI, int DEPTH>
+// The CTA's taps and bias sit in shared memory (read with warp broadcasts).
+template <int V, int EPI, int RB>
 __global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restrict__ x, int h, int w, int c,
                                                            const float* __restrict__ weight,
                                                            const float* __restrict__ bias, float* __restrict__ out,
@@ -126,52 +125,39 @@ __global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restri
     const int ch = qv * V;
     const float* xb_ = x + (int64_t)b * h * w * c;
 
-    Vec<V> win[kSets][3][3];
-    Vec<V> q[kSets][DEPTH][3];  // rows y+1 … y+DEPTH, loaded ahead
-#pragma unroll
-    for (int set = 0; set < kSets; ++set) {
-        load_row<V>(xb_, h, w, c, y0 - 1, ox, set * c_out + ch, win[set][0]);
-        load_row<V>(xb_, h, w, c, y0, ox, set * c_out + ch, win[set][1]);
-#pragma unroll
-        for (int d = 0; d < DEPTH; ++d) load_row<V>(xb_, h, w, c, y0 + 1 + d, ox, set * c_out + ch, q[set][d]);
-    }
+    // Blocks of RB output rows: their RB + 2 input rows are loaded together (all loads in
+    // flight at once, no register rotation), then the RB rows are computed; the two rows
+    // shared with the next block come from L1.
     const bool left = ox > 0, right = ox + 1 < w;
-    for (int y = y0; y < y1; ++y) {
-#pragma unroll
-        for (int set = 0; set < kSets; ++set) {
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                win[set][2][k] = q[set][0][k];
-#pragma unroll
-                for (int d = 0; d + 1 < DEPTH; ++d) q[set][d][k] = q[set][d + 1][k];
-            }
-            if (y + DEPTH < y1) load_row<V>(xb_, h, w, c, y + 1 + DEPTH, ox, set * c_out + ch, q[set][DEPTH - 1]);
-        }
-        const bool top = y > 0, bottom = y + 1 < h;
-        Vec<V> acc[kSets];
-#pragma unroll
-        for (int set = 0; set < kSets; ++set) {
-            Vec<V> wt[9];
-#pragma unroll
-            for (int k = 0; k < 9; ++k) wt[k] = s_w[set][k][qq];
-            acc[set] = taps<V>(win[set], wt, s_b[set][qq], top, bottom, left, right);
-        }
-        Vec<V> res = acc[0];
-        if constexpr (EPI == MBX_EPILOGUE_RELU) {
-#pragma unroll
-            for (int k = 0; k < V; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
-        } else if constexpr (kGlu) {
-#pragma unroll
-            for (int k = 0; k < V; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
-        }
-        vstore<V>(out + (((int64_t)b * h + y) * w + ox) * c_out + ch, res);
+    for (int y = y0; y < y1; y += RB) {
+        Vec<V> in[kSets][RB + 2][3];
 #pragma unroll
         for (int set = 0; set < kSets; ++set)
 #pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                win[set][0][k] = win[set][1][k];
-                win[set][1][k] = win[set][2][k];
+            for (int rr = 0; rr < RB + 2; ++rr) load_row<V>(xb_, h, w, c, y - 1 + rr, ox, set * c_out + ch, in[set][rr]);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            if (y + r >= y1) break;
+            const bool top = y + r > 0, bottom = y + r + 1 < h;
+            Vec<V> acc[kSets];
+#pragma unroll
+            for (int set = 0; set < kSets; ++set) {
+                const Vec<V>(&win)[3][3] = *reinterpret_cast<const Vec<V>(*)[3][3]>(&in[set][r]);
+                Vec<V> wt[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) wt[k] = s_w[set][k][qq];
+                acc[set] = taps<V>(win, wt, s_b[set][qq], top, bottom, left, right);
             }
+            Vec<V> res = acc[0];
+            if constexpr (EPI == MBX_EPILOGUE_RELU) {
+#pragma unroll
+                for (int k = 0; k < V; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
+            } else if constexpr (kGlu) {
+#pragma unroll
+                for (int k = 0; k < V; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
+            }
+            vstore<V>(out + (((int64_t)b * h + y + r) * w + ox) * c_out + ch, res);
+        }
     }
 }
 
@@ -197,7 +183,7 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
     MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h/64) must be <= 65535)");
     const int hh = (int)h, ww = (int)w, cc = (int)c, st = (int)strips;
 #define MBX_DW(VV, EE)                                                                                      \
-    dw3x3_kernel<VV, EE, EE == MBX_EPILOGUE_GLU_SILU ? 1 : 3><<<grid, kDwThreads, 0, ctx->stream>>>( \
+    dw3x3_kernel<VV, EE, EE == MBX_EPILOGUE_GLU_SILU ? 2 : 4><<<grid, kDwThreads, 0, ctx->stream>>>( \
         x, hh, ww, cc, weight, bias, out, qb, st)
     if (V == 4) {
         if (epilogue == MBX_EPILOGUE_NONE) MBX_DW(4, MBX_EPILOGUE_NONE);
