@@ -197,6 +197,62 @@ def tf32_peak(torch):
     return 2 * 8192 ** 3 / best / 1e12
 
 
+def decoder_flops(lat_h, lat_w):
+    """Direct-conv FLOPs of one decoder pass (1×1 and 3×3 convs, attention GEMMs)."""
+    vae = importlib.import_module("moebius-cpu_b200.vae")
+    total, h, w = 0.0, lat_h, lat_w
+    shapes = vae.decoder_weight_shapes()
+    # conv layers run at the resolution of their level
+    res = {"post_quant_conv": (h, w), "decoder.conv_in": (h, w), "decoder.mid_block": (h, w),
+           "decoder.conv_out": (8 * h, 8 * w), "decoder.conv_norm_out": (8 * h, 8 * w)}
+    for name, shp in shapes.items():
+        if not name.endswith(".weight") or len(shp) < 2:
+            continue
+        if name.startswith("decoder.up_blocks."):
+            lvl = int(name.split(".")[2])
+            hh, ww = h << lvl, w << lvl
+            if ".upsamplers." in name:
+                hh, ww = hh * 2, ww * 2
+        else:
+            key = next(k for k in res if name.startswith(k))
+            hh, ww = res[key]
+        taps = 9 if len(shp) == 4 else 1
+        total += 2.0 * hh * ww * shp[0] * shp[-1] * taps
+    hw = h * w
+    total += 2 * 2.0 * hw * hw * vae.VAE_BLOCK_OUT[-1]  # q·kᵀ and p·v
+    return total
+
+
+def bench_vae_decoder(mbx, ctx, torch, small=False):
+    vae = importlib.import_module("moebius-cpu_b200.vae")
+    lat_hw = 16 if small else 64
+    w = vae.random_decoder_weights(0, f16=True)
+    dec = vae.Decoder(ctx, w, "f16")
+    out = {"workload": f"BASELINE configs[3]: VAE decoder, latent [B,{lat_hw},{lat_hw},4] -> "
+                       f"[B,{8 * lat_hw},{8 * lat_hw},3], seeded random-init f16 weights (2xTF32)",
+           "gflop_per_image": round(decoder_flops(lat_hw, lat_hw) / 1e9, 1)}
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    for bsz in (1, 8):
+        lat = torch.randn(bsz, lat_hw, lat_hw, 4, device="cuda", generator=gen) * vae.SCALING_FACTOR
+        L = mbx.DeviceTensor.wrap(ctx, lat.data_ptr(), tuple(lat.shape))
+        for _ in range(2):
+            dec.decode(L)
+        torch.cuda.synchronize()
+        reps = 3
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(reps):
+            img = dec.decode(L)
+        e_ev.record()
+        e_ev.synchronize()
+        ms = s_ev.elapsed_time(e_ev) / reps
+        out[f"b{bsz}"] = {"ms": round(ms, 2), "images_per_s": round(bsz / (ms / 1e3), 2),
+                          "useful_tflops": round(bsz * decoder_flops(lat_hw, lat_hw) / (ms / 1e3) / 1e12, 1)}
+        del img
+    dec.close()
+    return out
+
+
 # --------------------------------------------------------------------------- our arm
 def run_ours(args):
     import torch
@@ -344,6 +400,11 @@ def run_ours(args):
                            "issued_frac_of_tf32_peak": round(useful * mmas / tf32, 3)}
             p.close()
 
+    # the full VAE decoder (64×64 latent → 512×512 RGB), B = 1 and B = 8.
+    vae_line = None
+    if not args.skip_vae and rank == 0:
+        vae_line = bench_vae_decoder(mbx, ctx, torch, small=args.small)
+
     hbm, peak_kind = peaks()
     dom = max(op_ms, key=op_ms.get)
     achieved = BYTES_PER_ELT[dom] * elems / (op_ms[dom] / 1e3) / 1e9
@@ -362,6 +423,7 @@ def run_ours(args):
                                 for k, v in op_ms.items()},
             "e2e": e2e, "gpu_launches": launches, "clocks": clocks, "result_finite": ok,
             "conv": conv,
+            "vae_decoder": vae_line,
         }
         if not args.skip_cpu:
             line["cpu_baseline"] = cpu_baseline()
@@ -426,6 +488,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-conv", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-vae", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: [1,256,256,512] sweep (128 MiB, above L2) and a [1,128,128,512] conv")
     args = ap.parse_args()

@@ -193,6 +193,25 @@ int32_t mbx_matmul(mbx_ctx *ctx, float *c, const float *a, int64_t m, int64_t k,
                    int64_t a_col_stride, const float *b, int64_t n, int64_t b_row_stride, int64_t b_col_stride,
                    int32_t accumulate);
 
+/* ---------------------------------------------------------------- attention and scaling */
+
+/* In place, for each of `rows` rows of n floats: softmax(scale * row), with
+ * probabilities below e^flush set to zero (pass -INFINITY to keep all).
+ * Reference: softmax_rows, src/vae/mod.rs:273-293 (flush = -40). */
+int32_t mbx_softmax_rows(mbx_ctx *ctx, float *x, int64_t rows, int64_t n, float scale, float flush);
+
+/* c[m x n] = a[m x k] . B^T (+ bias[n]) (+ residual[m x n]) on the tensor cores
+ * (3xTF32, f32 accumulation), with B a device matrix stored [n x k] row-major
+ * (b_is_kn = 0) or [k x n] row-major (b_is_kn = 1). c must not alias a or b.
+ * Reference: gemm::matmul with a transposed or row-major B view
+ * (src/engine/gemm.rs:25-63), as used by the attention (src/vae/mod.rs:259-262). */
+int32_t mbx_gemm(mbx_ctx *ctx, float *c, const float *a, int64_t m, int64_t k, const float *b, int64_t n,
+                 int32_t b_is_kn, const float *bias, const float *residual);
+
+/* out = x * mul + add over len floats (out may equal x). Reference: the decoder's
+ * latent unscale and (x + 1) / 2, src/vae/decoder.rs:81,97. */
+int32_t mbx_scale_add(mbx_ctx *ctx, const float *x, int64_t len, float mul, float add, float *out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -137,6 +137,16 @@ class DeviceTensor:
         """A view of caller-owned device memory (e.g. a torch tensor's data_ptr()); never freed here."""
         return cls(ctx, tuple(int(s) for s in shape), ptr=ptr)
 
+    def __del__(self):
+        # Owned blocks go back to the context's pool (stream-ordered, so safe while queued
+        # kernels still read them: only later work on the same stream can reuse the block).
+        try:
+            if self.ptr and self.owned and self.ctx.handle:
+                self.ctx.free(self.ptr)
+                self.ptr = 0
+        except Exception:
+            pass
+
     def numpy(self) -> np.ndarray:
         out = np.empty(self.shape, np.float32)
         if self.size:

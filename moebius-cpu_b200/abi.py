@@ -81,6 +81,9 @@ SIGNATURES = {
     "mbx_conv3x3": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _pi64, _i32, _vp, _vp, _i32, _vp,
                            _vp]),
     "mbx_matmul": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32]),
+    "mbx_softmax_rows": (_i32, [_vp, _vp, _i64, _i64, _f32, _f32]),
+    "mbx_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _vp]),
+    "mbx_scale_add": (_i32, [_vp, _vp, _i64, _f32, _f32, _vp]),
 }
 
 _lib = None

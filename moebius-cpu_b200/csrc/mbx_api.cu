@@ -612,6 +612,61 @@ int32_t mbx_conv3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t 
     });
 }
 
+int32_t mbx_softmax_rows(mbx_ctx* ctx, float* x, int64_t rows, int64_t n, float scale, float flush) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(rows >= 0 && n >= 0, "bad shape");
+        if (rows == 0 || n == 0) return;
+        require_ptr(x, "x");
+        use_device(ctx);
+        mbx::launch_softmax_rows(ctx, x, rows, n, scale, flush);
+    });
+}
+
+int32_t mbx_gemm(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, const float* b, int64_t n,
+                 int32_t b_is_kn, const float* bias, const float* residual) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(m >= 0 && n > 0 && k > 0, "bad shape");
+        MBX_REQUIRE(n <= (1 << 20) && k <= (1 << 20), "gemm: n or k too large");
+        if (m == 0) return;
+        require_ptr(c, "c");
+        require_ptr(a, "a");
+        require_ptr(b, "b");
+        MBX_REQUIRE(c != a && c != b, "gemm: c must alias neither a nor b");
+        use_device(ctx);
+        // B becomes a transient tensor-core operand: TF32 hi/lo, K-major, zero padded.
+        mbx_param p;
+        p.dtype = MBX_DTYPE_F32;
+        p.c_out = n;
+        p.taps = 1;
+        p.c_in = k;
+        p.cin_pad = int((k + 31) / 32 * 32);
+        p.bn = mbx::choose_bn(n);
+        p.cout_pad = int((n + p.bn - 1) / p.bn * p.bn);
+        const size_t elems = size_t(p.cout_pad) * p.cin_pad;
+        mbx::PoolBuf hi(ctx, elems * 4), lo(ctx, elems * 4);
+        p.hi = hi.as<float>();
+        p.lo = lo.as<float>();
+        mbx::launch_split_to_param(ctx, b, n, k, b_is_kn != 0, &p);
+        mbx::encode_param_tmaps(&p);
+        mbx::ConvShape s{1, m, 1, k, m, 1, 1, 0, 0, 0};
+        mbx::launch_conv_tc(ctx, a, s, &p, bias, nullptr, nullptr, false, residual, c);
+    });
+}
+
+int32_t mbx_scale_add(mbx_ctx* ctx, const float* x, int64_t len, float mul, float add, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(len >= 0, "negative length");
+        if (len == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::launch_scale_add(ctx, x, len, mul, add, out);
+    });
+}
+
 int32_t mbx_matmul(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, int64_t a_row_stride,
                    int64_t a_col_stride, const float* b, int64_t n, int64_t b_row_stride, int64_t b_col_stride,
                    int32_t accumulate) {

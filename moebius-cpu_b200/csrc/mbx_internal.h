@@ -128,6 +128,10 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
 void encode_param_tmaps(mbx_param* p);
 int choose_bn(int64_t c_out);
 
+void launch_softmax_rows(mbx_ctx* ctx, float* x, int64_t rows, int64_t n, float scale, float flush);
+void launch_split_to_param(mbx_ctx* ctx, const float* b, int64_t n, int64_t k, bool b_is_kn, mbx_param* p);
+void launch_scale_add(mbx_ctx* ctx, const float* x, int64_t len, float mul, float add, float* out);
+
 void launch_matmul_simt(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, int64_t a_rs, int64_t a_cs,
                         const float* b, int64_t n, int64_t b_rs, int64_t b_cs, bool accumulate);
 

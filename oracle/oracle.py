@@ -59,6 +59,8 @@ def lib():
         _lib.ora_conv3x3.argtypes = conv_args
         _lib.ora_conv3x3_im2col.argtypes = conv_args
         _lib.ora_matmul.argtypes = [_f, _f, _i64, _i64, _i64, _i64, _f, _i64, _i64, _i64, _ci]
+        _lib.ora_gemm_nt.argtypes = [_i64, _i64, _i64, _f, _f, _f, _ci]
+        _lib.ora_softmax_rows.argtypes = [_f, _i64, _i64, ctypes.c_float]
     return _lib
 
 
@@ -213,3 +215,20 @@ def matmul(a, b, c=None):
     lib().ora_matmul(_p(out), _p(a), _i64(m), _i64(k), _i64(k), _i64(1), _p(b), _i64(n), _i64(n), _i64(1),
                      ctypes.c_int(int(acc)))
     return out
+
+
+def gemm_nt(a, b):
+    """a [m, k] @ b[n, k]^T (the engine GEMM with a transposed weight view)."""
+    a, b = _c(a), _c(b)
+    m, k = a.shape
+    n = b.shape[0]
+    out = np.empty((m, n), np.float32)
+    lib().ora_gemm_nt(m, n, k, _p(a), _p(b), _p(out), 0)
+    return out
+
+
+def softmax_rows(x, scale):
+    """softmax_rows (src/vae/mod.rs:279-293) on a copy of the 2-D array x."""
+    y = _c(x).copy()
+    lib().ora_softmax_rows(_p(y), y.shape[0], y.shape[1], scale)
+    return y

@@ -510,6 +510,31 @@ void ora_conv3x3(const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in, 
                            pro_silu, out);
 }
 
+// C[m×n] (+)= A[m×k]·Bᵀ with B stored [n×k] (the blocked GEMM above, exposed
+// for the attention contractions of src/vae/mod.rs:259-262).
+void ora_gemm_nt(int64_t m, int64_t n, int64_t k, const float* a, const float* b, float* c, int accumulate) {
+    gemm_nt(m, n, k, a, k, b, k, c, n, accumulate != 0);
+}
+
+// softmax_rows, reference src/vae/mod.rs:273-293: in place per n-long row,
+// a = (v − max)·scale, e = a < −40 ? 0 : exp(a), then v = e · (1 / Σe).
+void ora_softmax_rows(float* x, int64_t rows, int64_t n, float scale) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        float* row = x + r * n;
+        float mx = -INFINITY;
+        for (int64_t i = 0; i < n; ++i) mx = std::max(mx, row[i]);
+        float sum = 0.0f;
+        for (int64_t i = 0; i < n; ++i) {
+            const float a = (row[i] - mx) * scale;
+            row[i] = a < -40.0f ? 0.0f : ref_exp(a);
+            sum += row[i];
+        }
+        const float inv = 1.0f / sum;
+        for (int64_t i = 0; i < n; ++i) row[i] *= inv;
+    }
+}
+
 // gemm::matmul with arbitrary strides, reference src/engine/gemm.rs:63-132
 // (MatRef :25-53). c is dense row-major [m × n]. Small cases only.
 void ora_matmul(float* c, const float* a, int64_t m, int64_t k, int64_t a_rs, int64_t a_cs, const float* b, int64_t n,
