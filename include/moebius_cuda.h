@@ -1,5 +1,5 @@
 /* moebius-cuda C API: the moebius-cpu engine kernel layer (the Rust crate's
- * src/engine/*) re-implemented for NVIDIA B200 (sm_100a).
+ * src/engine/ modules) re-implemented for NVIDIA B200 (sm_100a).
  *
  * Conventions (those of the reference's C ABI, src/ffi.rs:1-103):
  *  - every entry point returns an int32 status (MBX_OK = 0); on failure the
@@ -53,6 +53,10 @@ extern "C" {
 #define MBX_EPILOGUE_NONE     0
 #define MBX_EPILOGUE_RELU     1
 #define MBX_EPILOGUE_GLU_SILU 2 /* output has c/2 channels: y[:c/2] * SiLU(y[c/2:]) */
+
+/* Activation applied by a 1x1 conv's epilogue after bias and residual. */
+#define MBX_ACT_NONE 0
+#define MBX_ACT_SILU 1
 
 typedef struct mbx_ctx mbx_ctx;
 typedef struct mbx_param mbx_param;
@@ -167,6 +171,17 @@ int32_t mbx_depthwise3x3(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int
 int32_t mbx_conv1x1(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c_in,
                     const mbx_param *weight, const float *bias, const float *residual, float *out);
 
+/* mbx_conv1x1 with two fusions (no single reference counterpart): an optional
+ * GroupNorm prologue, the input read as [SiLU](x*pro_scale[item,c] +
+ * pro_shift[item,c]) (pro_scale/pro_shift [n, c_in] or NULL; reference:
+ * GroupNorm::forward feeding the conv, src/unet/transformer.rs:324-325), and an
+ * epilogue activation `act` (MBX_ACT_*) after bias and residual (reference:
+ * Conv1x1::forward then silu_inplace, src/unet/transformer.rs:351-352). */
+int32_t mbx_conv1x1_fused(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                          const mbx_param *weight, const float *bias, const float *pro_scale,
+                          const float *pro_shift, int32_t pro_silu, const float *residual, int32_t act,
+                          float *out);
+
 /* Output spatial size of mbx_conv3x3. Reference: Conv3x3::output_hw, src/engine/conv.rs:77-81. */
 int32_t mbx_conv3x3_output_hw(int64_t h, int64_t w, int64_t stride, const int64_t pad[4], int32_t upsample2x,
                               int64_t *ho, int64_t *wo);
@@ -211,6 +226,103 @@ int32_t mbx_gemm(mbx_ctx *ctx, float *c, const float *a, int64_t m, int64_t k, c
 /* out = x * mul + add over len floats (out may equal x). Reference: the decoder's
  * latent unscale and (x + 1) / 2, src/vae/decoder.rs:81,97. */
 int32_t mbx_scale_add(mbx_ctx *ctx, const float *x, int64_t len, float mul, float add, float *out);
+
+/* ---------------------------------------------------------------- lambda layers (UNet) */
+
+/* Content lambda of `items` independent row sets: for each item,
+ * lambda[kk][j] = sum_r e[r][kk] * values[r][j] / sum_r e[r][kk] with
+ * e = exp(keys - column max over r), a softmax over rows per key channel.
+ * keys: rows x k with row stride key_stride floats; values: rows x vd with row
+ * stride value_stride; item i starts at i * rows * stride. out: [items][k][vd].
+ * Reference: softmax_lambda, src/unet/lambda.rs:318-359 (chunk sums folded in f64). */
+int32_t mbx_lambda_content(mbx_ctx *ctx, const float *keys, int64_t key_stride, const float *values,
+                           int64_t value_stride, int64_t items, int64_t rows, int64_t k, int64_t vd,
+                           float *lambda_out);
+
+/* Self-lambda output added into `out` [n, h, w, 8k] (8 heads of k channels):
+ * out[p, hd*k + v] += sum_kk q[p, hd*k + kk] * lambda[item][kk][v]
+ *                     + a[p*8 + hd][225] + sum_{d < 225} a[p*8 + hd][d] * V[p + d, v]
+ * where d = ky*15 + kx walks the 15x15 window centred on p (zero outside the
+ * map) and V[p, v] = v_ptr[p * v_stride + v]. q [n, h, w, 8k]; lambda
+ * [n][k][k] (from mbx_lambda_content); a [n*h*w*8][a_stride], a_stride >= 228
+ * and a multiple of 4, holding Q . [W | b] (225 taps, then the bias column).
+ * k must be a multiple of 8; q, a, v, out 16-byte aligned, v_stride a
+ * multiple of 4. Reference: SelfLambda::forward + tap_filter,
+ * src/unet/lambda.rs:107-184. */
+int32_t mbx_self_lambda_position(mbx_ctx *ctx, const float *q, const float *lambda_c, const float *a,
+                                 int64_t a_stride, const float *v, int64_t v_stride, int64_t n, int64_t h,
+                                 int64_t w, int64_t k, float *out);
+
+/* Cross-lambda output added into `out` [n, hw, 8k]: for item i with branch
+ * b = i % branch_period,
+ * out[p, hd*k + v] += sum_kk q[p, hd*k + kk] * lambda_c[b][kk][v]
+ *                     + sum_m (sum_kk q[p, hd*k + kk] * e_table[p][m][kk]) * v_table[b][m][v]
+ * over the m = 10 conditioning tokens; e_table [hw][10][k] (shared by all
+ * items), lambda_c [branches][k][k], v_table [branches][10][k]. k a multiple of
+ * 8, pointers 16-byte aligned. Reference: CrossLambda::forward + position_term,
+ * src/unet/lambda.rs:252-294. */
+int32_t mbx_cross_lambda_position(mbx_ctx *ctx, const float *q, const float *e_table, const float *lambda_c,
+                                  const float *v_table, int64_t branch_period, int64_t n, int64_t hw, int64_t k,
+                                  float *out);
+
+/* ---------------------------------------------------------------- inpaint pipeline */
+
+/* n square model-size inputs used whole (8-bit RGB or RGBA, `channels` 3|4,
+ * tightly packed [n, h, w, channels]; masks [n, h, w], >= 128 = inpaint) ->
+ * encoder batch images_out [2n, h, w, 3] = (rgb_0, masked_0, rgb_1, ...) in
+ * [-1, 1], binary masks bin_out [n, h, w] (0 / 255), latent masks
+ * mask_lat [n, h/8, w/8] (0 / 1, pixel (8y, 8x)) and, unless NULL,
+ * nonempty_out [n] (1 where the mask has a pixel >= 128). h and w multiples
+ * of 8. Reference: to_model (src/imaging/resize.rs:32-57, a same-size window
+ * is a copy), src/pipeline.rs:202-204,236-252. */
+int32_t mbx_inpaint_prepare(mbx_ctx *ctx, const uint8_t *image, const uint8_t *mask, int64_t n, int64_t h,
+                            int64_t w, int64_t channels, float *images_out, uint8_t *bin_out, float *mask_lat,
+                            int32_t *nonempty_out);
+
+/* Posterior sample: z[p, c] = (mean + exp(0.5 * clamp(logvar, -30, 20)) * noise[p, c]) * scale
+ * with moments [pixels][8] = mean(4) | logvar(4); z, noise [pixels][4].
+ * Reference: encoder sample, src/vae/encoder.rs:219-230. */
+int32_t mbx_vae_sample(mbx_ctx *ctx, const float *moments, const float *noise, int64_t pixels, float scale,
+                       float *z);
+
+/* Starting latents of n inpaints: init = noise_init + noise_offset_scale * noise_offset[i][c];
+ * x = init when pure_noise, else sqrt_alpha * z_pairs[2i] + sqrt_one_minus_alpha * init.
+ * z_pairs [2n, hw, 4] (encoder output: image latent, masked latent per inpaint);
+ * noise_init, x [n, hw, 4]; noise_offset [n][4].
+ * Reference: src/pipeline.rs:295-311, Ddim::add_noise src/scheduler.rs:78-85. */
+int32_t mbx_latents_init(mbx_ctx *ctx, const float *z_pairs, const float *noise_init, const float *noise_offset,
+                         int64_t n, int64_t hw, float noise_offset_scale, float sqrt_alpha,
+                         float sqrt_one_minus_alpha, int32_t pure_noise, float *x);
+
+/* UNet input [n * copies, hw, 9]: per pixel x(4) | mask_lat(1) | masked latent(4)
+ * (z_pairs[2i + 1]), written `copies` times per inpaint (2 = CFG uncond/cond).
+ * Reference: src/pipeline.rs:318-322 and the CFG tiling in UNet::forward,
+ * src/unet/mod.rs:226-231. */
+int32_t mbx_unet_input(mbx_ctx *ctx, const float *x, const float *mask_lat, const float *z_pairs, int64_t n,
+                       int64_t hw, int64_t copies, float *out);
+
+/* Guidance combine and one eta = 0 DDIM update of x [n, hw, 4] in place:
+ * e = copies == 2 ? eps_u + guidance * (eps_c - eps_u) : eps; x0 = (x - coef[0]*e) / coef[1];
+ * x = coef[2]*x0 + coef[3]*e with coef = {sqrt(1-a_t), sqrt(a_t), sqrt(a_prev), sqrt(1-a_prev)}.
+ * eps [n * copies, hw, 4]. Reference: src/pipeline.rs:323-336, Ddim::step src/scheduler.rs:87-97. */
+int32_t mbx_cfg_ddim_step(mbx_ctx *ctx, const float *eps, int64_t n, int64_t hw, int64_t copies, float guidance,
+                          const float coef[4], float *x);
+
+/* Pillow GaussianBlur(radius) of n single-channel 8-bit images [n, h, w]
+ * (three fractional box passes per axis, rows first), byte-exact. `scratch`
+ * holds n*h*w bytes; out may equal in. Reference: pil_gaussian_blur,
+ * src/imaging/blend.rs:26-100. */
+int32_t mbx_gaussian_blur_u8(mbx_ctx *ctx, const uint8_t *in, int64_t n, int64_t h, int64_t w, float radius,
+                             uint8_t *scratch, uint8_t *out);
+
+/* Feathered paste of decoded images result [n, h, w, 3] (in [0, 1], truncated
+ * to 8 bits) into image [n, h, w, channels] in place through the blurred
+ * binary mask `blurred` [n, h, w]: out = res*m + (1 - m)*src in f64, m = blurred/255.
+ * Items whose nonempty[i] is 0 are left untouched (nonempty may be NULL).
+ * Reference: to_u8 and paste (Paste::Feather), src/imaging/blend.rs:20-23,174-215;
+ * an empty mask returns before any change, src/pipeline.rs:202-204. */
+int32_t mbx_feather_paste(mbx_ctx *ctx, const float *result, const uint8_t *blurred, uint8_t *image, int64_t n,
+                          int64_t h, int64_t w, int64_t channels, const int32_t *nonempty);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -109,12 +109,13 @@ class Context:
     def host_free(ptr: int) -> None:
         check(lib().mbx_host_free(ctypes.c_void_p(ptr)))
 
-    def empty(self, shape: Sequence[int]) -> "DeviceTensor":
-        return DeviceTensor(self, tuple(int(s) for s in shape))
+    def empty(self, shape: Sequence[int], dtype=np.float32) -> "DeviceTensor":
+        return DeviceTensor(self, tuple(int(s) for s in shape), dtype=dtype)
 
-    def upload(self, arr) -> "DeviceTensor":
-        a = np.ascontiguousarray(arr, dtype=np.float32)
-        t = DeviceTensor(self, a.shape)
+    def upload(self, arr, dtype=np.float32) -> "DeviceTensor":
+        """Copies a host array to a new device buffer (float32 unless `dtype` says otherwise)."""
+        a = np.ascontiguousarray(arr, dtype=dtype)
+        t = DeviceTensor(self, a.shape, dtype=a.dtype)
         if a.size:
             check(lib().mbx_memcpy_h2d(self.handle, ctypes.c_void_p(t.ptr), a.ctypes.data_as(ctypes.c_void_p),
                                        a.nbytes))
@@ -122,20 +123,21 @@ class Context:
 
 
 class DeviceTensor:
-    """A float32 device buffer from the context's pool, with an NHWC shape."""
+    """A device buffer from the context's pool, with a shape (float32 NHWC unless `dtype` says otherwise)."""
 
-    def __init__(self, ctx: Context, shape: tuple, ptr: Optional[int] = None):
+    def __init__(self, ctx: Context, shape: tuple, ptr: Optional[int] = None, dtype=np.float32):
         self.ctx = ctx
         self.shape = tuple(shape)
+        self.dtype = np.dtype(dtype)
         self.size = int(np.prod(self.shape)) if self.shape else 1
-        self.nbytes = 4 * self.size
+        self.nbytes = self.dtype.itemsize * self.size
         self.owned = ptr is None
         self.ptr = ctx.alloc(self.nbytes) if ptr is None else int(ptr)
 
     @classmethod
-    def wrap(cls, ctx: Context, ptr: int, shape: Sequence[int]) -> "DeviceTensor":
+    def wrap(cls, ctx: Context, ptr: int, shape: Sequence[int], dtype=np.float32) -> "DeviceTensor":
         """A view of caller-owned device memory (e.g. a torch tensor's data_ptr()); never freed here."""
-        return cls(ctx, tuple(int(s) for s in shape), ptr=ptr)
+        return cls(ctx, tuple(int(s) for s in shape), ptr=ptr, dtype=dtype)
 
     def __del__(self):
         # Owned blocks go back to the context's pool (stream-ordered, so safe while queued
@@ -148,7 +150,7 @@ class DeviceTensor:
             pass
 
     def numpy(self) -> np.ndarray:
-        out = np.empty(self.shape, np.float32)
+        out = np.empty(self.shape, self.dtype)
         if self.size:
             check(lib().mbx_memcpy_d2h(self.ctx.handle, out.ctypes.data_as(ctypes.c_void_p),
                                        ctypes.c_void_p(self.ptr), self.nbytes))
@@ -319,3 +321,6 @@ def matmul(a: DeviceTensor, b: DeviceTensor, c: Optional[DeviceTensor] = None,
     c = c or a.ctx.empty((m, n))
     check(lib().mbx_matmul(a.ctx.handle, c.vp, a.vp, m, k, k, 1, b.vp, n, n, 1, int(accumulate)))
     return c
+
+
+from . import engine, synthetic  # noqa: E402  (engine API; seeded converter-format weights)

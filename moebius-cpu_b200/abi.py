@@ -13,6 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "lib", "libmoebius_cuda.so")
 HEADER = os.path.join(REPO, "include", "moebius_cuda.h")
+ENGINE_HEADER = os.path.join(REPO, "include", "moebius_cuda_engine.h")
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
@@ -32,6 +33,9 @@ EPILOGUE_NONE = 0
 EPILOGUE_RELU = 1
 EPILOGUE_GLU_SILU = 2
 
+ACT_NONE = 0
+ACT_SILU = 1
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -42,6 +46,30 @@ _pvp = ctypes.POINTER(ctypes.c_void_p)
 _pi64 = ctypes.POINTER(ctypes.c_int64)
 _psz = ctypes.POINTER(ctypes.c_size_t)
 _pi32 = ctypes.POINTER(ctypes.c_int32)
+_pf32 = ctypes.POINTER(ctypes.c_float)
+_u32 = ctypes.c_uint32
+_f64 = ctypes.c_double
+
+PRESET_EXACT = 0
+PRESET_FAST = 1
+PASTE_DEFAULT = 0
+PASTE_NONE = 1
+PASTE_FEATHER = 2
+PASTE_FEATHER_COMPENSATE = 3
+
+
+class InpaintParams(ctypes.Structure):
+    """mbx_inpaint_params (the reference's MoebiusParams); zero = Exact defaults."""
+    _fields_ = [("preset", ctypes.c_uint32), ("steps", ctypes.c_uint32), ("guidance", ctypes.c_float),
+                ("seed", ctypes.c_uint64), ("paste", ctypes.c_uint32), ("mask_dilate", ctypes.c_uint32)]
+
+
+class Rect(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_uint32), ("y", ctypes.c_uint32), ("width", ctypes.c_uint32),
+                ("height", ctypes.c_uint32)]
+
+
+PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32)
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -84,6 +112,31 @@ SIGNATURES = {
     "mbx_softmax_rows": (_i32, [_vp, _vp, _i64, _i64, _f32, _f32]),
     "mbx_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _vp]),
     "mbx_scale_add": (_i32, [_vp, _vp, _i64, _f32, _f32, _vp]),
+    "mbx_conv1x1_fused": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp]),
+    "mbx_lambda_content": (_i32, [_vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mbx_self_lambda_position": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mbx_cross_lambda_position": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mbx_inpaint_prepare": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "mbx_vae_sample": (_i32, [_vp, _vp, _vp, _i64, _f32, _vp]),
+    "mbx_latents_init": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _f32, _f32, _i32, _vp]),
+    "mbx_unet_input": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "mbx_cfg_ddim_step": (_i32, [_vp, _vp, _i64, _i64, _i64, _f32, _pf32, _vp]),
+    "mbx_gaussian_blur_u8": (_i32, [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
+    "mbx_feather_paste": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    # include/moebius_cuda_engine.h
+    "mbx_engine_create": (_i32, [ctypes.c_char_p, _i32, _pvp]),
+    "mbx_engine_destroy": (None, [_vp]),
+    "mbx_engine_set_stream": (_i32, [_vp, _vp]),
+    "mbx_engine_info": (_i32, [_vp, _pi64, _pi64, _pi64]),
+    "mbx_inpaint": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, ctypes.POINTER(InpaintParams), PROGRESS_FN,
+                           _vp, ctypes.POINTER(Rect)]),
+    "mbx_inpaint_batch": (_i32, [_vp, _vp, _vp, _i64, _u32, _u32, ctypes.POINTER(InpaintParams), _vp, _vp, _vp,
+                                 _i32, PROGRESS_FN, _vp]),
+    "mbx_engine_unet_forward": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp]),
+    "mbx_engine_vae_encode": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "mbx_engine_vae_decode": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "mbx_ddim_timesteps": (_i32, [_u32, _f64, _i32, _pi64, _pi64]),
+    "mbx_ddim_alphas_cumprod": (_i32, [_pf32]),
 }
 
 _lib = None
@@ -96,9 +149,9 @@ class MbxError(RuntimeError):
 
 
 def header_symbols() -> list[str]:
-    """Function names declared in include/moebius_cuda.h."""
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"\b(mbx_[a-z0-9_]+)\s*\(", text)))
+    """Function names declared in include/moebius_cuda.h and include/moebius_cuda_engine.h."""
+    text = open(HEADER).read() + open(ENGINE_HEADER).read()
+    return sorted(set(re.findall(r"\b(mbx_[a-z0-9_]+)\s*\(", text)) - {"mbx_progress_fn"})
 
 
 def lib() -> ctypes.CDLL:

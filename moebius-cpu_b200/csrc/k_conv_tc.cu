@@ -72,6 +72,7 @@ struct ConvArgs {
     const float* pro_scale;
     const float* pro_shift;
     int pro_silu;
+    int act;  // epilogue activation after bias and residual: 0 none, 1 SiLU
     int* err;
 };
 
@@ -413,6 +414,11 @@ __global__ void __maxnreg__(128)
         int pb = 0, geo = 0;
         if constexpr (!FLAT) row_geo(r, pb, geo);
         const bool pro = args.pro_scale != nullptr;
+        if constexpr (FLAT) {
+            // 1×1: the row's item selects the prologue's per-item scale / shift.
+            const int64_t m = m0 + r;
+            pb = m < args.m_total ? (int)(m / hw_out) : 0;
+        }
         for (int kc = 0; kc < K; ++kc) {
             const int q = kc % kStgSlots, a = kc % astages;
             if (!mbar_wait(sfull_bar(q), (kc / kStgSlots) & 1, args.err, 9, abort_flag, true)) break;
@@ -562,9 +568,10 @@ __global__ void __maxnreg__(128)
                             const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
                             pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
                         }
-                        reinterpret_cast<float4*>(dst)[v] =
-                            make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
-                                        pre.w + acc[4 * v + 3]);
+                        float4 o4 = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1],
+                                                pre.z + acc[4 * v + 2], pre.w + acc[4 * v + 3]);
+                        if (args.act) o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                        reinterpret_cast<float4*>(dst)[v] = o4;
                     }
                 } else {
                     const int lim = min(32, args.c_out - nb);
@@ -573,7 +580,8 @@ __global__ void __maxnreg__(128)
                         if (i < lim) {
                             float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
                             if (res) pre = __ldg(res + i) + pre;
-                            dst[i] = pre + acc[i];
+                            const float o = pre + acc[i];
+                            dst[i] = args.act ? dev_silu(o) : o;
                         }
                     }
                 }
@@ -669,7 +677,7 @@ void encode_param_tmaps(mbx_param* p) {
 
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
-                    float* out) {
+                    float* out, int act) {
     ConvArgs a{};
     a.x = x;
     a.m_total = s.n * s.ho * s.wo;
@@ -698,6 +706,7 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.pro_scale = pro_scale;
     a.pro_shift = pro_shift;
     a.pro_silu = pro_silu ? 1 : 0;
+    a.act = act;
     a.err = ctx->dev_err;
     MBX_REQUIRE(a.m_total < (int64_t(1) << 40), "conv: too many output pixels");
     const int64_t m_tiles = (a.m_total + BM - 1) / BM;

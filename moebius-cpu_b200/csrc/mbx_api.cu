@@ -2,6 +2,7 @@
 // entry points. Argument checks mirror the reference engine's asserts; the
 // kernels themselves live in k_*.cu.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -150,22 +151,6 @@ void Pool::release_below(size_t min_bytes) {
 
 void record_error(int32_t code, const char* msg) { set_error(code, msg); }
 
-// Scoped pool allocation for per-call scratch (stream-ordered reuse).
-struct PoolBuf {
-    mbx_ctx* ctx;
-    void* p;
-    PoolBuf(mbx_ctx* c, size_t bytes) : ctx(c), p(c->pool->alloc(bytes)) {}
-    ~PoolBuf() {
-        try {
-            ctx->pool->free(p);
-        } catch (...) {
-        }
-    }
-    template <class T>
-    T* as() const {
-        return static_cast<T*>(p);
-    }
-};
 
 }  // namespace mbx
 
@@ -570,6 +555,28 @@ int32_t mbx_conv1x1(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t 
     });
 }
 
+int32_t mbx_conv1x1_fused(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                          const mbx_param* weight, const float* bias, const float* pro_scale,
+                          const float* pro_shift, int32_t pro_silu, const float* residual, int32_t act,
+                          float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(weight != nullptr, "null weight");
+        MBX_REQUIRE(weight->taps == 1, "Conv1x1 needs a 1x1 (taps = 1) weight");
+        MBX_REQUIRE(weight->c_in == c_in, "Conv1x1 input channels");
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0, "bad shape");
+        MBX_REQUIRE((pro_scale == nullptr) == (pro_shift == nullptr), "prologue needs both scale and shift");
+        MBX_REQUIRE(act == MBX_ACT_NONE || act == MBX_ACT_SILU, "unknown activation");
+        if (n * h * w == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        MBX_REQUIRE(out != x, "conv1x1: out must not alias x");
+        use_device(ctx);
+        mbx::ConvShape s{n, h, w, c_in, h, w, 1, 0, 0, 0};
+        mbx::launch_conv_tc(ctx, x, s, weight, bias, pro_scale, pro_shift, pro_silu != 0, residual, out, act);
+    });
+}
+
 int32_t mbx_conv3x3_output_hw(int64_t h, int64_t w, int64_t stride, const int64_t pad[4], int32_t upsample2x,
                               int64_t* ho, int64_t* wo) {
     return guard([&] {
@@ -664,6 +671,203 @@ int32_t mbx_scale_add(mbx_ctx* ctx, const float* x, int64_t len, float mul, floa
         require_ptr(out, "out");
         use_device(ctx);
         mbx::launch_scale_add(ctx, x, len, mul, add, out);
+    });
+}
+
+int32_t mbx_lambda_content(mbx_ctx* ctx, const float* keys, int64_t key_stride, const float* values,
+                           int64_t value_stride, int64_t items, int64_t rows, int64_t k, int64_t vd,
+                           float* lambda_out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(items >= 0 && rows >= 1 && k >= 1 && vd >= 1, "bad shape");
+        MBX_REQUIRE(key_stride >= k && value_stride >= vd, "row strides smaller than the widths");
+        if (items == 0) return;
+        require_ptr(keys, "keys");
+        require_ptr(values, "values");
+        require_ptr(lambda_out, "lambda_out");
+        use_device(ctx);
+        const int64_t chunks = mbx::lambda_chunks(rows);
+        mbx::PoolBuf pmax(ctx, size_t(items * chunks * k) * 4), psum(ctx, size_t(items * chunks * k) * 4);
+        mbx::PoolBuf plam(ctx, size_t(items * chunks * k * vd) * 4);
+        mbx::launch_lambda_content(ctx, keys, key_stride, values, value_stride, items, rows, k, vd,
+                                   pmax.as<float>(), plam.as<float>(), psum.as<float>(), lambda_out);
+    });
+}
+
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+}  // namespace
+
+int32_t mbx_self_lambda_position(mbx_ctx* ctx, const float* q, const float* lambda_c, const float* a,
+                                 int64_t a_stride, const float* v, int64_t v_stride, int64_t n, int64_t h,
+                                 int64_t w, int64_t k, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 1 && w >= 1, "bad shape");
+        MBX_REQUIRE(k >= 8 && k % 8 == 0, "self lambda: head width must be a positive multiple of 8");
+        MBX_REQUIRE(a_stride >= 228 && a_stride % 4 == 0, "self lambda: a_stride must be >= 228 and a multiple of 4");
+        MBX_REQUIRE(v_stride >= k && v_stride % 4 == 0, "self lambda: v_stride must be >= k and a multiple of 4");
+        MBX_REQUIRE(h < (1 << 20) && w < (1 << 20), "self lambda: map too large");
+        if (n == 0) return;
+        for (const void* p : {(const void*)q, (const void*)lambda_c, (const void*)a, (const void*)v, (const void*)out})
+            require_ptr(p, "operand");
+        MBX_REQUIRE(aligned16(q) && aligned16(a) && aligned16(v) && aligned16(out),
+                    "self lambda: q, a, v and out must be 16-byte aligned");
+        MBX_REQUIRE(out != q && out != a, "self lambda: out must alias neither q nor a");
+        use_device(ctx);
+        mbx::launch_self_position(ctx, q, lambda_c, a, a_stride, v, v_stride, n, h, w, k, out);
+    });
+}
+
+int32_t mbx_cross_lambda_position(mbx_ctx* ctx, const float* q, const float* e_table, const float* lambda_c,
+                                  const float* v_table, int64_t branch_period, int64_t n, int64_t hw, int64_t k,
+                                  float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 1, "bad shape");
+        MBX_REQUIRE(k >= 8 && k % 8 == 0, "cross lambda: head width must be a positive multiple of 8");
+        MBX_REQUIRE(branch_period >= 1 && branch_period <= 1024, "cross lambda: bad branch period");
+        if (n == 0) return;
+        for (const void* p : {(const void*)q, (const void*)e_table, (const void*)lambda_c, (const void*)v_table,
+                              (const void*)out})
+            require_ptr(p, "operand");
+        MBX_REQUIRE(aligned16(q) && aligned16(e_table) && aligned16(out),
+                    "cross lambda: q, e_table and out must be 16-byte aligned");
+        MBX_REQUIRE(out != q, "cross lambda: out must not alias q");
+        use_device(ctx);
+        mbx::launch_cross_position(ctx, q, e_table, lambda_c, v_table, branch_period, n, hw, k, out);
+    });
+}
+
+int32_t mbx_inpaint_prepare(mbx_ctx* ctx, const uint8_t* image, const uint8_t* mask, int64_t n, int64_t h,
+                            int64_t w, int64_t channels, float* images_out, uint8_t* bin_out, float* mask_lat,
+                            int32_t* nonempty_out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 8 && w >= 8 && h % 8 == 0 && w % 8 == 0,
+                    "inpaint: image sides must be positive multiples of 8");
+        MBX_REQUIRE(channels == 3 || channels == 4, "image must be RGB or RGBA");
+        if (n == 0) return;
+        for (const void* p : {(const void*)image, (const void*)mask, (const void*)images_out, (const void*)bin_out,
+                              (const void*)mask_lat})
+            require_ptr(p, "operand");
+        use_device(ctx);
+        mbx::launch_inpaint_prepare(ctx, image, mask, n, h, w, (int)channels, images_out, bin_out, mask_lat,
+                                    nonempty_out);
+    });
+}
+
+int32_t mbx_vae_sample(mbx_ctx* ctx, const float* moments, const float* noise, int64_t pixels, float scale,
+                       float* z) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(pixels >= 0, "bad shape");
+        if (pixels == 0) return;
+        require_ptr(moments, "moments");
+        require_ptr(noise, "noise");
+        require_ptr(z, "z");
+        use_device(ctx);
+        mbx::launch_vae_sample(ctx, moments, noise, pixels, scale, z);
+    });
+}
+
+int32_t mbx_latents_init(mbx_ctx* ctx, const float* z_pairs, const float* noise_init, const float* noise_offset,
+                         int64_t n, int64_t hw, float noise_offset_scale, float sqrt_alpha,
+                         float sqrt_one_minus_alpha, int32_t pure_noise, float* x) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0, "bad shape");
+        if (n * hw == 0) return;
+        MBX_REQUIRE(pure_noise || z_pairs != nullptr, "null pointer: z_pairs");
+        require_ptr(noise_init, "noise_init");
+        require_ptr(noise_offset, "noise_offset");
+        require_ptr(x, "x");
+        use_device(ctx);
+        mbx::launch_latents_init(ctx, z_pairs, noise_init, noise_offset, n, hw, noise_offset_scale, sqrt_alpha,
+                                 sqrt_one_minus_alpha, pure_noise != 0, x);
+    });
+}
+
+int32_t mbx_unet_input(mbx_ctx* ctx, const float* x, const float* mask_lat, const float* z_pairs, int64_t n,
+                       int64_t hw, int64_t copies, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0, "bad shape");
+        MBX_REQUIRE(copies == 1 || copies == 2, "copies must be 1 or 2");
+        if (n * hw == 0) return;
+        for (const void* p : {(const void*)x, (const void*)mask_lat, (const void*)z_pairs, (const void*)out})
+            require_ptr(p, "operand");
+        use_device(ctx);
+        mbx::launch_unet_input(ctx, x, mask_lat, z_pairs, n, hw, (int)copies, out);
+    });
+}
+
+int32_t mbx_cfg_ddim_step(mbx_ctx* ctx, const float* eps, int64_t n, int64_t hw, int64_t copies, float guidance,
+                          const float coef[4], float* x) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0, "bad shape");
+        MBX_REQUIRE(copies == 1 || copies == 2, "copies must be 1 or 2");
+        require_ptr(coef, "coef");
+        if (n * hw == 0) return;
+        require_ptr(eps, "eps");
+        require_ptr(x, "x");
+        use_device(ctx);
+        mbx::launch_cfg_ddim(ctx, eps, n, hw * 4, (int)copies, guidance, coef, x);
+    });
+}
+
+namespace {
+// Pillow's _gaussian_blur_radius in f32 with f64 sqrt / floor (src/imaging/blend.rs:26-39).
+float gaussian_box_radius(float sigma, uint32_t passes) {
+    const float sigma2 = sigma * sigma / (float)passes;
+    const float big_l = (float)std::sqrt(12.0 * (double)sigma2 + 1.0);
+    const float l = (float)std::floor(((double)big_l - 1.0) / 2.0);
+    float a = (2.0f * l + 1.0f) * (l * (l + 1.0f) - 3.0f * sigma2);
+    a /= 6.0f * (sigma2 - (l + 1.0f) * (l + 1.0f));
+    return l + a;
+}
+}  // namespace
+
+int32_t mbx_gaussian_blur_u8(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t h, int64_t w, float radius,
+                             uint8_t* scratch, uint8_t* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0, "bad shape");
+        MBX_REQUIRE(h <= 16384 && w <= 16384, "blur: sides above 16384");
+        if (n * h * w == 0) return;
+        require_ptr(in, "in");
+        require_ptr(out, "out");
+        use_device(ctx);
+        if (!(radius > 0.0f)) {
+            if (out != in)
+                check_cuda(cudaMemcpyAsync(out, in, size_t(n * h * w), cudaMemcpyDeviceToDevice, ctx->stream),
+                           "blur copy");
+            return;
+        }
+        require_ptr(scratch, "scratch");
+        const uint32_t passes = 3;
+        const float fr = gaussian_box_radius(radius, passes);
+        const int rad = (int)fr;
+        const uint32_t ww = (uint32_t)((float)(1u << 24) / (fr * 2.0f + 1.0f));
+        const uint32_t fw = ((1u << 24) - (uint32_t)(rad * 2 + 1) * ww) / 2;
+        mbx::launch_blur_lines(ctx, in, scratch, n * h, h, h * w, w, 1, (int)w, rad, ww, fw, (int)passes);
+        mbx::launch_blur_lines(ctx, scratch, out, n * w, w, h * w, 1, w, (int)h, rad, ww, fw, (int)passes);
+    });
+}
+
+int32_t mbx_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blurred, uint8_t* image, int64_t n,
+                          int64_t h, int64_t w, int64_t channels, const int32_t* nonempty) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0, "bad shape");
+        MBX_REQUIRE(channels == 3 || channels == 4, "image must be RGB or RGBA");
+        if (n * h * w == 0) return;
+        require_ptr(result, "result");
+        require_ptr(blurred, "blurred");
+        require_ptr(image, "image");
+        use_device(ctx);
+        mbx::launch_feather_paste(ctx, result, blurred, image, n * h * w, h * w, (int)channels, nonempty);
     });
 }
 

@@ -123,7 +123,7 @@ struct ConvShape {
 };
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
-                    float* out);
+                    float* out, int act = 0);
 // Tensor maps for a param's hi / lo arrays (TMA, 128-byte swizzle).
 void encode_param_tmaps(mbx_param* p);
 int choose_bn(int64_t c_out);
@@ -132,8 +132,53 @@ void launch_softmax_rows(mbx_ctx* ctx, float* x, int64_t rows, int64_t n, float 
 void launch_split_to_param(mbx_ctx* ctx, const float* b, int64_t n, int64_t k, bool b_is_kn, mbx_param* p);
 void launch_scale_add(mbx_ctx* ctx, const float* x, int64_t len, float mul, float add, float* out);
 
+// λ layers (k_lambda.cu). lambda_content needs scratch: pmax and psum
+// [items][chunks][k], plam [items][chunks][k][vd] with chunks = lambda_chunks(rows).
+int64_t lambda_chunks(int64_t rows);
+void launch_lambda_content(mbx_ctx* ctx, const float* keys, int64_t ks, const float* vals, int64_t vs,
+                           int64_t items, int64_t rows, int64_t k, int64_t vd, float* pmax, float* plam,
+                           float* psum, float* lam);
+void launch_self_position(mbx_ctx* ctx, const float* q, const float* lam, const float* a, int64_t a_stride,
+                          const float* v, int64_t v_stride, int64_t n, int64_t h, int64_t w, int64_t k, float* out);
+void launch_cross_position(mbx_ctx* ctx, const float* q, const float* e_table, const float* lam, const float* vtab,
+                           int64_t period, int64_t n, int64_t hw, int64_t k, float* out);
+
+// Pipeline element work (k_pipeline.cu).
+void launch_inpaint_prepare(mbx_ctx* ctx, const uint8_t* img, const uint8_t* mask, int64_t n, int64_t h, int64_t w,
+                            int ch, float* images, uint8_t* bin, float* mask_lat, int32_t* nonempty);
+void launch_vae_sample(mbx_ctx* ctx, const float* moments, const float* noise, int64_t pixels, float scale,
+                       float* z);
+void launch_latents_init(mbx_ctx* ctx, const float* z_pairs, const float* noise_init, const float* noise_offset,
+                         int64_t n, int64_t hw, float offset_scale, float sa, float sb, bool pure, float* x);
+void launch_unet_input(mbx_ctx* ctx, const float* x, const float* mask_lat, const float* z_pairs, int64_t n,
+                       int64_t hw, int copies, float* out);
+void launch_cfg_ddim(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int copies, float guidance,
+                     const float coef[4], float* x);
+void launch_blur_lines(mbx_ctx* ctx, const uint8_t* in, uint8_t* out, int64_t lines, int64_t lines_per_item,
+                       int64_t item_stride, int64_t line_stride, int64_t elem_stride, int len, int radius,
+                       uint32_t ww, uint32_t fw, int passes);
+void launch_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blurred, uint8_t* image, int64_t pixels,
+                          int64_t item_pixels, int ch, const int32_t* nonempty);
+
 void launch_matmul_simt(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, int64_t a_rs, int64_t a_cs,
                         const float* b, int64_t n, int64_t b_rs, int64_t b_cs, bool accumulate);
+
+// Scoped pool allocation for per-call scratch (stream-ordered reuse).
+struct PoolBuf {
+    mbx_ctx* ctx;
+    void* p;
+    PoolBuf(mbx_ctx* c, size_t bytes) : ctx(c), p(c->pool->alloc(bytes)) {}
+    ~PoolBuf() {
+        try {
+            ctx->pool->free(p);
+        } catch (...) {
+        }
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(p);
+    }
+};
 
 // Launch-configuration helpers.
 inline int grid_for(mbx_ctx* ctx, int64_t work_items, int per_block, int max_waves = 8) {

@@ -61,6 +61,11 @@ def lib():
         _lib.ora_matmul.argtypes = [_f, _f, _i64, _i64, _i64, _i64, _f, _i64, _i64, _i64, _ci]
         _lib.ora_gemm_nt.argtypes = [_i64, _i64, _i64, _f, _f, _f, _ci]
         _lib.ora_softmax_rows.argtypes = [_f, _i64, _i64, ctypes.c_float]
+        _lib.ora_softmax_lambda.argtypes = [_f, _f, _i64, _i64, _i64, _f]
+        _lib.ora_tap_filter.argtypes = [_f, _f, _f, _i64, _i64, _i64]
+        _lib.ora_position_term.argtypes = [_f, _f, _f, _f, _i64, _i64]
+        _lib.ora_timestep_sinusoid.argtypes = [_i64, _i64, _f]
+        _lib.ora_vae_sample.argtypes = [_f, _f, _i64, _f]
     return _lib
 
 
@@ -232,3 +237,45 @@ def softmax_rows(x, scale):
     y = _c(x).copy()
     lib().ora_softmax_rows(_p(y), y.shape[0], y.shape[1], scale)
     return y
+
+
+def softmax_lambda(keys, v):
+    """softmax_lambda (src/unet/lambda.rs:318-359): keys [rows, k], v [rows, vd] -> [k, vd]."""
+    keys = _c(keys).copy()
+    v = _c(v)
+    rows, k = keys.shape
+    vd = v.shape[1]
+    lam = np.empty((k, vd), np.float32)
+    lib().ora_softmax_lambda(_p(keys), _p(v), rows, k, vd, _p(lam))
+    return lam
+
+
+def tap_filter(a, v, o, hh, ww):
+    """tap_filter (src/unet/lambda.rs:154-184) into o [hw, 8·vd] in place; a [hw·8, 226], v [hw, vd]."""
+    a, v = _c(a), _c(v)
+    assert o.dtype == np.float32 and o.flags["C_CONTIGUOUS"]
+    lib().ora_tap_filter(_p(a), _p(v), _p(o), hh, ww, v.shape[-1])
+    return o
+
+
+def position_term(q, e, v, o):
+    """position_term (src/unet/lambda.rs:276-295) into o [hw, 8k] in place."""
+    q, e, v = _c(q), _c(e), _c(v)
+    assert o.dtype == np.float32 and o.flags["C_CONTIGUOUS"]
+    k = v.shape[-1]
+    lib().ora_position_term(_p(q), _p(e), _p(v), _p(o), q.size // (8 * k), k)
+    return o
+
+
+def timestep_sinusoid(t, dim):
+    out = np.empty(dim, np.float32)
+    lib().ora_timestep_sinusoid(int(t), dim, _p(out))
+    return out
+
+
+def vae_sample(moments, noise):
+    """sample (src/vae/encoder.rs:219-230): moments [..., 8], noise [..., 4] -> z [..., 4]."""
+    moments, noise = _c(moments), _c(noise)
+    z = np.empty_like(noise)
+    lib().ora_vae_sample(_p(moments), _p(noise), noise.size // 4, _p(z))
+    return z

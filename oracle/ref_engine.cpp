@@ -548,4 +548,123 @@ void ora_matmul(float* c, const float* a, int64_t m, int64_t k, int64_t a_rs, in
         }
 }
 
+// ---------------------------------------------------------------- lambda.rs
+// softmax_lambda, reference src/unet/lambda.rs:318-359 (column_max :361-369,
+// exp_and_sum :371-380): keys [rows × k] is overwritten with exp(key − colmax);
+// per-column sums in f32 over 256-row chunks folded in f64; λ = keysᵀ·v with
+// f32 FMA accumulation, each row scaled by (float)(1 / sum).
+void ora_softmax_lambda(float* keys, const float* v, int64_t rows, int64_t k, int64_t vd, float* lam) {
+    std::vector<float> mx(size_t(k), -INFINITY);
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t kk = 0; kk < k; ++kk) mx[size_t(kk)] = std::max(mx[size_t(kk)], keys[r * k + kk]);
+    std::vector<double> sum(size_t(k), 0.0);
+    for (int64_t r0 = 0; r0 < rows; r0 += 256) {
+        std::vector<float> s(size_t(k), 0.0f);
+        for (int64_t r = r0; r < std::min<int64_t>(rows, r0 + 256); ++r)
+            for (int64_t kk = 0; kk < k; ++kk) {
+                float& e = keys[r * k + kk];
+                e = ref_exp(e - mx[size_t(kk)]);
+                s[size_t(kk)] += e;
+            }
+        for (int64_t kk = 0; kk < k; ++kk) sum[size_t(kk)] += (double)s[size_t(kk)];
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t kk = 0; kk < k; ++kk) {
+        const float inv = (float)(1.0 / sum[size_t(kk)]);
+        for (int64_t j = 0; j < vd; ++j) {
+            float acc = 0.0f;
+            for (int64_t r = 0; r < rows; ++r) acc = fmaf(keys[r * k + kk], v[r * vd + j], acc);
+            lam[kk * vd + j] = acc * inv;
+        }
+    }
+}
+
+// tap_filter, reference src/unet/lambda.rs:154-184: for every pixel of one item and
+// head, o[h] += A[p,h,225], then o[h] = fma(A[p,h,d], V[p+d], o[h]) over the in-map
+// taps d = ky·15 + kx of the 15×15 window. a: [hw × 8 × 226]; v: [hw × vd];
+// o: [hw × 8·vd].
+void ora_tap_filter(const float* a, const float* v, float* o, int64_t hh, int64_t ww, int64_t vd) {
+    const int64_t c = 8 * vd, hw = hh * ww;
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < hw; ++p) {
+        const int64_t y = p / ww, x = p % ww;
+        const float* ap = a + p * 8 * 226;
+        float* op = o + p * c;
+        for (int h = 0; h < 8; ++h) {
+            const float bias = ap[h * 226 + 225];
+            for (int64_t t = 0; t < vd; ++t) op[h * vd + t] += bias;
+        }
+        const int64_t kx0 = std::max<int64_t>(0, 7 - x), kx1 = std::min<int64_t>(15, ww + 7 - x);
+        for (int64_t ky = 0; ky < 15; ++ky) {
+            const int64_t iy = y + ky - 7;
+            if (iy < 0 || iy >= hh) continue;
+            for (int64_t kx = kx0; kx < kx1; ++kx) {
+                const float* vr = v + (iy * ww + x + kx - 7) * vd;
+                const int64_t d = ky * 15 + kx;
+                for (int h = 0; h < 8; ++h) {
+                    const float coef = ap[h * 226 + d];
+                    for (int64_t t = 0; t < vd; ++t) op[h * vd + t] = fmaf(coef, vr[t], op[h * vd + t]);
+                }
+            }
+        }
+    }
+}
+
+// dot with 8 independent lanes, then the lane sum and the tail (reference
+// src/unet/lambda.rs:297-309).
+static float lambda_dot(const float* a, const float* b, int64_t n) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int64_t body = n / 8 * 8;
+    float tail = 0.0f;
+    for (int64_t i = body; i < n; ++i) tail += a[i] * b[i];
+    for (int64_t i = 0; i < body; i += 8)
+        for (int l = 0; l < 8; ++l) acc[l] = fmaf(a[i + l], b[i + l], acc[l]);
+    float s = 0.0f;
+    for (int l = 0; l < 8; ++l) s += acc[l];
+    return s + tail;
+}
+
+// position_term, reference src/unet/lambda.rs:276-295: per pixel and head,
+// B[m] = Q_h · E[p, m], then o[h] = fma(B[m], V[m], o[h]) for the 10 tokens.
+// q, o: [hw × 8k]; e: [hw × 10 × k]; v: [10 × k].
+void ora_position_term(const float* q, const float* e, const float* v, float* o, int64_t hw, int64_t k) {
+    const int64_t c = 8 * k;
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < hw; ++p) {
+        const float* ep = e + p * 10 * k;
+        for (int h = 0; h < 8; ++h) {
+            const float* qh = q + p * c + h * k;
+            float* oh = o + p * c + h * k;
+            for (int m = 0; m < 10; ++m) {
+                const float b = lambda_dot(qh, ep + m * k, k);
+                for (int64_t t = 0; t < k; ++t) oh[t] = fmaf(b, v[m * k + t], oh[t]);
+            }
+        }
+    }
+}
+
+// timestep_sinusoid, reference src/unet/embed.rs:20-30: [cos | sin] of
+// t · exp(log_period · i / half) with log_period = −ln(10000) as f32.
+void ora_timestep_sinusoid(int64_t t, int64_t dim, float* out) {
+    const int64_t half = dim / 2;
+    const float log_period = -(float)std::log(10000.0);
+    for (int64_t i = 0; i < half; ++i) {
+        const float freq = std::exp(log_period * (float)i / (float)half);
+        const float arg = (float)t * freq;
+        out[i] = std::cos(arg);
+        out[half + i] = std::sin(arg);
+    }
+}
+
+// sample, reference src/vae/encoder.rs:219-230:
+// z = fma(exp(0.5·clamp(logvar, −30, 20)), noise, mean) · 0.13025 per pixel;
+// moments [pixels × 8] = mean(4) ‖ logvar(4).
+void ora_vae_sample(const float* moments, const float* noise, int64_t pixels, float* z) {
+    for (int64_t p = 0; p < pixels; ++p)
+        for (int c = 0; c < 4; ++c) {
+            const float lv = std::min(std::max(moments[p * 8 + 4 + c], -30.0f), 20.0f);
+            z[p * 4 + c] = fmaf(ref_exp(0.5f * lv), noise[p * 4 + c], moments[p * 8 + c]) * 0.13025f;
+        }
+}
+
 }  // extern "C"

@@ -1,8 +1,10 @@
-"""TEST INFRASTRUCTURE ONLY: the moebius-cpu VAE decoder composed from the
-oracle kernels (reference src/vae/decoder.rs:74-99, src/vae/mod.rs:174-293):
-the CPU counterpart of moebius-cpu_b200/vae.py, for parity tests and the CPU
-baseline. Stride-1 3×3 convs run the oracle's Winograd path, as the reference
+"""TEST INFRASTRUCTURE ONLY: the moebius-cpu VAE (encoder and decoder)
+composed from the oracle kernels (reference src/vae/encoder.rs:173-230,
+src/vae/decoder.rs:74-99, src/vae/mod.rs:174-293): the CPU counterpart of the
+library's VAE, for parity tests and the CPU baseline. Stride-1 3×3 convs run
+the oracle's Winograd path and stride-2 ones its im2col path, as the reference
 does; GroupNorm+SiLU is applied as the convs' prologue, as the reference does.
+Weights are a dict of numpy arrays in the converter's layout (f16 widened).
 """
 from __future__ import annotations
 
@@ -22,11 +24,11 @@ def _affine(w, name, x):
 
 
 def _conv3(w, name, x, **kw):
-    return O.conv3x3(x, w[f"{name}.weight"], w[f"{name}.bias"], **kw)
+    return O.conv3x3(x, np.ascontiguousarray(w[f"{name}.weight"], np.float32), w[f"{name}.bias"], **kw)
 
 
 def _conv1(w, name, x, residual=None):
-    return O.conv1x1(x, w[f"{name}.weight"], w[f"{name}.bias"], residual)
+    return O.conv1x1(x, np.ascontiguousarray(w[f"{name}.weight"], np.float32), w[f"{name}.bias"], residual)
 
 
 def resnet(w, name, x):
@@ -70,3 +72,20 @@ def decode(w, latents):
     s, t = _affine(w, "decoder.conv_norm_out", cur)
     out = _conv3(w, "decoder.conv_out", cur, prologue=(s, t, True))
     return ((out + np.float32(1.0)) * np.float32(0.5)).astype(np.float32)
+
+
+def encode(w, images, noise):
+    """images [b, h, w, 3] in [-1, 1], noise [b, h/8, w/8, 4] -> scaled latents (encoder.rs:173-230)."""
+    cur = _conv3(w, "encoder.conv_in", np.asarray(images, np.float32))
+    for i in range(4):
+        for j in range(2):
+            cur = resnet(w, f"encoder.down_blocks.{i}.resnets.{j}", cur)
+        if i < 3:
+            cur = _conv3(w, f"encoder.down_blocks.{i}.downsamplers.0.conv", cur, stride=2, pad=(0, 0, 1, 1))
+    cur = resnet(w, "encoder.mid_block.resnets.0", cur)
+    cur = mid_attention(w, "encoder.mid_block.attentions.0", cur)
+    cur = resnet(w, "encoder.mid_block.resnets.1", cur)
+    s, t = _affine(w, "encoder.conv_norm_out", cur)
+    mom = _conv3(w, "encoder.conv_out", cur, prologue=(s, t, True))
+    moments = _conv1(w, "quant_conv", mom)
+    return O.vae_sample(moments, noise)

@@ -13,6 +13,17 @@
    of 4, depthwise channel tails, a GN(+SiLU) prologue fused into 3×3 convs
    (plain and upsampled), LayerNorm at UNet widths, and the broadcast adds.
 
+3. ``imaging_ref.safetensors``: the reference's Pillow blur fixture
+   (``tests/fixtures/blur.safetensors``, Pillow 10.4 per its generator), copied,
+   plus two model-size cases written here with the installed Pillow: random
+   filled ellipses covering 10-40 % of a 512² mask (the BASELINE mask
+   distribution), blurred with ``GaussianBlur(3)`` as upstream ``_post_process``
+   does.
+4. ``weights_manifest.json``: every tensor of the converted UNet and VAE
+   (name -> shape), derived from the reference's ``docs/weights-manifest.txt``
+   with the converter's transformations (BatchNorms folded into new ``.bias``
+   tensors, layouts of ``tools/convert_weights.py``).
+
 Layouts follow the reference converter: activations NHWC, 1×1 weights
 [o, i], dense 3×3 [o, 3, 3, i], depthwise [3, 3, c].
 """
@@ -112,6 +123,70 @@ def extra_cases() -> dict:
     return f32(t)
 
 
+def ellipse_mask(rng, side=512, lo=0.10, hi=0.40):
+    """Union of random filled ellipses until the covered fraction lies in [lo, hi]."""
+    yy, xx = np.mgrid[:side, :side]
+    while True:
+        m = np.zeros((side, side), bool)
+        target = rng.uniform(lo, hi)
+        while m.mean() < target:
+            cy, cx = rng.uniform(0, side, 2)
+            ry, rx = rng.uniform(side * 0.05, side * 0.3, 2)
+            th = rng.uniform(0, np.pi)
+            dy, dx = yy - cy, xx - cx
+            u = (dx * np.cos(th) + dy * np.sin(th)) / rx
+            v = (-dx * np.sin(th) + dy * np.cos(th)) / ry
+            m |= u * u + v * v <= 1.0
+        if lo <= m.mean() <= hi:
+            return (m * 255).astype(np.uint8)
+
+
+def imaging_cases(reference_root):
+    from PIL import Image, ImageFilter
+    import PIL
+    t = {k: np.ascontiguousarray(v) for k, v in
+         load_file(os.path.join(reference_root, "tests", "fixtures", "blur.safetensors")).items()}
+    rng = np.random.default_rng(512)
+    for k in ("e1", "e2"):
+        m = ellipse_mask(rng)
+        blurred = np.asarray(Image.fromarray(m).convert("RGB").filter(ImageFilter.GaussianBlur(radius=3)))[:, :, 0]
+        t[f"{k}.mask"] = m
+        t[f"{k}.blurred"] = np.ascontiguousarray(blurred, np.uint8)
+    return t, PIL.__version__
+
+
+def converted_manifest(reference_root):
+    """name -> shape of the converted weights (tools/convert_weights.py transformations)."""
+    import ast
+    bn_targets = {"bn1": "conv_dw", "bn2": "conv_pw", "norm_q": "to_q", "norm_v": "to_v"}
+    out, cur = {}, None
+    for line in open(os.path.join(reference_root, "docs", "weights-manifest.txt")):
+        line = line.rstrip("\n")
+        if not line or line.startswith("#"):
+            continue
+        if line.startswith("["):
+            cur = line.strip("[]")
+            out[cur] = {}
+            continue
+        name, shape = line.split("\t")
+        shape = ast.literal_eval(shape)
+        mod, _, leaf = name.rpartition(".")
+        parent, _, bn = mod.rpartition(".")
+        if bn in bn_targets:
+            if leaf == "weight":
+                out[cur][f"{parent}.{bn_targets[bn]}.bias"] = [shape[0]]
+            continue
+        if leaf == "rel_pos_emb":
+            shape = shape[:3]
+        elif leaf == "weight" and len(shape) == 5:
+            shape = [shape[0], shape[3] * shape[4]]
+        elif leaf == "weight" and len(shape) == 4:
+            o, i, kh, kw = shape
+            shape = [o, i] if (kh, kw) == (1, 1) else ([3, 3, o] if i == 1 else [o, 3, 3, i])
+        out[cur][name] = list(shape)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", default="/root/reference")
@@ -125,7 +200,15 @@ def main():
     save_file(extra, os.path.join(HERE, "kernels_extra.safetensors"),
               metadata={"format": "moebius-b200-fixture/1", "generator": "tests/golden/make_golden.py",
                         "torch": torch.__version__, "seed": "20261201"})
-    print(f"wrote {len(ref)} reference tensors and {len(extra)} extra tensors")
+    img, pil_version = imaging_cases(args.reference_root)
+    save_file(img, os.path.join(HERE, "imaging_ref.safetensors"),
+              metadata={"format": "moebius-b200-fixture/1", "generator": "tests/golden/make_golden.py",
+                        "source": "moebius-cpu tests/fixtures/blur.safetensors (a, b, c); e1, e2 from Pillow "
+                                  + pil_version})
+    import json
+    with open(os.path.join(HERE, "weights_manifest.json"), "w") as f:
+        json.dump(converted_manifest(args.reference_root), f, indent=0, sort_keys=True)
+    print(f"wrote {len(ref)} reference tensors, {len(extra)} extra tensors, {len(img)} imaging tensors")
 
 
 if __name__ == "__main__":

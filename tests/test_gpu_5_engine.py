@@ -1,0 +1,218 @@
+"""GPU parity of the engine (include/moebius_cuda_engine.h) against the CPU
+oracle composed in the reference's order: the UNet (src/unet/*), the VAE
+encoder (src/vae/encoder.rs) and the whole Exact inpaint (src/pipeline.rs)
+with caller-supplied noise, on seeded random-init weights in the converter's
+format. Scaled-down networks of the same structure (widths 64/128/256,
+latent 16; VAE widths 32/64/128/128) keep the oracle fast; the full-size
+network runs one UNet step and a 2-step inpaint. Gates (BASELINE
+north_star): max relative error ≤ 1e-3 (f32 weights, 3xTF32) / 5e-3 (f16
+weights, 2xTF32) per network output, 8-bit PSNR ≥ 45 dB end to end."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from conftest import load_package, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+TINY_UNET = ((64, 128, 256), 16)
+TINY_VAE = (32, 64, 128, 128)
+
+
+def psnr8(a, b):
+    mse = np.mean((a.astype(np.float64) - b.astype(np.float64)) ** 2)
+    return float("inf") if mse == 0 else 10 * np.log10(255.0 ** 2 / mse)
+
+
+def _weights(tmp_path_factory, name, unet=TINY_UNET, vae=TINY_VAE, f16=True, seed=0):
+    syn = load_package().synthetic
+    d = str(tmp_path_factory.mktemp(name))
+    syn.write_weights_dir(d, seed=seed, f16=f16, unet_widths=unet[0], latent=unet[1], vae_widths=vae)
+    wu, _ = syn.read_safetensors(os.path.join(d, "unet.safetensors"))
+    wv, _ = syn.read_safetensors(os.path.join(d, "vae.safetensors"))
+    return d, wu, wv
+
+
+@pytest.fixture(scope="module", params=["f16", "f32"])
+def tiny(request, tmp_path_factory, mbx, ctx):
+    d, wu, wv = _weights(tmp_path_factory, f"tiny_{request.param}", f16=request.param == "f16")
+    eng = mbx.engine.Engine(d, 0)
+    eng.set_stream(ctx.stream)
+    yield eng, wu, wv, request.param
+    eng.close()
+
+
+@pytest.fixture(scope="module")
+def full(tmp_path_factory, mbx, ctx):
+    syn = mbx.synthetic
+    d, wu, wv = _weights(tmp_path_factory, "full", unet=(syn.UNET_WIDTHS, syn.UNET_LATENT), vae=syn.VAE_WIDTHS)
+    eng = mbx.engine.Engine(d, 0)
+    eng.set_stream(ctx.stream)
+    yield eng, wu, wv
+    eng.close()
+
+
+def _gate(wdtype):
+    return 1e-3 if wdtype == "f32" else 5e-3
+
+
+def test_engine_reads_the_network_shape(tiny):
+    eng = tiny[0]
+    assert (eng.latent, eng.side, eng.widths) == (16, 128, (64, 128, 256))
+
+
+@pytest.mark.parametrize("items,cfg,t", [(2, True, 900), (4, True, 450), (1, False, 0)])
+def test_unet_forward_matches_oracle(ctx, tiny, items, cfg, t):
+    from oracle import unet_ref
+    eng, wu, _, wdtype = tiny
+    rng = np.random.default_rng(items + t)
+    x = rng.standard_normal((items, 16, 16, 9)).astype(np.float32)
+    xd, eps = ctx.upload(x), ctx.empty((items, 16, 16, 4))
+    eng.unet_forward(xd.ptr, items, t, cfg, eps.ptr)
+    got = eps.numpy()
+    branches = [i % 2 for i in range(items)] if cfg else [1] * items
+    want = unet_ref.forward(wu, x, t, branches)
+    assert max_rel_err(got, want) <= _gate(wdtype)
+
+
+def test_vae_encode_decode_match_oracle(ctx, tiny):
+    from oracle import vae_ref
+    eng, _, wv, wdtype = tiny
+    rng = np.random.default_rng(8)
+    img = rng.uniform(-1, 1, (2, 64, 64, 3)).astype(np.float32)
+    noise = rng.standard_normal((2, 8, 8, 4)).astype(np.float32)
+    z = ctx.empty((2, 8, 8, 4))
+    imgd, nd = ctx.upload(img), ctx.upload(noise)
+    eng.vae_encode(imgd.ptr, nd.ptr, 2, 64, 64, z.ptr)
+    assert max_rel_err(z.numpy(), vae_ref.encode(wv, img, noise)) <= _gate(wdtype)
+    lat = (rng.standard_normal((2, 8, 8, 4)) * 0.13025).astype(np.float32)
+    out = ctx.empty((2, 64, 64, 3))
+    latd = ctx.upload(lat)
+    eng.vae_decode(latd.ptr, 2, 8, 8, out.ptr)
+    assert max_rel_err(out.numpy(), vae_ref.decode(wv, lat)) <= _gate(wdtype)
+
+
+def _inputs(rng, n, side, ch=3):
+    lat = side // 8
+    img = rng.integers(0, 256, (n, side, side, ch), dtype=np.uint8)
+    yy, xx = np.mgrid[:side, :side]
+    masks = np.zeros((n, side, side), np.uint8)
+    for i in range(n):
+        cy, cx = rng.uniform(0.3, 0.7, 2) * side
+        ry, rx = rng.uniform(0.15, 0.3, 2) * side
+        masks[i] = ((((yy - cy) / ry) ** 2 + ((xx - cx) / rx) ** 2) <= 1) * rng.integers(128, 256)
+    nv = rng.standard_normal((2 * n, lat, lat, 4)).astype(np.float32)
+    ni = rng.standard_normal((n, lat, lat, 4)).astype(np.float32)
+    no = rng.standard_normal((n, 4)).astype(np.float32)
+    return img, masks, nv, ni, no
+
+
+def test_inpaint_batch_matches_oracle(mbx, tiny):
+    """Three inpaints in one batch (the last with an empty mask), Exact preset, 19 DDIM steps."""
+    from oracle import pipeline_ref, unet_ref
+    eng, wu, wv, _ = tiny
+    rng = np.random.default_rng(21)
+    img, masks, nv, ni, no = _inputs(rng, 3, 128)
+    masks[2] = 0
+    got = img.copy()
+    eng.inpaint_batch(got, masks, noise=(nv, ni, no))
+    ehs = unet_ref.conditioning(wu)
+    for i in range(2):
+        want = pipeline_ref.inpaint(wu, wv, img[i], masks[i], nv[2 * i:2 * i + 2], ni[i], no[i], ehs=ehs)
+        assert psnr8(got[i], want) >= 45.0
+        assert not np.array_equal(got[i], img[i])
+    assert np.array_equal(got[2], img[2]), "an empty mask changes nothing"
+
+
+def test_batch_items_are_independent(mbx, tiny):
+    eng = tiny[0]
+    rng = np.random.default_rng(22)
+    img, masks, nv, ni, no = _inputs(rng, 2, 128, ch=4)
+    both = img.copy()
+    eng.inpaint_batch(both, masks, noise=(nv, ni, no), p=mbx.engine.params(steps=4))
+    one = img[1:].copy()
+    eng.inpaint_batch(one, masks[1:], noise=(nv[2:], ni[1:], no[1:]), p=mbx.engine.params(steps=4))
+    assert np.array_equal(both[1:], one)
+    assert np.array_equal(both[..., 3], img[..., 3]), "alpha is preserved"
+
+
+def test_single_image_api(mbx, tiny):
+    eng = tiny[0]
+    rng = np.random.default_rng(23)
+    img, masks, *_ = _inputs(rng, 1, 128, ch=4)
+    # Strided image rows (reference moebius_inpaint takes a row stride).
+    canvas = np.zeros((128, 128 + 7, 4), np.uint8)
+    canvas[:, :128] = img[0]
+    view = canvas[:, :128]
+    rect = eng.inpaint(view, masks[0], mbx.engine.params(steps=3, seed=5))
+    assert rect == (0, 0, 128, 128)
+    past = np.argwhere(canvas[:, 128:] != 0)
+    assert past.size == 0, f"bytes past the row width changed: {past[:8].tolist()} of {len(past)}"
+    assert np.array_equal(view[..., 3], img[0, ..., 3])
+    again = np.ascontiguousarray(img[0]).copy()
+    eng.inpaint(again, masks[0], mbx.engine.params(steps=3, seed=5))
+    assert np.array_equal(again, view), "seeded noise is deterministic"
+    blank = img[0].copy()
+    assert eng.inpaint(blank, np.zeros((128, 128), np.uint8)) == (0, 0, 0, 0)
+    assert np.array_equal(blank, img[0])
+
+
+def test_engine_rejects_unsupported_requests(mbx, tiny):
+    eng = tiny[0]
+    img = np.zeros((64, 64, 3), np.uint8)
+    with pytest.raises(mbx.MbxError) as e:
+        eng.inpaint(img, np.full((64, 64), 255, np.uint8))
+    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+    img = np.zeros((128, 128, 3), np.uint8)
+    for p in (mbx.engine.params(preset=mbx.abi.PRESET_FAST), mbx.engine.params(mask_dilate=3),
+              mbx.engine.params(steps=1001)):
+        with pytest.raises(mbx.MbxError) as e:
+            eng.inpaint(img, np.full((128, 128), 255, np.uint8), p)
+        assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+
+
+def test_progress_reports_and_cancel_leaves_image_untouched(mbx, tiny):
+    eng = tiny[0]
+    rng = np.random.default_rng(24)
+    img, masks, *_ = _inputs(rng, 1, 128)
+    seen = []
+
+    def progress(stage, done, total):
+        seen.append((stage, done, total))
+        return stage == 1 and done == 2  # cancel after the second denoising step
+
+    work = img[0].copy()
+    with pytest.raises(mbx.MbxError) as e:
+        eng.inpaint(work, masks[0], mbx.engine.params(steps=5), progress)
+    assert e.value.code == mbx.abi.ERR_CANCELLED
+    assert np.array_equal(work, img[0])
+    assert seen == [(0, 0, 1), (0, 1, 1), (1, 1, 4), (1, 2, 4)]
+    seen.clear()
+    eng.inpaint(work, masks[0], mbx.engine.params(steps=5), lambda s, d, t: seen.append((s, d, t)) and False)
+    assert seen[-3:] == [(1, 4, 4), (2, 0, 1), (2, 1, 1)]
+
+
+def test_full_size_unet_step_matches_oracle(ctx, full):
+    from oracle import unet_ref
+    eng, wu, _ = full
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((2, 64, 64, 9)).astype(np.float32)
+    eps = ctx.empty((2, 64, 64, 4))
+    xd = ctx.upload(x)
+    eng.unet_forward(xd.ptr, 2, 900, True, eps.ptr)
+    want = unet_ref.forward(wu, x, 900, [0, 1])
+    assert max_rel_err(eps.numpy(), want) <= 5e-3
+
+
+def test_full_size_inpaint_matches_oracle(mbx, full):
+    """One 512² inpaint, Exact preset with 3 steps (2 denoising steps), f16 weights."""
+    from oracle import pipeline_ref
+    eng, wu, wv = full
+    rng = np.random.default_rng(32)
+    img, masks, nv, ni, no = _inputs(rng, 1, 512)
+    got = img.copy()
+    eng.inpaint_batch(got, masks, mbx.engine.params(steps=3), noise=(nv, ni, no))
+    want = pipeline_ref.inpaint(wu, wv, img[0], masks[0], nv, ni[0], no[0], steps=3)
+    assert psnr8(got[0], want) >= 45.0
