@@ -1,39 +1,44 @@
 #!/usr/bin/env python
-"""Benchmark of the moebius-cuda engine kernel layer on B200.
+"""Benchmark of moebius-cuda on B200: Exact-preset 512² inpaints per second.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
-Workload (the memory-bound sweep, at its largest shape):
-one step runs the sweep's four ops over an NHWC f32 batch [8, 512, 512, 512]
-(4 GiB, larger than L2, so no flush is needed between steps):
+Workload: end-to-end Exact inpaints of 512×512 RGB u8
+images ~U[0,255] with binary masks of random filled ellipses covering 10-40 %,
+seeded latent noise, the 0.22B Moebius UNet + SDXL VAE with seeded
+random-init f16 weights in the reference converter's format (no checkpoint
+offline), preset.rs Exact: 20 steps at strength 0.99 (19 DDIM steps from
+t = 900), CFG 2.5 (UNet batch 2 per inpaint), noise offset 0.0357, VAE encode
+of [image, masked] and decode, Pillow-blur feathered paste.
 
-    y1 = SiLU(GroupNorm32(x))           8 B/elt  (read x, write y1)
-    y2 = y1 + bias[c] + temb[item, c]   8 B/elt
-    y2 += x        (residual add)      12 B/elt
-    y4 = depthwise3x3(y2) + bias        8 B/elt
+One step = one batch of B inpaints per GPU (default 8): prepare → VAE encode
+(2B images) → 19 × (UNet at batch 2B replayed from a CUDA graph, CFG + DDIM)
+→ VAE decode (B) → blur + paste. `value` = inpaints/s of the whole job with
+the inputs already in HBM (device-timed, max over ranks; L2 flushed between
+steps); `e2e` = the same through mbx_inpaint_batch with pinned host buffers
+(pixels, masks and noise copied in and the pixels out inside the timed region).
+Each rank owns its own inpaints (weak scaling, no collective on the data path;
+torch.distributed carries only the barrier and the max of the device times).
 
-The metric is algorithmic bytes per second (36 B/elt per step), whole job.
-Each rank owns its own batch (independent inputs, no collective on the data
-path: weak scaling); torch.distributed only carries the barrier and the
-max-over-ranks of the device time.
-
-Printed on rank 0 as one JSON line, also with the roofline of the dominant
-op, the CPU baseline (the oracle port on the host cores), the end-to-end
-number through the C ABI with pinned host buffers (H2D of x, D2H of y4 in
-the timed region), the tensor-core conv sweep's largest shape, the SM clocks
-sampled during the timed region and the count of this library's kernel
-launches.
+Also in the line: the roofline of the dominant kernel (the tcgen05 implicit-
+GEMM conv, timed live on the conv sweep's largest 3×3 shape against the
+measured cuBLAS TF32 peak), the memory-bound sweep (its
+largest shape, against the measured HBM copy bandwidth), the VAE decoder
+(configs[3], B = 1 and 8), the CPU baseline (the oracle on the host cores), SM
+clocks sampled during the timed region and this library's kernel launches.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import os
 import re
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -42,13 +47,18 @@ import numpy as np
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-SHAPE = (8, 512, 512, 512)
-CPU_SAMPLE = (1, 128, 256, 512)
+METRIC = "512x512 Exact-preset inpaints/s (UNet + VAE + DDIM, CFG 2.5, 19 steps), whole job"
+UNIT = "inpaints/s"
+SIDE = 512
+LATENT = 64
+STEPS_EXACT = 20
+# The reference's own per-inpaint FLOP count (upstream count: UNet 632 GFLOP/step × 19
+# + VAE encode 2233 + decode 2515 GFLOP), used to express inpaints/s as TFLOP/s.
+INPAINT_TFLOP = 16.76
+SWEEP_SHAPE = (8, 512, 512, 512)
 BYTES_PER_ELT = {"group_norm_silu": 8, "bias_temb_add": 8, "residual_add": 12, "depthwise3x3": 8}
-METRIC = ("memory-bound sweep throughput (GroupNorm32+SiLU, bias+temb add, residual add, depthwise 3x3) "
-          "in algorithmic GB/s")
-UNIT = "GB/s"
-CONV_SHAPE = (8, 256, 256, 512, 512)  # n, h, w, c_in, c_out: the conv sweep's largest 3x3 case
+CONV_SHAPE = (8, 256, 256, 512, 512)  # n, h, w, c_in, c_out: the conv sweep's largest 3×3 case
+L2_FLUSH_BYTES = 256 << 20
 
 
 def peaks():
@@ -60,10 +70,14 @@ def peaks():
 
 
 def config(args):
-    return {"workload": "BASELINE configs[1] memory-bound sweep, largest shape; 4 ops per step",
-            "shape_nhwc": list(SHAPE), "groups": 32, "eps": 1e-6, "dtype": "f32",
-            "per_rank_batch": SHAPE[0], "global_batch": SHAPE[0] * args.gpus, "parallelism": f"dp{args.gpus}",
-            "l2": "inputs (4 GiB per tensor) larger than L2; no flush"}
+    return {"workload": "BASELINE configs[4]: end-to-end Exact inpaint, 512x512 RGB, random-ellipse masks "
+                        "10-40 %, 0.22B UNet + SDXL VAE (seeded random-init f16 weights)",
+            "model": "moebius student UNet (320/640/1280, lambda layers) + SDXL VAE", "image": [SIDE, SIDE, 3],
+            "per_rank_batch": args.batch, "global_batch": args.batch * args.gpus, "parallelism": f"dp{args.gpus}",
+            "preset": {"steps": STEPS_EXACT, "strength": 0.99, "denoise_steps": 19, "guidance": 2.5,
+                       "noise_offset": 0.0357, "scheduler": "DDIM leading", "paste": "feather"},
+            "weights": "f16 GEMM weights (2xTF32 products), f32 accumulation",
+            "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MiB write)"}
 
 
 # --------------------------------------------------------------------------- clocks
@@ -74,15 +88,14 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_uuid: str | None):
-        self.uuid = gpu_uuid
+    def __init__(self, index: int):
+        self.index = index
         self.proc = None
         self.lines: list[str] = []
 
     def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
-        if self.uuid:
-            cmd += ["-i", self.uuid]
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+               "-i", str(self.index)]
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
@@ -121,9 +134,8 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-# --------------------------------------------------------------------------- helpers
 def traffic_from_profiles(kernel_key: str):
-    """Per-launch DRAM traffic (bytes) of a kernel at the bench shape, from a committed ncu summary."""
+    """Per-launch DRAM traffic (bytes) at the bench shape, from a committed ncu summary."""
     pdir = os.path.join(REPO, "profiles")
     if not os.path.isdir(pdir):
         return None
@@ -135,35 +147,6 @@ def traffic_from_profiles(kernel_key: str):
     return None
 
 
-def cpu_baseline(steps=3):
-    """The oracle (CPU restatement of the reference kernels) on a bounded sample, all host threads."""
-    from oracle import oracle
-    threads = oracle.set_threads(0)
-    rng = np.random.default_rng(1234)
-    n, h, w, c = CPU_SAMPLE
-    x = rng.standard_normal(CPU_SAMPLE, dtype=np.float32)
-    gamma = (1.0 + 0.02 * rng.standard_normal(c)).astype(np.float32)
-    beta = (0.02 * rng.standard_normal(c)).astype(np.float32)
-    bias = (0.01 * rng.standard_normal(c)).astype(np.float32)
-    temb = rng.standard_normal((n, c), dtype=np.float32)
-    dw_w = (rng.standard_normal((3, 3, c)) / np.sqrt(3.0)).astype(np.float32)
-    dw_b = (0.01 * rng.standard_normal(c)).astype(np.float32)
-    best = None
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        y1 = oracle.group_norm(x, 32, 1e-6, gamma, beta, silu=True)
-        y2 = oracle.bias_temb_add(y1, bias, temb)
-        y2 = oracle.add(y2, x)
-        oracle.depthwise3x3(y2, dw_w, dw_b, "none")
-        dt = time.perf_counter() - t0
-        best = dt if best is None else min(best, dt)
-    elems = int(np.prod(CPU_SAMPLE))
-    gbs = sum(BYTES_PER_ELT.values()) * elems / best / 1e9
-    return {"value": round(gbs, 2), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"the same 4-op step on {list(CPU_SAMPLE)} (oracle/ref_engine.cpp, OpenMP), best of {steps}",
-            "seconds_per_sample_step": round(best, 4)}
-
-
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -173,10 +156,81 @@ def init_dist():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     return world, rank, local, dist
 
 
+def weights_dir(rank, dist, small):
+    """Seeded converter-format weights, written once per box (rank 0) and shared by the ranks."""
+    syn = importlib.import_module("moebius-cpu_b200.synthetic")
+    tag = "small" if small else "full"
+    d = os.path.join(tempfile.gettempdir(), f"moebius_b200_bench_weights_{tag}_seed0")
+    done = os.path.join(d, "complete")
+    if rank == 0 and not os.path.exists(done):
+        if small:
+            syn.write_weights_dir(d, seed=0, f16=True, unet_widths=(64, 128, 256), latent=16,
+                                  vae_widths=(32, 64, 128, 128))
+        else:
+            syn.write_weights_dir(d, seed=0, f16=True)
+        open(done, "w").close()
+    if dist:
+        dist.barrier()
+    return d
+
+
+def synthetic_inputs(rank, n, side):
+    """Seeded images ~U[0,255], ellipse masks (10-40 %), and the pipeline's noise tensors."""
+    syn = importlib.import_module("moebius-cpu_b200.synthetic")
+    rng = np.random.default_rng(1234 + rank)
+    lat = side // 8
+    img = rng.integers(0, 256, (n, side, side, 3), dtype=np.uint8)
+    masks = syn.ellipse_masks(rng, n, side)
+    nv = rng.standard_normal((2 * n, lat, lat, 4), dtype=np.float32)
+    ni = rng.standard_normal((n, lat, lat, 4), dtype=np.float32)
+    no = rng.standard_normal((n, 4), dtype=np.float32)
+    return img, masks, nv, ni, no
+
+
+# --------------------------------------------------------------------------- CPU baseline (the oracle)
+def cpu_inpaint_baseline(small=False):
+    """The oracle on a bounded sample of one inpaint: one UNet CFG step (batch 2), the VAE encode
+    of [image, masked] and the decode, each timed once on all host threads; an inpaint costs
+    19 UNet steps + encode + decode (the element work between them is negligible)."""
+    from oracle import oracle, unet_ref, vae_ref
+    syn = importlib.import_module("moebius-cpu_b200.synthetic")
+    threads = oracle.set_threads(0)
+    if small:
+        wu = syn.random_weights(syn.unet_shapes((64, 128, 256), 16), 0)
+        wv = syn.random_weights(syn.vae_shapes((32, 64, 128, 128)), 1)
+        side = 128
+    else:
+        wu = syn.random_weights(syn.unet_shapes(), 0)
+        wv = syn.random_weights(syn.vae_shapes(), 1)
+        side = SIDE
+    lat = side // 8
+    rng = np.random.default_rng(99)
+    ehs = unet_ref.conditioning(wu)
+    x = rng.standard_normal((2, lat, lat, 9)).astype(np.float32)
+    t0 = time.perf_counter()
+    unet_ref.forward(wu, x, 900, [0, 1], ehs)
+    t_unet = time.perf_counter() - t0
+    img = rng.uniform(-1, 1, (2, side, side, 3)).astype(np.float32)
+    noise = rng.standard_normal((2, lat, lat, 4)).astype(np.float32)
+    t0 = time.perf_counter()
+    z = vae_ref.encode(wv, img, noise)
+    t_enc = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    vae_ref.decode(wv, z[:1])
+    t_dec = time.perf_counter() - t0
+    per = 19 * t_unet + t_enc + t_dec
+    return {"value": round(1.0 / per, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"one {side}x{side} inpaint timed by parts on the oracle (oracle/, C++ + OpenMP restatement "
+                       "of the reference's Rust engine, which cannot be built here): 1 UNet CFG step at batch 2 "
+                       f"({t_unet:.2f} s) x 19 + VAE encode of 2 images ({t_enc:.2f} s) + decode ({t_dec:.2f} s)"),
+            "seconds_per_inpaint": round(per, 2)}
+
+
+# --------------------------------------------------------------------------- secondary measurements
 def tf32_peak(torch):
     """Dense TF32 throughput of cuBLAS (8192^3 matmul, TF32 on), burst best of 10: the conv roofline."""
     torch.backends.cuda.matmul.allow_tf32 = True
@@ -197,80 +251,48 @@ def tf32_peak(torch):
     return 2 * 8192 ** 3 / best / 1e12
 
 
-def decoder_flops(lat_h, lat_w):
-    """Direct-conv FLOPs of one decoder pass (1×1 and 3×3 convs, attention GEMMs)."""
-    vae = importlib.import_module("moebius-cpu_b200.vae")
-    total, h, w = 0.0, lat_h, lat_w
-    shapes = vae.decoder_weight_shapes()
-    # conv layers run at the resolution of their level
-    res = {"post_quant_conv": (h, w), "decoder.conv_in": (h, w), "decoder.mid_block": (h, w),
-           "decoder.conv_out": (8 * h, 8 * w), "decoder.conv_norm_out": (8 * h, 8 * w)}
-    for name, shp in shapes.items():
-        if not name.endswith(".weight") or len(shp) < 2:
-            continue
-        if name.startswith("decoder.up_blocks."):
-            lvl = int(name.split(".")[2])
-            hh, ww = h << lvl, w << lvl
-            if ".upsamplers." in name:
-                hh, ww = hh * 2, ww * 2
-        else:
-            key = next(k for k in res if name.startswith(k))
-            hh, ww = res[key]
-        taps = 9 if len(shp) == 4 else 1
-        total += 2.0 * hh * ww * shp[0] * shp[-1] * taps
-    hw = h * w
-    total += 2 * 2.0 * hw * hw * vae.VAE_BLOCK_OUT[-1]  # q·kᵀ and p·v
-    return total
-
-
-def bench_vae_decoder(mbx, ctx, torch, small=False):
-    vae = importlib.import_module("moebius-cpu_b200.vae")
-    lat_hw = 16 if small else 64
-    w = vae.random_decoder_weights(0, f16=True)
-    dec = vae.Decoder(ctx, w, "f16")
-    out = {"workload": f"BASELINE configs[3]: VAE decoder, latent [B,{lat_hw},{lat_hw},4] -> "
-                       f"[B,{8 * lat_hw},{8 * lat_hw},3], seeded random-init f16 weights (2xTF32)",
-           "gflop_per_image": round(decoder_flops(lat_hw, lat_hw) / 1e9, 1)}
-    gen = torch.Generator(device="cuda").manual_seed(7)
-    for bsz in (1, 8):
-        lat = torch.randn(bsz, lat_hw, lat_hw, 4, device="cuda", generator=gen) * vae.SCALING_FACTOR
-        L = mbx.DeviceTensor.wrap(ctx, lat.data_ptr(), tuple(lat.shape))
+def bench_conv(mbx, ctx, torch, dev, small):
+    """The tcgen05 implicit-GEMM conv on the conv sweep's largest 3×3 shape (f16 and f32 weights)."""
+    cn, chh, cww, cci, cco = (1, 128, 128, 512, 512) if small else CONV_SHAPE
+    gen = torch.Generator(device=dev).manual_seed(7)
+    cx = torch.randn(cn, chh, cww, cci, device=dev, generator=gen)
+    cy = torch.empty(cn, chh, cww, cco, device=dev)
+    wt = (torch.randn(cco, 3, 3, cci, generator=torch.Generator().manual_seed(7)) / (9 * cci) ** 0.5).numpy()
+    cb = 0.01 * torch.randn(cco, device=dev, generator=gen)
+    W = lambda t: mbx.DeviceTensor.wrap(ctx, t.data_ptr(), tuple(t.shape))  # noqa: E731
+    CX, CY, CB = W(cx), W(cy), W(cb)
+    flops = 2.0 * cn * chh * cww * 9 * cci * cco
+    tf32 = tf32_peak(torch)
+    out = {"shape": f"[{cn},{chh},{cww},{cci}] -> {cco}, 3x3 pad 1, bias", "tf32_dense_peak_tflops": round(tf32, 1),
+           "tf32_peak_source": "measured here: cuBLAS 8192^3 TF32 matmul, best of 10", "flops_per_launch": flops}
+    for dtype in ("f16", "f32"):
+        p = mbx.Param(ctx, wt, dtype)
         for _ in range(2):
-            dec.decode(L)
+            mbx.conv3x3(CX, p, CB, out=CY)
         torch.cuda.synchronize()
-        reps = 3
+        reps = 5
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record()
         for _ in range(reps):
-            img = dec.decode(L)
+            mbx.conv3x3(CX, p, CB, out=CY)
         e_ev.record()
         e_ev.synchronize()
-        ms = s_ev.elapsed_time(e_ev) / reps
-        out[f"b{bsz}"] = {"ms": round(ms, 2), "images_per_s": round(bsz / (ms / 1e3), 2),
-                          "useful_tflops": round(bsz * decoder_flops(lat_hw, lat_hw) / (ms / 1e3) / 1e12, 1)}
-        del img
-    dec.close()
+        cms = s_ev.elapsed_time(e_ev) / reps
+        mmas = 2 if dtype == "f16" else 3
+        useful = flops / (cms / 1e3) / 1e12
+        out[dtype] = {"ms": round(cms, 3), "useful_tflops": round(useful, 1), "issued_tflops": round(useful * mmas, 1),
+                      "mma_per_product": mmas, "useful_frac_of_tf32_peak": round(useful / tf32, 3),
+                      "issued_frac_of_tf32_peak": round(useful * mmas / tf32, 3)}
+        p.close()
     return out
 
 
-# --------------------------------------------------------------------------- our arm
-def run_ours(args):
-    import torch
-
-    world, rank, local, dist = init_dist()
-    torch.cuda.set_device(local)
-    mbx = importlib.import_module("moebius-cpu_b200")
-    ctx = mbx.Context(local)
-    # One explicit stream for torch's events and this library's kernels (the legacy
-    # default stream has handle 0, which mbx_ctx_set_stream reads as "own stream").
-    stream = torch.cuda.Stream(device=local)
-    torch.cuda.set_stream(stream)
-    ctx.set_stream(stream.cuda_stream)
-    assert ctx.stream == stream.cuda_stream
-    dev = torch.device("cuda", local)
-    n, h, w, c = SHAPE
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    x = torch.randn(SHAPE, device=dev, generator=gen)
+def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm):
+    """BASELINE configs[1] at its largest shape: the four memory-bound ops, algorithmic GB/s."""
+    shape = (1, 256, 256, 512) if small else SWEEP_SHAPE
+    n, h, w, c = shape
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    x = torch.randn(shape, device=dev, generator=gen)
     gamma = 1.0 + 0.02 * torch.randn(c, device=dev, generator=gen)
     beta = 0.02 * torch.randn(c, device=dev, generator=gen)
     bias = 0.01 * torch.randn(c, device=dev, generator=gen)
@@ -281,13 +303,83 @@ def run_ours(args):
     W = lambda t: mbx.DeviceTensor.wrap(ctx, t.data_ptr(), tuple(t.shape))  # noqa: E731
     X, G, B, BI, TE, DW, DB = map(W, (x, gamma, beta, bias, temb, dw_w, dw_b))
     Y1, Y2, Y4 = W(y1), W(y2), W(y4)
+    ops = [("group_norm_silu", lambda: mbx.group_norm(X, 32, 1e-6, G, B, silu=True, out=Y1)),
+           ("bias_temb_add", lambda: mbx.bias_temb_add(Y1, BI, TE, out=Y2)),
+           ("residual_add", lambda: mbx.add_inplace(Y2, X)),
+           ("depthwise3x3", lambda: mbx.depthwise3x3(Y2, DW, DB, "none", out=Y4))]
+    for _ in range(3):
+        for _, f in ops:
+            f()
+    torch.cuda.synchronize()
+    ev = {name: [] for name, _ in ops}
+    for _ in range(5):
+        for name, f in ops:
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            f()
+            e_ev.record()
+            ev[name].append((s_ev, e_ev))
+    torch.cuda.synchronize()
+    elems = int(np.prod(shape))
+    op_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in ev.items()}
+    total_ms = sum(op_ms.values())
+    return {"workload": f"BASELINE configs[1], largest shape {list(shape)} (inputs larger than L2)",
+            "gbs": round(sum(BYTES_PER_ELT.values()) * elems / (total_ms / 1e3) / 1e9, 1),
+            "ops_ms": {k: round(v, 4) for k, v in op_ms.items()},
+            "ops_frac_of_hbm": {k: round(BYTES_PER_ELT[k] * elems / (v / 1e3) / 1e9 / hbm, 4)
+                                for k, v in op_ms.items()}}
 
-    ops = [
-        ("group_norm_silu", lambda: mbx.group_norm(X, 32, 1e-6, G, B, silu=True, out=Y1)),
-        ("bias_temb_add", lambda: mbx.bias_temb_add(Y1, BI, TE, out=Y2)),
-        ("residual_add", lambda: mbx.add_inplace(Y2, X)),
-        ("depthwise3x3", lambda: mbx.depthwise3x3(Y2, DW, DB, "none", out=Y4)),
-    ]
+
+def bench_vae_decoder(eng, torch, dev, latent):
+    """the VAE decoder at B = 1 and 8 through the engine."""
+    out = {"workload": f"BASELINE configs[3]: VAE decoder, latent [B,{latent},{latent},4] -> "
+                       f"[B,{8 * latent},{8 * latent},3], seeded random-init f16 weights (2xTF32)"}
+    gen = torch.Generator(device=dev).manual_seed(7)
+    for bsz in (1, 8):
+        lat = torch.randn(bsz, latent, latent, 4, device=dev, generator=gen) * 0.13025
+        img = torch.empty(bsz, 8 * latent, 8 * latent, 3, device=dev)
+        for _ in range(2):
+            eng.vae_decode(lat.data_ptr(), bsz, latent, latent, img.data_ptr())
+        torch.cuda.synchronize()
+        reps = 3
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(reps):
+            eng.vae_decode(lat.data_ptr(), bsz, latent, latent, img.data_ptr())
+        e_ev.record()
+        e_ev.synchronize()
+        ms = s_ev.elapsed_time(e_ev) / reps
+        out[f"b{bsz}"] = {"ms": round(ms, 2), "images_per_s": round(bsz / (ms / 1e3), 2)}
+    return out
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+
+    world, rank, local, dist = init_dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    mbx = importlib.import_module("moebius-cpu_b200")
+    side = 128 if args.small else SIDE
+    wdir = weights_dir(rank, dist, args.small)
+    eng = mbx.engine.Engine(wdir, local)
+    # One explicit stream for torch's events and the engine's kernels.
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream.cuda_stream)
+    n = args.batch
+    img, masks, nv, ni, no = synthetic_inputs(rank, n, side)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    d_src, d_masks, d_nv, d_ni, d_no = t(img), t(masks), t(nv), t(ni), t(no)
+    d_work = torch.empty_like(d_src)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    p = mbx.engine.params()
+
+    def step():
+        d_work.copy_(d_src)
+        eng.inpaint_batch_device(d_work.data_ptr(), d_masks.data_ptr(), n, side, 3, p,
+                                 (d_nv.data_ptr(), d_ni.data_ptr(), d_no.data_ptr()))
 
     def barrier():
         torch.cuda.synchronize()
@@ -295,207 +387,190 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        for _, f in ops:
-            f()
+    for _ in range(args.warmup):  # the first one also captures the UNet graph for this batch size
+        step()
     barrier()
-    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid) if hasattr(
-        torch.cuda.get_device_properties(dev), "uuid") else None)
-    if sampler.uuid and not sampler.uuid.startswith("GPU-"):
-        sampler.uuid = "GPU-" + sampler.uuid
+    sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    ev = {name: [] for name, _ in ops}
-    launches0 = ctx.launch_count
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record()
+    launches0 = eng.launch_count
+    evs = []
     for _ in range(args.steps):
-        for name, f in ops:
-            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_ev.record()
-            f()
-            e_ev.record()
-            ev[name].append((s_ev, e_ev))
-    end.record()
+        flush.zero_()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        step()
+        e_ev.record()
+        evs.append((s_ev, e_ev))
     barrier()
-    launches = ctx.launch_count - launches0
+    launches = eng.launch_count - launches0
     clocks = sampler.stop()
-    ms = start.elapsed_time(end) / args.steps
-    op_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in ev.items()}
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    ms = float(sum(a.elapsed_time(b) for a, b in evs)) / args.steps
+    tt = torch.tensor([ms], device=dev, dtype=torch.float64)
     if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    elems = int(np.prod(SHAPE))
-    step_bytes = sum(BYTES_PER_ELT.values()) * elems
-    value = world * step_bytes / (ms_max / 1e3) / 1e9
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_max = float(tt.item())
+    value = world * n / (ms_max / 1e3)
+    changed = float((d_work != d_src).any(dim=-1).float().mean().item())
 
-    # Parity spot-check of this very run (size-independent properties on the device result).
-    ok = bool(torch.isfinite(y4).all().item())
-
-    # End to end through the C ABI with pinned host buffers: H2D x, the 4 ops, D2H y4.
+    # End to end through mbx_inpaint_batch with pinned host buffers (copies inside the timed region).
     e2e = None
     if not args.skip_e2e:
-        nbytes = x.numel() * 4
-        hx = mbx.Context.host_alloc(nbytes)
-        hy = mbx.Context.host_alloc(nbytes)
+        hosts = {}
         try:
-            ctx.copy_d2h(hx, x.data_ptr(), nbytes)
-            ctx.synchronize()
+            for name, a in (("img", img), ("masks", masks), ("nv", nv), ("ni", ni), ("no", no)):
+                ptr = mbx.Context.host_alloc(a.nbytes)
+                buf = np.ctypeslib.as_array((ctypes.c_uint8 * a.nbytes).from_address(ptr)).view(a.dtype)
+                hosts[name] = (ptr, buf.reshape(a.shape))
+                hosts[name][1][...] = a
+            work_ptr = mbx.Context.host_alloc(img.nbytes)
+            work = np.ctypeslib.as_array((ctypes.c_uint8 * img.nbytes).from_address(work_ptr)).reshape(img.shape)
+            lib = mbx.abi.lib()
             e2e_steps = max(1, min(3, args.steps))
+
+            def host_step():
+                mbx.abi.check(lib.mbx_inpaint_batch(eng.handle, ctypes.c_void_p(work_ptr),
+                                                    ctypes.c_void_p(hosts["masks"][0]), n, side, 3, ctypes.byref(p),
+                                                    ctypes.c_void_p(hosts["nv"][0]), ctypes.c_void_p(hosts["ni"][0]),
+                                                    ctypes.c_void_p(hosts["no"][0]), 0, mbx.abi.PROGRESS_FN(), None))
+
+            work[...] = hosts["img"][1]
+            host_step()
             barrier()
-            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_ev.record()
+            tot = 0.0
             for _ in range(e2e_steps):
-                ctx.copy_h2d(x.data_ptr(), hx, nbytes)
-                for _, f in ops:
-                    f()
-                ctx.copy_d2h(hy, y4.data_ptr(), nbytes)
-            e_ev.record()
+                work[...] = hosts["img"][1]  # fresh pixels (the call inpaints in place); outside the timing
+                flush.zero_()
+                s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_ev.record()
+                host_step()
+                e_ev.record()
+                e_ev.synchronize()
+                tot += s_ev.elapsed_time(e_ev)
             barrier()
-            e_ms = s_ev.elapsed_time(e_ev) / e2e_steps
-            te = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+            te = torch.tensor([tot / e2e_steps], device=dev, dtype=torch.float64)
             if dist:
                 dist.all_reduce(te, op=dist.ReduceOp.MAX)
-            e2e = {"value": round(world * step_bytes / (float(te.item()) / 1e3) / 1e9, 2), "unit": UNIT,
-                   "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes, "ms_per_step": round(float(te.item()), 3),
-                   "path": "mbx C ABI: mbx_memcpy_h2d from pinned host, 4 ops, mbx_memcpy_d2h to pinned host"}
+            h2d = img.nbytes + masks.nbytes + nv.nbytes + ni.nbytes + no.nbytes
+            e2e = {"value": round(world * n / (float(te.item()) / 1e3), 3), "unit": UNIT,
+                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(img.nbytes),
+                   "ms_per_step": round(float(te.item()), 2),
+                   "path": "mbx_inpaint_batch(device_buffers=0) from pinned host memory: H2D pixels, masks, noise; "
+                           "whole pipeline; D2H pixels"}
+            mbx.Context.host_free(work_ptr)
         finally:
-            mbx.Context.host_free(hx)
-            mbx.Context.host_free(hy)
-
-    # Tensor-core conv sweep, largest 3x3 shape (f16 and f32 weights).
-    conv = None
-    if not args.skip_conv and rank == 0:
-        cn, chh, cww, cci, cco = CONV_SHAPE
-        del y1, y2
-        torch.cuda.empty_cache()
-        cx = torch.randn(cn, chh, cww, cci, device=dev, generator=gen)
-        cy = torch.empty(cn, chh, cww, cco, device=dev)
-        wt = (torch.randn(cco, 3, 3, cci, generator=torch.Generator().manual_seed(7)) / (9 * cci) ** 0.5).numpy()
-        cb = 0.01 * torch.randn(cco, device=dev, generator=gen)
-        CX, CY, CB = W(cx), W(cy), W(cb)
-        flops = 2.0 * cn * chh * cww * 9 * cci * cco
-        tf32 = tf32_peak(torch)
-        conv = {"shape": f"[{cn},{chh},{cww},{cci}] -> {cco}, 3x3 pad 1, bias", "tf32_dense_peak_tflops": round(tf32, 1),
-                "tf32_peak_source": "measured here: cuBLAS 8192^3 TF32 matmul, best of 10"}
-        for dtype in ("f16", "f32"):
-            p = mbx.Param(ctx, wt, dtype)
-            for _ in range(2):
-                mbx.conv3x3(CX, p, CB, out=CY)
-            torch.cuda.synchronize()
-            reps = 5
-            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_ev.record()
-            for _ in range(reps):
-                mbx.conv3x3(CX, p, CB, out=CY)
-            e_ev.record()
-            e_ev.synchronize()
-            cms = s_ev.elapsed_time(e_ev) / reps
-            mmas = 2 if dtype == "f16" else 3
-            useful = flops / (cms / 1e3) / 1e12
-            conv[dtype] = {"ms": round(cms, 3), "useful_tflops": round(useful, 1),
-                           "issued_tflops": round(useful * mmas, 1), "mma_per_product": mmas,
-                           "issued_frac_of_tf32_peak": round(useful * mmas / tf32, 3)}
-            p.close()
-
-    # the full VAE decoder (64×64 latent → 512×512 RGB), B = 1 and B = 8.
-    vae_line = None
-    if not args.skip_vae and rank == 0:
-        vae_line = bench_vae_decoder(mbx, ctx, torch, small=args.small)
+            for ptr, _ in hosts.values():
+                mbx.Context.host_free(ptr)
 
     hbm, peak_kind = peaks()
-    dom = max(op_ms, key=op_ms.get)
-    achieved = BYTES_PER_ELT[dom] * elems / (op_ms[dom] / 1e3) / 1e9
+    conv = sweep = vae_line = None
     if rank == 0:
+        ctxm = mbx.Context(local)
+        ctxm.set_stream(stream.cuda_stream)
+        if not args.skip_conv:
+            conv = bench_conv(mbx, ctxm, torch, dev, args.small)
+        if not args.skip_sweep:
+            sweep = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm)
+        if not args.skip_vae:
+            vae_line = bench_vae_decoder(eng, torch, dev, side // 8)
+        ctxm.close()
+    if rank == 0:
+        roof = None
+        if conv:
+            ach = conv["f16"]["useful_tflops"]
+            roof = {"bound": "tensor", "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM 3x3, f16 weights, 2xTF32)",
+                    "achieved": ach, "peak": conv["tf32_dense_peak_tflops"], "unit": "TFLOP/s",
+                    "frac": round(ach / conv["tf32_dense_peak_tflops"], 4),
+                    "peak_kind": "measured here (cuBLAS TF32 dense, burst); MEASURED_PEAKS.json holds no TF32 figure",
+                    "issued_frac": conv["f16"]["issued_frac_of_tf32_peak"],
+                    "algorithmic_flops_per_launch": conv["flops_per_launch"], "shape": conv["shape"],
+                    "traffic": traffic_from_profiles("conv_tc")}
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) NHWC f32, generated on device)",
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded U[0,255] images, random-ellipse masks, N(0,1) noise; random-init weights)",
             "config": config(args),
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": BYTES_PER_ELT[dom] * elems,
-                         "traffic": traffic_from_profiles(dom)},
-            "ops_ms": {k: round(v, 4) for k, v in op_ms.items()},
-            "ops_frac_of_hbm": {k: round(BYTES_PER_ELT[k] * elems / (v / 1e3) / 1e9 / hbm, 4)
-                                for k, v in op_ms.items()},
-            "e2e": e2e, "gpu_launches": launches, "clocks": clocks, "result_finite": ok,
-            "conv": conv,
-            "vae_decoder": vae_line,
+            "implied_tflops": round(value * INPAINT_TFLOP, 1),
+            "roofline": roof, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+            "result_changed_pixel_frac": round(changed, 4),
+            "conv": conv, "memory_sweep": sweep, "vae_decoder": vae_line,
+            "hbm_peak_gbs": hbm, "hbm_peak_kind": peak_kind,
         }
         if not args.skip_cpu:
-            line["cpu_baseline"] = cpu_baseline()
+            line["cpu_baseline"] = cpu_inpaint_baseline(args.small)
         print(json.dumps(line), flush=True)
+    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    ctx.close()
 
 
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args):
+    """The reference's CPU path, restated by the oracle (the Rust crate cannot be built here),
+    on all host threads. Each step is one UNet CFG step (batch 2), the bulk of an inpaint; the
+    VAE encode + decode of one inpaint is timed once and amortised over its 19 steps."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import oracle
+    from oracle import oracle, unet_ref, vae_ref
+    syn = importlib.import_module("moebius-cpu_b200.synthetic")
     threads = oracle.set_threads(0)
-    rng = np.random.default_rng(1234)
-    n, h, w, c = CPU_SAMPLE
-    x = rng.standard_normal(CPU_SAMPLE, dtype=np.float32)
-    gamma = (1.0 + 0.02 * rng.standard_normal(c)).astype(np.float32)
-    beta = (0.02 * rng.standard_normal(c)).astype(np.float32)
-    bias = (0.01 * rng.standard_normal(c)).astype(np.float32)
-    temb = rng.standard_normal((n, c), dtype=np.float32)
-    dw_w = (rng.standard_normal((3, 3, c)) / np.sqrt(3.0)).astype(np.float32)
-    dw_b = (0.01 * rng.standard_normal(c)).astype(np.float32)
-
-    def step():
-        y1 = oracle.group_norm(x, 32, 1e-6, gamma, beta, silu=True)
-        y2 = oracle.bias_temb_add(y1, bias, temb)
-        y2 = oracle.add(y2, x)
-        oracle.depthwise3x3(y2, dw_w, dw_b, "none")
-
+    side = 128 if args.small else SIDE
+    if args.small:
+        wu = syn.random_weights(syn.unet_shapes((64, 128, 256), 16), 0)
+        wv = syn.random_weights(syn.vae_shapes((32, 64, 128, 128)), 1)
+    else:
+        wu = syn.random_weights(syn.unet_shapes(), 0)
+        wv = syn.random_weights(syn.vae_shapes(), 1)
+    lat = side // 8
+    rng = np.random.default_rng(99)
+    ehs = unet_ref.conditioning(wu)
+    img = rng.uniform(-1, 1, (2, side, side, 3)).astype(np.float32)
+    noise = rng.standard_normal((2, lat, lat, 4)).astype(np.float32)
+    t0 = time.perf_counter()
+    z = vae_ref.encode(wv, img, noise)
+    vae_ref.decode(wv, z[:1])
+    t_vae = time.perf_counter() - t0
+    x = rng.standard_normal((2, lat, lat, 9)).astype(np.float32)
     for _ in range(args.warmup):
-        step()
+        unet_ref.forward(wu, x, 900, [0, 1], ehs)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
-    elems = int(np.prod(CPU_SAMPLE))
-    value = sum(BYTES_PER_ELT.values()) * elems / dt / 1e9
-    sample = (f"each step: the same 4-op step on {list(CPU_SAMPLE)} (a bounded sample of the "
-              f"{list(SHAPE)} workload); oracle/ref_engine.cpp, the C++ restatement of the reference's "
-              "Rust kernels (the Rust crate cannot be built here: no cargo)")
-    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) NHWC f32)", "config": config(args),
-            "impl": "reference",
-            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+        unet_ref.forward(wu, x, 900, [0, 1], ehs)
+    t_step = (time.perf_counter() - t0) / args.steps
+    per = 19 * t_step + t_vae
+    value = 1.0 / per
+    sample = (f"each step: one UNet CFG step at batch 2 ({t_step:.2f} s) of a {side}x{side} inpaint; VAE encode of 2 "
+              f"images + decode of 1 timed once ({t_vae:.2f} s); inpaints/s = 1 / (19 x step + VAE); oracle/ "
+              "(C++ + OpenMP restatement of the reference's Rust engine: cargo is absent, the crate cannot be built)")
+    line = {"metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded inputs, random-init weights)", "config": config(args), "impl": "reference",
+            "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": sample},
-            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=8, help="inpaints per GPU per step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-conv", action="store_true")
+    ap.add_argument("--skip-sweep", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-vae", action="store_true")
     ap.add_argument("--small", action="store_true",
-                    help="profiling case: [1,256,256,512] sweep (128 MiB, above L2) and a [1,128,128,512] conv")
+                    help="profiling case: a scaled-down network (64/128/256, 128x128 images) and small sweeps")
     args = ap.parse_args()
-    if args.small:
-        global SHAPE, CONV_SHAPE
-        SHAPE = (1, 256, 256, 512)
-        CONV_SHAPE = (1, 128, 128, 512, 512)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -66,6 +66,9 @@ void mbx_engine_destroy(mbx_engine *engine);
 /* Runs the engine's work on `stream` (a cudaStream_t; NULL = its own stream). */
 int32_t mbx_engine_set_stream(mbx_engine *engine, void *stream);
 
+/* Kernels this engine has launched so far (graph replays count every kernel in the graph). */
+uint64_t mbx_engine_launch_count(const mbx_engine *engine);
+
 /* latent side, model image side and the three UNet level widths. */
 int32_t mbx_engine_info(const mbx_engine *engine, int64_t *latent_side, int64_t *image_side, int64_t widths[3]);
 

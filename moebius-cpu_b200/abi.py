@@ -128,6 +128,7 @@ SIGNATURES = {
     "mbx_engine_destroy": (None, [_vp]),
     "mbx_engine_set_stream": (_i32, [_vp, _vp]),
     "mbx_engine_info": (_i32, [_vp, _pi64, _pi64, _pi64]),
+    "mbx_engine_launch_count": (_u64, [_vp]),
     "mbx_inpaint": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, ctypes.POINTER(InpaintParams), PROGRESS_FN,
                            _vp, ctypes.POINTER(Rect)]),
     "mbx_inpaint_batch": (_i32, [_vp, _vp, _vp, _i64, _u32, _u32, ctypes.POINTER(InpaintParams), _vp, _vp, _vp,

@@ -430,6 +430,8 @@ int32_t mbx_engine_set_stream(mbx_engine* engine, void* stream) {
     });
 }
 
+uint64_t mbx_engine_launch_count(const mbx_engine* engine) { return engine && engine->ctx ? engine->ctx->launches : 0; }
+
 int32_t mbx_engine_info(const mbx_engine* engine, int64_t* latent_side, int64_t* image_side, int64_t widths[3]) {
     return eguard([&] {
         require_engine(engine);

@@ -50,6 +50,10 @@ class Engine:
     def __exit__(self, *exc):
         self.close()
 
+    @property
+    def launch_count(self) -> int:
+        return int(lib().mbx_engine_launch_count(self.handle))
+
     def set_stream(self, stream_ptr: Optional[int]) -> None:
         check(lib().mbx_engine_set_stream(self.handle, ctypes.c_void_p(stream_ptr or 0)))
 

@@ -269,3 +269,26 @@ def write_weights_dir(path: str, seed: int = 0, f16: bool = True, unet_widths=UN
     write_safetensors(os.path.join(path, "vae.safetensors"), random_weights(vae_shapes(vae_widths), seed + 1, f16),
                       {"format": "moebius-cpu/1", "dtype": dtype, "scaling_factor": SCALING_FACTOR})
     return path
+
+
+def ellipse_masks(rng, n: int, side: int = 512, lo: float = 0.10, hi: float = 0.40) -> np.ndarray:
+    """n binary masks [n, side, side] (0 / 255): unions of random filled ellipses covering a
+    fraction in [lo, hi] of the image (BASELINE config 5's mask distribution)."""
+    yy, xx = np.mgrid[:side, :side].astype(np.float32)
+    out = np.zeros((n, side, side), np.uint8)
+    for i in range(n):
+        while True:
+            m = np.zeros((side, side), bool)
+            target = rng.uniform(lo, hi)
+            while m.mean() < target:
+                cy, cx = rng.uniform(0, side, 2)
+                ry, rx = rng.uniform(side * 0.05, side * 0.3, 2)
+                th = rng.uniform(0, np.pi)
+                dy, dx = yy - cy, xx - cx
+                u = (dx * np.cos(th) + dy * np.sin(th)) / rx
+                v = (-dx * np.sin(th) + dy * np.cos(th)) / ry
+                m |= u * u + v * v <= 1.0
+            if lo <= m.mean() <= hi:
+                out[i] = m * 255
+                break
+    return out
