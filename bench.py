@@ -253,7 +253,7 @@ def tf32_peak(torch):
 
 def bench_conv(mbx, ctx, torch, dev, small):
     """The tcgen05 implicit-GEMM conv on the conv sweep's largest 3×3 shape (f16 and f32 weights)."""
-    cn, chh, cww, cci, cco = (1, 128, 128, 512, 512) if small else CONV_SHAPE
+    cn, chh, cww, cci, cco = CONV_SHAPE
     gen = torch.Generator(device=dev).manual_seed(7)
     cx = torch.randn(cn, chh, cww, cci, device=dev, generator=gen)
     cy = torch.empty(cn, chh, cww, cco, device=dev)
@@ -362,12 +362,15 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     mbx = importlib.import_module("moebius-cpu_b200")
     side = 128 if args.small else SIDE
-    wdir = weights_dir(rank, dist, args.small)
-    eng = mbx.engine.Engine(wdir, local)
     # One explicit stream for torch's events and the engine's kernels.
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
-    eng.set_stream(stream.cuda_stream)
+    eng = None
+    if not (args.skip_inpaint and args.skip_vae):
+        eng = mbx.engine.Engine(weights_dir(rank, dist, args.small), local)
+        eng.set_stream(stream.cuda_stream)
+    if args.skip_inpaint:
+        return run_secondary_only(args, mbx, torch, dev, eng, stream, world, rank, dist)
     n = args.batch
     img, masks, nv, ni, no = synthetic_inputs(rank, n, side)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
@@ -506,6 +509,28 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_secondary_only(args, mbx, torch, dev, eng, stream, world, rank, dist):
+    """--skip-inpaint: only the kernel-level measurements (profiling cases); no headline value."""
+    hbm, peak_kind = peaks()
+    out = {"metric": METRIC, "value": None, "unit": UNIT, "n_gpus": world, "note": "--skip-inpaint: kernel cases only"}
+    if rank == 0:
+        ctxm = mbx.Context(dev.index)
+        ctxm.set_stream(stream.cuda_stream)
+        if not args.skip_conv:
+            out["conv"] = bench_conv(mbx, ctxm, torch, dev, args.small)
+        if not args.skip_sweep:
+            out["memory_sweep"] = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm)
+        if not args.skip_vae:
+            out["vae_decoder"] = bench_vae_decoder(eng, torch, dev, (128 if args.small else SIDE) // 8)
+        ctxm.close()
+        print(json.dumps(out), flush=True)
+    if eng:
+        eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU path, restated by the oracle (the Rust crate cannot be built here),
@@ -568,9 +593,16 @@ def main():
     ap.add_argument("--skip-sweep", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-vae", action="store_true")
+    ap.add_argument("--skip-inpaint", action="store_true", help="kernel-level measurements only")
+    ap.add_argument("--conv-shape", default=None, help="n,h,w,c_in,c_out of the conv measurement")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a scaled-down network (64/128/256, 128x128 images) and small sweeps")
     args = ap.parse_args()
+    global CONV_SHAPE
+    if args.conv_shape:
+        CONV_SHAPE = tuple(int(v) for v in args.conv_shape.split(","))
+    elif args.small:
+        CONV_SHAPE = (1, 128, 128, 512, 512)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
