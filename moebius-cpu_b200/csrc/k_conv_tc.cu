@@ -215,15 +215,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Nearest TF32 value (ties away from zero: cvt.rna), returned as an f32 whose
-// low 13 mantissa bits are zero, so the tensor core reads it exactly. Rounding
-// (not truncation) keeps the split errors unbiased; truncation biases every
-// product toward zero and the bias grows linearly with K.
-__device__ __forceinline__ float tf32_rn(float v) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-    return __uint_as_float(r);
-}
+// The A-operand split: the tensor core reads an f32 operand as TF32 by dropping
+// its 13 low mantissa bits, so the raw value serves as the high part and
+// v − trunc_tf32(v) (exact in f32) as the low part. The two truncated parts
+// carry v to within 2^-21 relative, one-signed per element; summed over
+// products of either sign the error of a K-long dot product stays near 2^-22
+// of Σ|a·w| (a CPU simulation at K up to 11520 gives ≤ 1e-8), far below the
+// f32 accumulation error, and costs two integer/FP ops instead of two cvt.
+__device__ __forceinline__ float tf32_split_lo(float v) { return v - __uint_as_float(__float_as_uint(v) & 0xffffe000u); }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -452,13 +451,13 @@ __global__ void __maxnreg__(128)
                     }
                 }
             }
-            float h[32];
+            // High part: the value itself (the tensor core reads its TF32 truncation); low part:
+            // v − trunc_tf32(v), exact in f32 (again read truncated). See tf32_split_lo.
+            tmem_st32(lane_base + a_col(a), v);  // v stays untouched until the wait below
+            float lo[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) h[e] = tf32_rn(v[e]);
-            tmem_st32(lane_base + a_col(a), h);  // h stays untouched until the wait below
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = tf32_rn(v[e] - h[e]);
-            tmem_st32(lane_base + a_col(a) + 32u, v);
+            for (int e = 0; e < 32; ++e) lo[e] = tf32_split_lo(v[e]);
+            tmem_st32(lane_base + a_col(a) + 32u, lo);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(a_full_bar(a));
@@ -466,29 +465,33 @@ __global__ void __maxnreg__(128)
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
+            // The tensor pipe queues almost nothing ahead, so every cycle this thread spends
+            // between MMAs is a pipe bubble: ring positions and phases advance incrementally
+            // (no division), descriptors step by their 16-byte address units.
             const uint32_t idesc = idesc_tf32(bn);
+            int s = 0, sphase = 0, a = 0, aphase = 0, seg = 0, kin = 0;
             for (int kc = 0; kc < K; ++kc) {
-                const int s = kc % bstages, a = kc % astages;
-                const int seg = kc / kSegChunks, b = seg & 1;
-                const bool seg_first = kc % kSegChunks == 0;
-                const bool seg_last = (kc + 1) % kSegChunks == 0 || kc + 1 == K;
+                const int b = seg & 1;
+                const bool seg_first = kin == 0;
+                const bool seg_last = kin == kSegChunks - 1 || kc + 1 == K;
                 if (seg_first &&
                     !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true))
                     break;
-                if (!mbar_wait(b_full_bar(s), (kc / bstages) & 1, args.err, 3, abort_flag, true)) break;
-                if (!mbar_wait(a_full_bar(a), (kc / astages) & 1, args.err, 10, abort_flag, true)) break;
+                if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true)) break;
+                if (!mbar_wait(a_full_bar(a), (uint32_t)aphase, args.err, 10, abort_flag, true)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * bn);
                 const uint32_t ah = tmem + a_col(a), al = ah + 32u;
                 const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
-                const uint32_t b_lo = b_hi + b_bytes;
+                const uint64_t bdh0 = sw128_desc(b_hi);
+                const uint64_t bdl0 = sw128_desc(b_hi + b_bytes);
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint64_t bdh = sw128_desc(b_hi + (uint32_t)kk * 32u);
+                    const uint64_t bdh = bdh0 + (uint64_t)(2 * kk);  // + kk·32 bytes
                     const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
                     const uint32_t ko = (uint32_t)kk * 8u;
                     if constexpr (F32W) {
-                        const uint64_t bdl = sw128_desc(b_lo + (uint32_t)kk * 32u);
+                        const uint64_t bdl = bdl0 + (uint64_t)(2 * kk);
                         mma_tf32_ts(d, al + ko, bdh, idesc, acc);
                         mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
                         mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
@@ -500,6 +503,18 @@ __global__ void __maxnreg__(128)
                 mma_commit(b_empty_bar(s));
                 mma_commit(a_empty_bar(a));
                 if (seg_last) mma_commit(acc_full_bar(b));
+                if (++s == bstages) {
+                    s = 0;
+                    sphase ^= 1;
+                }
+                if (++a == astages) {
+                    a = 0;
+                    aphase ^= 1;
+                }
+                if (++kin == kSegChunks) {
+                    kin = 0;
+                    ++seg;
+                }
             }
             if (*abort_flag) {
                 // Do not let TMEM be freed under MMAs that are still running.
