@@ -66,6 +66,7 @@ struct ConvArgs {
     int cin_chunks, k_chunks;
     int flat;  // 1×1 conv: input pixel = output pixel (no padding, stride or upsample)
     int c_out, bn, n_tiles, stages, a_stages, tmem_cols;
+    int64_t tiles;  // m tiles × n tiles
     const float* bias;
     const float* residual;
     float* out;
@@ -287,12 +288,14 @@ __global__ void __maxnreg__(128)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tile = blockIdx.x % args.n_tiles;
-    const int64_t m_tile = blockIdx.x / args.n_tiles;
-    const int64_t m0 = m_tile * BM;
-    const int n0 = n_tile * bn;
     const int K = args.k_chunks;
     const int nseg = (K + kSegChunks - 1) / kSegChunks;
+    // Persistent CTA: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (N tile fastest, so the CTAs
+    // in flight share A rows through L2). Every ring keeps its position and phase across tiles,
+    // so the next tile's loads and MMAs overlap this tile's epilogue.
+    const int64_t tiles = args.tiles;
+    auto tile_m0 = [&](int64_t t) { return (t / args.n_tiles) * (int64_t)BM; };
+    auto tile_n0 = [&](int64_t t) { return (int)(t % args.n_tiles) * bn; };
     // TMEM columns: accumulators [0, 2·bn), A stage a at 2·bn + 64·a (32 columns of TF32
     // high parts, then 32 of low parts; lane = tile row).
     auto a_col = [&](int a) { return (uint32_t)(2 * bn + 64 * a); };
@@ -331,7 +334,7 @@ __global__ void __maxnreg__(128)
     const int64_t hw_out = (int64_t)args.ho * args.wo;
     // Row geometry: item index and the top-left input tap packed as (iy0 << 16) | (ix0 & 0xffff);
     // rows past the end get an iy0 far outside the image, so every tap reads as padding.
-    auto row_geo = [&](int r, int& pb, int& geo) {
+    auto row_geo = [&](int64_t m0, int r, int& pb, int& geo) {
         const int64_t m = m0 + r;
         const bool valid = m < args.m_total;
         const int64_t mm = valid ? m : 0;
@@ -345,7 +348,7 @@ __global__ void __maxnreg__(128)
         geo = (int)(((uint32_t)iy0 << 16) | ((uint32_t)ix0 & 0xffffu));
     };
     // Spatial validity and input pixel index of row r's tap (ky, kx).
-    auto tap_pixel = [&](int r, int pb, int geo, int ky, int kx, bool& ok) -> int64_t {
+    auto tap_pixel = [&](int64_t m0, int r, int pb, int geo, int ky, int kx, bool& ok) -> int64_t {
         if constexpr (FLAT) {
             const int64_t pix = m0 + r;
             ok = pix < args.m_total;
@@ -365,102 +368,138 @@ __global__ void __maxnreg__(128)
         const int tid = threadIdx.x;
         const int j = tid & 7;       // 16-byte chunk (4 channels) of the 128-byte row
         const int rbase = tid >> 3;  // rows rbase + 16·i
-        int pb[8], geo[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            pb[i] = 0;
-            geo[i] = 0;
-            if constexpr (!FLAT) row_geo(rbase + 16 * i, pb[i], geo[i]);
-        }
-        for (int kc = 0; kc < K; ++kc) {
-            const int q = kc % kStgSlots;
-            if (!mbar_wait(sempty_bar(q), ((kc / kStgSlots) & 1) ^ 1, args.err, 8, abort_flag, true)) break;
-            const int tap = kc / args.cin_chunks;
-            const int c0 = (kc - tap * args.cin_chunks) * BK + 4 * j;
-            const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-            const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+        int q = 0, qphase = 0;
+        bool live = true;
+        for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+            const int64_t m0 = tile_m0(t);
+            int pb[8], geo[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const int r = rbase + 16 * i;
-                const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
-                bool ok;
-                const int64_t pix = tap_pixel(r, pb[i], geo[i], ky, kx, ok);
-                if constexpr (VEC4) {
-                    const bool in = ok && c0 < args.c_in;
-                    cp_async_16(stg + off, in ? (const void*)(args.x + pix * args.c_in + c0) : (const void*)args.x,
-                                in ? 16u : 0u);
-                } else {
+                pb[i] = 0;
+                geo[i] = 0;
+                if constexpr (!FLAT) row_geo(m0, rbase + 16 * i, pb[i], geo[i]);
+            }
+            int tap = 0, cchunk = 0;
+            for (int kc = 0; kc < K; ++kc) {
+                if (!mbar_wait(sempty_bar(q), (uint32_t)(qphase ^ 1), args.err, 8, abort_flag, true)) {
+                    live = false;
+                    break;
+                }
+                const int c0 = cchunk * BK + 4 * j;
+                const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const bool in = ok && c0 + e < args.c_in;
-                        cp_async_4(stg + off + 4u * e,
-                                   in ? (const void*)(args.x + pix * args.c_in + c0 + e) : (const void*)args.x,
-                                   in ? 4u : 0u);
+                for (int i = 0; i < 8; ++i) {
+                    const int r = rbase + 16 * i;
+                    const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
+                    bool ok;
+                    const int64_t pix = tap_pixel(m0, r, pb[i], geo[i], ky, kx, ok);
+                    if constexpr (VEC4) {
+                        const bool in = ok && c0 < args.c_in;
+                        cp_async_16(stg + off,
+                                    in ? (const void*)(args.x + pix * args.c_in + c0) : (const void*)args.x,
+                                    in ? 16u : 0u);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const bool in = ok && c0 + e < args.c_in;
+                            cp_async_4(stg + off + 4u * e,
+                                       in ? (const void*)(args.x + pix * args.c_in + c0 + e) : (const void*)args.x,
+                                       in ? 4u : 0u);
+                        }
                     }
                 }
+                cp_async_mbar_arrive(sfull_bar(q));
+                if (++q == kStgSlots) {
+                    q = 0;
+                    qphase ^= 1;
+                }
+                if (++cchunk == args.cin_chunks) {
+                    cchunk = 0;
+                    ++tap;
+                }
             }
-            cp_async_mbar_arrive(sfull_bar(q));
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
     } else if (warp >= 10) {
         // ------------------------------------------------------------ converters
         // One tile row per thread (its TMEM lane): staging row → [SiLU](x·scale + shift) at a
         // spatially valid tap (padding stays zero; channel padding beyond c_in meets zero
-        // weights) → TF32-rounded high and low parts written to the A stage in TMEM.
+        // weights) → TF32 high and low parts written to the A stage in TMEM.
         const int qd = warp & 3;
         const int r = qd * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
-        int pb = 0, geo = 0;
-        if constexpr (!FLAT) row_geo(r, pb, geo);
         const bool pro = args.pro_scale != nullptr;
-        if constexpr (FLAT) {
-            // 1×1: the row's item selects the prologue's per-item scale / shift.
-            const int64_t m = m0 + r;
-            pb = m < args.m_total ? (int)(m / hw_out) : 0;
-        }
-        for (int kc = 0; kc < K; ++kc) {
-            const int q = kc % kStgSlots, a = kc % astages;
-            if (!mbar_wait(sfull_bar(q), (kc / kStgSlots) & 1, args.err, 9, abort_flag, true)) break;
-            if (!mbar_wait(a_empty_bar(a), ((kc / astages) & 1) ^ 1, args.err, 1, abort_flag, true)) break;
-            const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
-            float v[32];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                const float4 f = ld_shared_v4(stg + ((uint32_t)(jj ^ (r & 7)) << 4));
-                v[4 * jj] = f.x;
-                v[4 * jj + 1] = f.y;
-                v[4 * jj + 2] = f.z;
-                v[4 * jj + 3] = f.w;
+        int q = 0, qphase = 0, a = 0, aphase = 0;
+        bool live = true;
+        for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+            const int64_t m0 = tile_m0(t);
+            int pb = 0, geo = 0;
+            if constexpr (FLAT) {
+                // 1×1: the row's item selects the prologue's per-item scale / shift.
+                const int64_t m = m0 + r;
+                pb = m < args.m_total ? (int)(m / hw_out) : 0;
+            } else {
+                row_geo(m0, r, pb, geo);
             }
-            mbar_arrive(sempty_bar(q));  // the staging row is in registers
-            if (pro) {
-                const int tap = kc / args.cin_chunks;
-                const int cb = (kc - tap * args.cin_chunks) * BK;
-                bool ok;
-                (void)tap_pixel(r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
-                if (ok) {
-                    const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
-                    const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
+            int tap = 0, cchunk = 0;
+            for (int kc = 0; kc < K; ++kc) {
+                if (!mbar_wait(sfull_bar(q), (uint32_t)qphase, args.err, 9, abort_flag, true) ||
+                    !mbar_wait(a_empty_bar(a), (uint32_t)(aphase ^ 1), args.err, 1, abort_flag, true)) {
+                    live = false;
+                    break;
+                }
+                const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
+                float v[32];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (cb + e < args.c_in) {
-                            float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
-                            if (args.pro_silu) y = dev_silu(y);
-                            v[e] = y;
+                for (int jj = 0; jj < 8; ++jj) {
+                    const float4 f = ld_shared_v4(stg + ((uint32_t)(jj ^ (r & 7)) << 4));
+                    v[4 * jj] = f.x;
+                    v[4 * jj + 1] = f.y;
+                    v[4 * jj + 2] = f.z;
+                    v[4 * jj + 3] = f.w;
+                }
+                mbar_arrive(sempty_bar(q));  // the staging row is in registers
+                if (pro) {
+                    const int cb = cchunk * BK;
+                    bool ok;
+                    (void)tap_pixel(m0, r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
+                    if (ok) {
+                        const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
+                        const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            if (cb + e < args.c_in) {
+                                float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
+                                if (args.pro_silu) y = dev_silu(y);
+                                v[e] = y;
+                            }
                         }
                     }
                 }
-            }
-            // High part: the value itself (the tensor core reads its TF32 truncation); low part:
-            // v − trunc_tf32(v), exact in f32 (again read truncated). See tf32_split_lo.
-            tmem_st32(lane_base + a_col(a), v);  // v stays untouched until the wait below
-            float lo[32];
+                // High part: the value itself (the tensor core reads its TF32 truncation); low part:
+                // v − trunc_tf32(v), exact in f32 (again read truncated). See tf32_split_lo.
+                tmem_st32(lane_base + a_col(a), v);  // v stays untouched until the wait below
+                float lo[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) lo[e] = tf32_split_lo(v[e]);
-            tmem_st32(lane_base + a_col(a) + 32u, lo);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(a_full_bar(a));
+                for (int e = 0; e < 32; ++e) lo[e] = tf32_split_lo(v[e]);
+                tmem_st32(lane_base + a_col(a) + 32u, lo);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(a_full_bar(a));
+                if (++q == kStgSlots) {
+                    q = 0;
+                    qphase ^= 1;
+                }
+                if (++a == astages) {
+                    a = 0;
+                    aphase ^= 1;
+                }
+                if (++cchunk == args.cin_chunks) {
+                    cchunk = 0;
+                    ++tap;
+                }
+            }
         }
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
@@ -469,51 +508,62 @@ __global__ void __maxnreg__(128)
             // between MMAs is a pipe bubble: ring positions and phases advance incrementally
             // (no division), descriptors step by their 16-byte address units.
             const uint32_t idesc = idesc_tf32(bn);
-            int s = 0, sphase = 0, a = 0, aphase = 0, seg = 0, kin = 0;
-            for (int kc = 0; kc < K; ++kc) {
-                const int b = seg & 1;
-                const bool seg_first = kin == 0;
-                const bool seg_last = kin == kSegChunks - 1 || kc + 1 == K;
-                if (seg_first &&
-                    !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true))
-                    break;
-                if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true)) break;
-                if (!mbar_wait(a_full_bar(a), (uint32_t)aphase, args.err, 10, abort_flag, true)) break;
-                tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(b * bn);
-                const uint32_t ah = tmem + a_col(a), al = ah + 32u;
-                const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
-                const uint64_t bdh0 = sw128_desc(b_hi);
-                const uint64_t bdl0 = sw128_desc(b_hi + b_bytes);
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint64_t bdh = bdh0 + (uint64_t)(2 * kk);  // + kk·32 bytes
-                    const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
-                    const uint32_t ko = (uint32_t)kk * 8u;
-                    if constexpr (F32W) {
-                        const uint64_t bdl = bdl0 + (uint64_t)(2 * kk);
-                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
-                        mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
-                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
-                    } else {
-                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
-                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
+            int s = 0, sphase = 0, a = 0, aphase = 0, seg = 0;
+            bool live = true;
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+                int kin = 0;
+                for (int kc = 0; kc < K; ++kc) {
+                    const int b = seg & 1;
+                    const bool seg_first = kin == 0;
+                    const bool seg_last = kin == kSegChunks - 1 || kc + 1 == K;
+                    if (seg_first &&
+                        !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true)) {
+                        live = false;
+                        break;
                     }
-                }
-                mma_commit(b_empty_bar(s));
-                mma_commit(a_empty_bar(a));
-                if (seg_last) mma_commit(acc_full_bar(b));
-                if (++s == bstages) {
-                    s = 0;
-                    sphase ^= 1;
-                }
-                if (++a == astages) {
-                    a = 0;
-                    aphase ^= 1;
-                }
-                if (++kin == kSegChunks) {
-                    kin = 0;
-                    ++seg;
+                    if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true) ||
+                        !mbar_wait(a_full_bar(a), (uint32_t)aphase, args.err, 10, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)(b * bn);
+                    const uint32_t ah = tmem + a_col(a), al = ah + 32u;
+                    const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
+                    const uint64_t bdh0 = sw128_desc(b_hi);
+                    const uint64_t bdl0 = sw128_desc(b_hi + b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint64_t bdh = bdh0 + (uint64_t)(2 * kk);  // + kk·32 bytes
+                        const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
+                        const uint32_t ko = (uint32_t)kk * 8u;
+                        if constexpr (F32W) {
+                            const uint64_t bdl = bdl0 + (uint64_t)(2 * kk);
+                            mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                            mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
+                            mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
+                        } else {
+                            mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                            mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
+                        }
+                    }
+                    mma_commit(b_empty_bar(s));
+                    mma_commit(a_empty_bar(a));
+                    if (seg_last) mma_commit(acc_full_bar(b));
+                    if (++s == bstages) {
+                        s = 0;
+                        sphase ^= 1;
+                    }
+                    if (++a == astages) {
+                        a = 0;
+                        aphase ^= 1;
+                    }
+                    if (seg_last) {
+                        kin = 0;
+                        ++seg;
+                    } else {
+                        ++kin;
+                    }
                 }
             }
             if (*abort_flag) {
@@ -526,83 +576,103 @@ __global__ void __maxnreg__(128)
     } else if (warp == 5) {
         // ------------------------------------------------------------ TMA issuer
         if (lane == 0) {
-            for (int kc = 0; kc < K; ++kc) {
-                const int s = kc % bstages;
-                if (!mbar_wait(b_empty_bar(s), ((kc / bstages) & 1) ^ 1, args.err, 4, abort_flag, true)) break;
-                const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
-                mbar_arrive_expect_tx(b_full_bar(s), bstage_bytes);
-                tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, b_full_bar(s));
-                if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, b_full_bar(s));
+            int s = 0, sphase = 0;
+            bool live = true;
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+                const int n0 = tile_n0(t);
+                for (int kc = 0; kc < K; ++kc) {
+                    if (!mbar_wait(b_empty_bar(s), (uint32_t)(sphase ^ 1), args.err, 4, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
+                    mbar_arrive_expect_tx(b_full_bar(s), bstage_bytes);
+                    tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, b_full_bar(s));
+                    if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, b_full_bar(s));
+                    if (++s == bstages) {
+                        s = 0;
+                        sphase ^= 1;
+                    }
+                }
             }
         }
         __syncwarp();
     } else if (warp >= 6 && warp < 10) {
         // ------------------------------------------------------------ drain + epilogue
-        const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const int row = q * 32 + lane;
-        const int64_t m = m0 + row;
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const int qd = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row = qd * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
         const uint32_t srow = sum_base + (uint32_t)row * sum_stride;
         const bool vec_out = (args.c_out & 3) == 0;
-        for (int seg = 0; seg < nseg; ++seg) {
-            const int b = seg & 1;
-            if (!mbar_wait(acc_full_bar(b), (seg >> 1) & 1, args.err, 6, abort_flag, true)) break;
-            tc_fence_after();
-            const bool last = seg + 1 == nseg;
-            for (int cc = 0; cc < bn; cc += 32) {
-                float acc[32];
-                tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
-                if (seg > 0) {
-#pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        const float4 r4 = ld_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u);
-                        acc[4 * v] = r4.x + acc[4 * v];
-                        acc[4 * v + 1] = r4.y + acc[4 * v + 1];
-                        acc[4 * v + 2] = r4.z + acc[4 * v + 2];
-                        acc[4 * v + 3] = r4.w + acc[4 * v + 3];
-                    }
+        int gseg = 0;
+        bool live = true;
+        for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+            const int64_t m = tile_m0(t) + row;
+            const int n0 = tile_n0(t);
+            for (int seg = 0; seg < nseg; ++seg, ++gseg) {
+                const int b = gseg & 1;
+                if (!mbar_wait(acc_full_bar(b), (gseg >> 1) & 1, args.err, 6, abort_flag, true)) {
+                    live = false;
+                    break;
                 }
-                if (!last) {
+                tc_fence_after();
+                const bool last = seg + 1 == nseg;
+                for (int cc = 0; cc < bn; cc += 32) {
+                    float acc[32];
+                    tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
+                    if (seg > 0) {
 #pragma unroll
-                    for (int v = 0; v < 8; ++v)
-                        st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1], acc[4 * v + 2],
-                                     acc[4 * v + 3]);
-                    continue;
-                }
-                if (m >= args.m_total) continue;
-                const int nb = n0 + cc;
-                if (nb >= args.c_out) continue;
-                float* dst = args.out + m * args.c_out + nb;
-                const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
-                if (vec_out && nb + 32 <= args.c_out) {
-#pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + v)
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (res) {
-                            const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
-                            pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
-                        }
-                        float4 o4 = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1],
-                                                pre.z + acc[4 * v + 2], pre.w + acc[4 * v + 3]);
-                        if (args.act) o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
-                        reinterpret_cast<float4*>(dst)[v] = o4;
-                    }
-                } else {
-                    const int lim = min(32, args.c_out - nb);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (i < lim) {
-                            float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
-                            if (res) pre = __ldg(res + i) + pre;
-                            const float o = pre + acc[i];
-                            dst[i] = args.act ? dev_silu(o) : o;
+                        for (int v = 0; v < 8; ++v) {
+                            const float4 r4 = ld_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u);
+                            acc[4 * v] = r4.x + acc[4 * v];
+                            acc[4 * v + 1] = r4.y + acc[4 * v + 1];
+                            acc[4 * v + 2] = r4.z + acc[4 * v + 2];
+                            acc[4 * v + 3] = r4.w + acc[4 * v + 3];
                         }
                     }
+                    if (!last) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1],
+                                         acc[4 * v + 2], acc[4 * v + 3]);
+                        continue;
+                    }
+                    if (m >= args.m_total) continue;
+                    const int nb = n0 + cc;
+                    if (nb >= args.c_out) continue;
+                    float* dst = args.out + m * args.c_out + nb;
+                    const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
+                    if (vec_out && nb + 32 <= args.c_out) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + v)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (res) {
+                                const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
+                                pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
+                            }
+                            float4 o4 = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1],
+                                                    pre.z + acc[4 * v + 2], pre.w + acc[4 * v + 3]);
+                            if (args.act)
+                                o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                            reinterpret_cast<float4*>(dst)[v] = o4;
+                        }
+                    } else {
+                        const int lim = min(32, args.c_out - nb);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (i < lim) {
+                                float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
+                                if (res) pre = __ldg(res + i) + pre;
+                                const float o = pre + acc[i];
+                                dst[i] = args.act ? dev_silu(o) : o;
+                            }
+                        }
+                    }
                 }
+                tc_fence_before();
+                mbar_arrive(acc_empty_bar(b));  // the accumulator has been read into registers
             }
-            tc_fence_before();
-            mbar_arrive(acc_empty_bar(b));  // the accumulator has been read into registers
         }
     }
     tc_fence_before();
@@ -661,7 +731,9 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_til
                                        " threads");
         configured = true;
     }
-    const int64_t blocks = m_tiles * a.n_tiles;
+    (void)m_tiles;
+    // Persistent: one CTA per SM (the shared-memory footprint allows one), tiles strided over them.
+    const int64_t blocks = std::min<int64_t>(a.tiles, (int64_t)ctx->sm_count);
     kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, a);
 }
 
@@ -725,7 +797,8 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.err = ctx->dev_err;
     MBX_REQUIRE(a.m_total < (int64_t(1) << 40), "conv: too many output pixels");
     const int64_t m_tiles = (a.m_total + BM - 1) / BM;
-    MBX_REQUIRE(m_tiles * a.n_tiles < (int64_t(1) << 31), "conv: grid too large");
+    MBX_REQUIRE(m_tiles * a.n_tiles < (int64_t(1) << 40), "conv: too many tiles");
+    a.tiles = m_tiles * a.n_tiles;
     const bool vec4 = (s.c_in & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                       (!pro_scale || ((reinterpret_cast<uintptr_t>(pro_scale) & 15) == 0 &&
                                       (reinterpret_cast<uintptr_t>(pro_shift) & 15) == 0));
