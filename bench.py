@@ -369,6 +369,8 @@ def run_ours(args):
     if not (args.skip_inpaint and args.skip_vae):
         eng = mbx.engine.Engine(weights_dir(rank, dist, args.small), local)
         eng.set_stream(stream.cuda_stream)
+    if args.component:
+        return run_component(args, mbx, torch, dev, eng, world, rank, dist)
     if args.skip_inpaint:
         return run_secondary_only(args, mbx, torch, dev, eng, stream, world, rank, dist)
     n = args.batch
@@ -465,6 +467,12 @@ def run_ours(args):
             for ptr, _ in hosts.values():
                 mbx.Context.host_free(ptr)
 
+    components = None
+    if rank == 0 and not args.skip_components:
+        components = {k: round(component_ms(eng, torch, dev, k, n, side // 8, 2, 3), 2)
+                      for k in ("unet", "vae_encode", "vae_decode")}
+        components["note"] = (f"ms per call at the step's batch: one UNet step at batch {2 * n} (eager, no graph), "
+                              f"VAE encode of {2 * n} images, decode of {n}")
     hbm, peak_kind = peaks()
     conv = sweep = vae_line = None
     if rank == 0:
@@ -496,13 +504,63 @@ def run_ours(args):
             "config": config(args),
             "implied_tflops": round(value * INPAINT_TFLOP, 1),
             "roofline": roof, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-            "result_changed_pixel_frac": round(changed, 4),
+            "result_changed_pixel_frac": round(changed, 4), "components_ms": components,
             "conv": conv, "memory_sweep": sweep, "vae_decoder": vae_line,
             "hbm_peak_gbs": hbm, "hbm_peak_kind": peak_kind,
         }
         if not args.skip_cpu:
             line["cpu_baseline"] = cpu_inpaint_baseline(args.small)
         print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def component_ms(eng, torch, dev, name, n, latent, warmup, steps, nvtx=False):
+    """Device time of one pipeline component at the headline batch: the UNet step at batch 2n
+    (eager, no graph), the VAE encode of 2n images or the VAE decode of n latents."""
+    gen = torch.Generator(device=dev).manual_seed(5)
+    side = latent * 8
+    if name == "unet":
+        x = torch.randn(2 * n, latent, latent, 9, device=dev, generator=gen)
+        y = torch.empty(2 * n, latent, latent, 4, device=dev)
+        call = lambda: eng.unet_forward(x.data_ptr(), 2 * n, 900, True, y.data_ptr())  # noqa: E731
+    elif name == "vae_encode":
+        x = torch.rand(2 * n, side, side, 3, device=dev, generator=gen) * 2 - 1
+        z = torch.randn(2 * n, latent, latent, 4, device=dev, generator=gen)
+        y = torch.empty(2 * n, latent, latent, 4, device=dev)
+        call = lambda: eng.vae_encode(x.data_ptr(), z.data_ptr(), 2 * n, side, side, y.data_ptr())  # noqa: E731
+    else:
+        x = torch.randn(n, latent, latent, 4, device=dev, generator=gen) * 0.13025
+        y = torch.empty(n, side, side, 3, device=dev)
+        call = lambda: eng.vae_decode(x.data_ptr(), n, latent, latent, y.data_ptr())  # noqa: E731
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for i in range(steps):
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if nvtx and i == steps - 1:
+            torch.cuda.nvtx.range_push(name)
+        s_ev.record()
+        call()
+        e_ev.record()
+        if nvtx and i == steps - 1:
+            torch.cuda.nvtx.range_pop()
+        e_ev.synchronize()
+        tot += s_ev.elapsed_time(e_ev)
+    return tot / steps
+
+
+def run_component(args, mbx, torch, dev, eng, world, rank, dist):
+    """--component NAME: one pipeline component alone (profiling case; the last timed call is
+    wrapped in an NVTX range named NAME for ncu --nvtx-include)."""
+    latent = (128 if args.small else SIDE) // 8
+    ms = component_ms(eng, torch, dev, args.component, args.batch, latent, args.warmup, args.steps, nvtx=True)
+    if rank == 0:
+        print(json.dumps({"component": args.component, "batch_inpaints": args.batch, "ms": round(ms, 3),
+                          "n_gpus": world}), flush=True)
     eng.close()
     if dist:
         dist.barrier()
@@ -594,6 +652,9 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-vae", action="store_true")
     ap.add_argument("--skip-inpaint", action="store_true", help="kernel-level measurements only")
+    ap.add_argument("--skip-components", action="store_true")
+    ap.add_argument("--component", choices=["unet", "vae_encode", "vae_decode"], default=None,
+                    help="time one pipeline component alone (profiling case)")
     ap.add_argument("--conv-shape", default=None, help="n,h,w,c_in,c_out of the conv measurement")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a scaled-down network (64/128/256, 128x128 images) and small sweeps")

@@ -1,10 +1,8 @@
 // The SDXL VAE (diffusers AutoencoderKL, reference src/vae/{mod,encoder,decoder}.rs)
 // on the kernel ABI: block_out (128, 256, 512, 512) (read from the weights),
 // 2 resnets per encoder level and 3 per decoder level, one single-head
-// attention in each mid block, GroupNorm(32) eps 1e-6. Every GroupNorm+SiLU in
-// front of a 3×3 conv is applied in that conv's operand gather (the
-// reference's forward_prologue, src/vae/mod.rs:174-211), and residuals /
-// shortcut outputs are added in the conv epilogues.
+// attention in each mid block, GroupNorm(32) eps 1e-6. Residuals and shortcut
+// outputs are added in the conv epilogues.
 #include <cmath>
 
 #include "eng_models.h"
@@ -32,15 +30,27 @@ VaeResnet VaeResnet::load(const Loader& l, int64_t c_in, int64_t c_out) {
     return r;
 }
 
+namespace {
+// SiLU(GN(x)) materialised once. The reference applies it inside the 3×3 convs' input
+// gather (forward_prologue, src/vae/mod.rs:190-211); on the GPU that gather reads every
+// input element nine times (once per tap), so the nine SiLUs cost more MUFU work than the
+// tensor cores' MMAs, while one apply pass costs 8 B/elt of HBM traffic. Same values.
+Tensor norm_silu(const Tensor& x, const GroupNormP& g) {
+    Tensor out(x.ctx(), x.n, x.h, x.w, x.c);
+    ck(mbx_group_norm_forward(x.ctx(), x.data(), x.n, x.h, x.w, x.c, g.groups, g.eps, g.gamma.f(), g.beta.f(),
+                              nullptr, 1, out.data()));
+    return out;
+}
+}  // namespace
+
 // h = conv1(SiLU(GN1(x))); h = conv2(SiLU(GN2(h))); h + (shortcut(x) | x)  (src/vae/mod.rs:190-211).
 Tensor VaeResnet::forward(const Tensor& x) const {
-    Tensor s, t;
-    gn_affine(x, norm1, nullptr, s, t);
-    Tensor h = conv3x3(x, conv1, s.data(), t.data(), true);
-    gn_affine(h, norm2, nullptr, s, t);
-    if (!has_shortcut) return conv3x3(h, conv2, s.data(), t.data(), true, x.data());
-    Tensor o = conv3x3(h, conv2, s.data(), t.data(), true);
+    Tensor h = conv3x3(norm_silu(x, norm1), conv1);
+    Tensor a = norm_silu(h, norm2);
     h = Tensor();
+    if (!has_shortcut) return conv3x3(a, conv2, nullptr, nullptr, false, x.data());
+    Tensor o = conv3x3(a, conv2);
+    a = Tensor();
     return conv1x1(x, shortcut, o.data());
 }
 
@@ -146,9 +156,7 @@ Tensor Vae::encode(const Tensor& images, const float* noise) const {
     cur = e_mid0.forward(cur);
     cur = e_attn.forward(cur);
     cur = e_mid1.forward(cur);
-    Tensor s, t;
-    gn_affine(cur, e_norm_out, nullptr, s, t);
-    Tensor mom = conv3x3(cur, e_conv_out, s.data(), t.data(), true);
+    Tensor mom = conv3x3(norm_silu(cur, e_norm_out), e_conv_out);
     cur = Tensor();
     Tensor moments = conv1x1(mom, quant_conv);
     mom = Tensor();
@@ -172,9 +180,8 @@ Tensor Vae::decode(const Tensor& latents) const {
         for (const VaeResnet& r : d_res[size_t(i)]) cur = r.forward(cur);
         if (i < 3) cur = conv3x3(cur, d_up[size_t(i)]);
     }
-    Tensor s, t;
-    gn_affine(cur, d_norm_out, nullptr, s, t);
-    Tensor out = conv3x3(cur, d_conv_out, s.data(), t.data(), true);
+    Tensor out = conv3x3(norm_silu(cur, d_norm_out), d_conv_out);
+    cur = Tensor();
     ck(mbx_scale_add(ctx_, out.data(), out.size(), 0.5f, 0.5f, out.data()));
     return out;
 }

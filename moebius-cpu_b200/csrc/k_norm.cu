@@ -18,14 +18,16 @@ constexpr int kGnThreads = 256;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// One CTA per (pixel chunk, item). V = 4 (float4 lanes over channels) or 1.
+// One CTA per (pixel chunk, item, channel slice of whole groups): small maps (few chunks) still
+// fill the GPU. V = 4 (float4 lanes over channels) or 1.
 template <int V, bool ADD>
 __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __restrict__ x, int64_t hw, int c,
-                                                                 int groups, const float* __restrict__ add,
+                                                                 int groups, int cs, const float* __restrict__ add,
                                                                  double* __restrict__ part) {
-    extern __shared__ float red[];  // [2][rows][c]
-    const int cv = c / V;
+    extern __shared__ float red[];  // [2][rows][cs]
+    const int cv = cs / V;
     const int64_t chunk = blockIdx.x, b = blockIdx.y, chunks = gridDim.x;
+    const int c0 = blockIdx.z * cs;
     const int64_t p0 = chunk * kGnChunk;
     const int npx = (int)(hw - p0 < kGnChunk ? hw - p0 : kGnChunk);
     const int t = threadIdx.x;
@@ -33,8 +35,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __
     const int rows = narrow ? kGnThreads / cv : 1;
     const int r = narrow ? t / cv : 0;
     float* rs = red;
-    float* rq = red + rows * c;
-    const float* xb = x + (b * hw + p0) * (int64_t)c;
+    float* rq = red + rows * cs;
+    const float* xb = x + (b * hw + p0) * (int64_t)c + c0;
     if (r < rows) {
         for (int j = narrow ? t % cv : t; j < cv; j += narrow ? cv : kGnThreads) {
             float s[V], q[V], a[V];
@@ -42,7 +44,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __
             for (int k = 0; k < V; ++k) {
                 s[k] = 0.0f;
                 q[k] = 0.0f;
-                a[k] = ADD ? add[b * c + j * V + k] : 0.0f;
+                a[k] = ADD ? add[b * c + c0 + j * V + k] : 0.0f;
             }
 #pragma unroll 8
             for (int p = r; p < npx; p += rows) {
@@ -65,18 +67,18 @@ __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __
             }
 #pragma unroll
             for (int k = 0; k < V; ++k) {
-                rs[r * c + j * V + k] = s[k];
-                rq[r * c + j * V + k] = q[k];
+                rs[r * cs + j * V + k] = s[k];
+                rq[r * cs + j * V + k] = q[k];
             }
         }
     }
     __syncthreads();
     // Per-channel chunk partial (f32, in row order), kept in row 0.
-    for (int ch = t; ch < c; ch += kGnThreads) {
+    for (int ch = t; ch < cs; ch += kGnThreads) {
         float s = rs[ch], q = rq[ch];
         for (int rr = 1; rr < rows; ++rr) {
-            s += rs[rr * c + ch];
-            q += rq[rr * c + ch];
+            s += rs[rr * cs + ch];
+            q += rq[rr * cs + ch];
         }
         rs[ch] = s;
         rq[ch] = q;
@@ -84,13 +86,14 @@ __global__ void __launch_bounds__(kGnThreads) gn_partials_kernel(const float* __
     __syncthreads();
     // f64 fold per group (src/engine/norm.rs:78-80).
     const int cg = c / groups;
-    for (int g = t; g < groups; g += kGnThreads) {
+    const int g0 = c0 / cg;
+    for (int gl = t; gl < cs / cg; gl += kGnThreads) {
         double ss = 0.0, qq = 0.0;
-        for (int ch = g * cg; ch < (g + 1) * cg; ++ch) {
+        for (int ch = gl * cg; ch < (gl + 1) * cg; ++ch) {
             ss += (double)rs[ch];
             qq += (double)rq[ch];
         }
-        double* dst = part + ((b * chunks + chunk) * groups + g) * 2;
+        double* dst = part + ((b * chunks + chunk) * groups + g0 + gl) * 2;
         dst[0] = ss;
         dst[1] = qq;
     }
@@ -271,15 +274,26 @@ void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int
     MBX_REQUIRE(chunks < (int64_t(1) << 31) && n < 65536, "GroupNorm tensor too large");
     const bool vec = c % 4 == 0 && aligned16(x) && (!add || aligned16(add));
     const int V = vec ? 4 : 1;
-    const int64_t cv = c / V;
+    // Channel slices of whole groups, at most 128 channels each (a multiple of V), so small maps
+    // with few pixel chunks still fill the GPU. The slicing depends on c alone, so an item's
+    // partial sums do not depend on the batch it is in.
+    const int64_t cg = c / groups;
+    int64_t gps = groups;
+    for (int64_t d = groups; d >= 1; --d) {
+        if (groups % d || (d * cg) % V) continue;
+        gps = d;
+        if (d * cg <= 128) break;
+    }
+    const int64_t cs = gps * cg;
+    const int64_t cv = cs / V;
     const int rows = cv <= kGnThreads ? int(kGnThreads / cv) : 1;
-    const size_t smem = size_t(2) * rows * c * sizeof(float);
-    dim3 grid((unsigned)chunks, (unsigned)n);
+    const size_t smem = size_t(2) * rows * cs * sizeof(float);
+    dim3 grid((unsigned)chunks, (unsigned)n, (unsigned)(groups / gps));
     auto run = [&](auto kernel) {
         if (smem > 48 * 1024)
             check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "gn smem attribute");
-        kernel<<<grid, kGnThreads, smem, ctx->stream>>>(x, hw, (int)c, (int)groups, add, part);
+        kernel<<<grid, kGnThreads, smem, ctx->stream>>>(x, hw, (int)c, (int)groups, (int)cs, add, part);
     };
     if (vec)
         add ? run(gn_partials_kernel<4, true>) : run(gn_partials_kernel<4, false>);

@@ -130,7 +130,8 @@ void Pool::free(void* p) {
     std::lock_guard<std::mutex> lock(mu_);
     auto it = used_.find(p);
     if (it == used_.end()) fail(MBX_ERR_INVALID_ARGUMENT, "mbx_free: pointer not from this context's pool");
-    free_.emplace(it->second, p);
+    // Most recently freed first among equal sizes (still warm in L2).
+    free_.emplace_hint(free_.lower_bound(it->second), it->second, p);
     cached_ += it->second;
     in_use_ -= it->second;
     used_.erase(it);
