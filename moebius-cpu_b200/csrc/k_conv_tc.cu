@@ -259,8 +259,12 @@ __global__ void __maxnreg__(128)
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
     const int bn = args.bn;
-    const int bstages = args.stages;    // weight-tile ring (shared memory)
-    const int astages = args.a_stages;  // A-operand ring (TMEM)
+    // One ring of K-chunk stages: stage s holds the weight tile (shared memory, by TMA) and the A
+    // tile (TMEM, by the converters); a single full barrier (128 converter arrivals + the TMA's
+    // expect-tx arrival) and a single empty barrier (the MMA commit) per stage, so the MMA thread
+    // does one barrier wait per chunk.
+    const int bstages = args.stages;
+    const int astages = args.stages;
     const uint32_t b_bytes = (uint32_t)bn * 128u;
     const uint32_t bstage_bytes = (F32W ? 2 : 1) * b_bytes;
     const uint32_t stg_base = base + (uint32_t)bstages * bstage_bytes;  // raw A staging ring
@@ -277,8 +281,8 @@ __global__ void __maxnreg__(128)
     auto sfull_bar = [&](int q) { return sbars + 8u * q; };
     auto sempty_bar = [&](int q) { return sbars + 8u * (kStgSlots + q); };
     const uint32_t tbars = sbars + 16u * kStgSlots;
-    auto a_full_bar = [&](int a) { return tbars + 8u * a; };
-    auto a_empty_bar = [&](int a) { return tbars + 8u * (kMaxAStages + a); };
+    auto a_full_bar = [&](int a) { return b_full_bar(a); };
+    auto a_empty_bar = [&](int a) { return b_empty_bar(a); };
     const uint32_t abars = tbars + 16u * kMaxAStages;
     auto acc_full_bar = [&](int b) { return abars + 8u * b; };
     auto acc_empty_bar = [&](int b) { return abars + 16u + 8u * b; };
@@ -302,16 +306,12 @@ __global__ void __maxnreg__(128)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < bstages; ++s) {
-            mbar_init(b_full_bar(s), 1);
+            mbar_init(b_full_bar(s), 129);
             mbar_init(b_empty_bar(s), 1);
         }
         for (int q = 0; q < kStgSlots; ++q) {
             mbar_init(sfull_bar(q), 128);
             mbar_init(sempty_bar(q), 128);
-        }
-        for (int a = 0; a < kMaxAStages; ++a) {
-            mbar_init(a_full_bar(a), 128);
-            mbar_init(a_empty_bar(a), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full_bar(b), 1);
@@ -521,8 +521,7 @@ __global__ void __maxnreg__(128)
                         live = false;
                         break;
                     }
-                    if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true) ||
-                        !mbar_wait(a_full_bar(a), (uint32_t)aphase, args.err, 10, abort_flag, true)) {
+                    if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true)) {
                         live = false;
                         break;
                     }
@@ -547,8 +546,7 @@ __global__ void __maxnreg__(128)
                             mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
                         }
                     }
-                    mma_commit(b_empty_bar(s));
-                    mma_commit(a_empty_bar(a));
+                    mma_commit(b_empty_bar(s));  // frees the stage's weight tile and A tile
                     if (seg_last) mma_commit(acc_full_bar(b));
                     if (++s == bstages) {
                         s = 0;
@@ -784,9 +782,9 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.bn = p->bn;
     a.n_tiles = p->cout_pad / p->bn;
     const bool f32w = p->lo != nullptr;
-    a.stages = stage_count(f32w, p->bn);
+    a.stages = std::min(stage_count(f32w, p->bn), std::min(kMaxAStages, (512 - 2 * p->bn) / 64));
     a.tmem_cols = 512;
-    a.a_stages = std::min(kMaxAStages, (512 - 2 * p->bn) / 64);
+    a.a_stages = a.stages;
     a.bias = bias;
     a.residual = residual;
     a.out = out;
