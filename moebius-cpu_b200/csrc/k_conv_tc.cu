@@ -508,59 +508,70 @@ __global__ void __maxnreg__(128)
             // between MMAs is a pipe bubble: ring positions and phases advance incrementally
             // (no division), descriptors step by their 16-byte address units.
             const uint32_t idesc = idesc_tf32(bn);
-            int s = 0, sphase = 0, a = 0, aphase = 0, seg = 0;
+            // Issues one K chunk (4 K-steps of 8) from stage st into accumulator d.
+            auto issue = [&](int st, uint32_t d, bool first) {
+                const uint32_t ah = tmem + a_col(st), al = ah + 32u;
+                const uint32_t b_hi = base + (uint32_t)st * bstage_bytes;
+                const uint64_t bdh0 = sw128_desc(b_hi);
+                const uint64_t bdl0 = sw128_desc(b_hi + b_bytes);
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint64_t bdh = bdh0 + (uint64_t)(2 * kk);  // + kk·32 bytes
+                    const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+                    const uint32_t ko = (uint32_t)kk * 8u;
+                    if constexpr (F32W) {
+                        const uint64_t bdl = bdl0 + (uint64_t)(2 * kk);
+                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                        mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
+                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
+                    } else {
+                        mma_tf32_ts(d, al + ko, bdh, idesc, acc);
+                        mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
+                    }
+                }
+            };
+            // Chunks go out in pairs (one synchronisation per 16 or 24 MMAs); a segment's odd
+            // last chunk goes alone.
+            int s = 0, sphase = 0, seg = 0;
             bool live = true;
             for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
                 int kin = 0;
-                for (int kc = 0; kc < K; ++kc) {
+                for (int kc = 0; kc < K;) {
                     const int b = seg & 1;
                     const bool seg_first = kin == 0;
-                    const bool seg_last = kin == kSegChunks - 1 || kc + 1 == K;
+                    const int left = min(kSegChunks - kin, K - kc);
+                    const int g = left >= 2 ? 2 : 1;
+                    const int s1 = s + 1 == bstages ? 0 : s + 1;
+                    const int ph1 = s + 1 == bstages ? sphase ^ 1 : sphase;
                     if (seg_first &&
                         !mbar_wait(acc_empty_bar(b), ((seg >> 1) & 1) ^ 1, args.err, 5, abort_flag, true)) {
                         live = false;
                         break;
                     }
-                    if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true)) {
+                    if (!mbar_wait(b_full_bar(s), (uint32_t)sphase, args.err, 3, abort_flag, true) ||
+                        (g == 2 && !mbar_wait(b_full_bar(s1), (uint32_t)ph1, args.err, 3, abort_flag, true))) {
                         live = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)(b * bn);
-                    const uint32_t ah = tmem + a_col(a), al = ah + 32u;
-                    const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
-                    const uint64_t bdh0 = sw128_desc(b_hi);
-                    const uint64_t bdl0 = sw128_desc(b_hi + b_bytes);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint64_t bdh = bdh0 + (uint64_t)(2 * kk);  // + kk·32 bytes
-                        const uint32_t acc = (!seg_first || kk > 0) ? 1u : 0u;
-                        const uint32_t ko = (uint32_t)kk * 8u;
-                        if constexpr (F32W) {
-                            const uint64_t bdl = bdl0 + (uint64_t)(2 * kk);
-                            mma_tf32_ts(d, al + ko, bdh, idesc, acc);
-                            mma_tf32_ts(d, ah + ko, bdl, idesc, 1u);
-                            mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
-                        } else {
-                            mma_tf32_ts(d, al + ko, bdh, idesc, acc);
-                            mma_tf32_ts(d, ah + ko, bdh, idesc, 1u);
-                        }
-                    }
+                    issue(s, d, seg_first);
+                    if (g == 2) issue(s1, d, false);
                     mma_commit(b_empty_bar(s));  // frees the stage's weight tile and A tile
-                    if (seg_last) mma_commit(acc_full_bar(b));
-                    if (++s == bstages) {
-                        s = 0;
-                        sphase ^= 1;
-                    }
-                    if (++a == astages) {
-                        a = 0;
-                        aphase ^= 1;
-                    }
-                    if (seg_last) {
+                    if (g == 2) mma_commit(b_empty_bar(s1));
+                    kc += g;
+                    kin += g;
+                    if (kin == kSegChunks || kc == K) {
+                        mma_commit(acc_full_bar(b));
                         kin = 0;
                         ++seg;
+                    }
+                    if (g == 2) {
+                        s = s1 + 1 == bstages ? 0 : s1 + 1;
+                        sphase = s1 + 1 == bstages ? ph1 ^ 1 : ph1;
                     } else {
-                        ++kin;
+                        s = s1;
+                        sphase = ph1;
                     }
                 }
             }
@@ -783,6 +794,8 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.n_tiles = p->cout_pad / p->bn;
     const bool f32w = p->lo != nullptr;
     a.stages = std::min(stage_count(f32w, p->bn), std::min(kMaxAStages, (512 - 2 * p->bn) / 64));
+    // The MMA thread waits for two consecutive stages at once: the ring needs at least two.
+    if (a.stages < 2) fail(MBX_ERR_INTERNAL, "conv: fewer than two pipeline stages fit");
     a.tmem_cols = 512;
     a.a_stages = a.stages;
     a.bias = bias;
