@@ -61,6 +61,11 @@ extern "C" {
 typedef struct mbx_ctx mbx_ctx;
 typedef struct mbx_param mbx_param;
 
+/* A pixel rectangle (reference MoebiusRect, include/moebius_cpu.h:41-43). */
+typedef struct mbx_rect {
+    uint32_t x, y, width, height;
+} mbx_rect;
+
 uint32_t mbx_abi_version(void);
 
 /* Message for the last failed call on the calling thread (valid until the next
@@ -323,6 +328,78 @@ int32_t mbx_gaussian_blur_u8(mbx_ctx *ctx, const uint8_t *in, int64_t n, int64_t
  * an empty mask returns before any change, src/pipeline.rs:202-204. */
 int32_t mbx_feather_paste(mbx_ctx *ctx, const float *result, const uint8_t *blurred, uint8_t *image, int64_t n,
                           int64_t h, int64_t w, int64_t channels, const int32_t *nonempty);
+
+/* DPM-Solver++(2M) step of the Fast preset: e as in mbx_cfg_ddim_step, x0 = (x - coef[0]*e) * coef[1];
+ * order 0 (the last step): x = x0; order 1: x = coef[2]*x + coef[3]*x0; order 2:
+ * x = coef[2]*x + coef[3]*x0 - coef[4]*x0_prev. x0 is stored into x0_prev (orders 1, 2).
+ * coef = {sigma_t, 1/alpha_t, sigma_next/sigma_t, phi or c0, c1}, computed in f64 and
+ * rounded to f32 as the reference does (mbx_dpm_coefficients).
+ * Reference: Dpm2M::step, src/scheduler.rs:107-152; src/pipeline.rs:323-344. */
+int32_t mbx_cfg_dpm_step(mbx_ctx *ctx, const float *eps, int64_t n, int64_t hw, int64_t copies, float guidance,
+                         const float coef[5], int32_t order, float *x, float *x0_prev);
+
+/* Host-only: the coefficients of DPM-Solver++(2M) step i of the schedule (steps, strength,
+ * spacing 0 leading / 1 trailing) with history restarted at step `restart_at` (-1 = never):
+ * coef[5] and order as mbx_cfg_dpm_step takes them. Reference: src/scheduler.rs:100-152. */
+int32_t mbx_dpm_coefficients(uint32_t steps, double strength, int32_t trailing, int64_t i, int64_t restart_at,
+                             float coef[5], int32_t *order);
+
+/* ---- Images of any size around the model window (reference src/imaging/ modules). ----
+ * Images are 8-bit RGB or RGBA with a row stride in bytes; masks are 8-bit with
+ * a row stride. A buffer may hold only a region of the whole image: origin_x,
+ * origin_y give the image coordinates of its first pixel, width and height the
+ * whole image's extent. All pixel work is byte-exact with the reference. */
+
+/* Host-only: the square crop window (x, y, side) for a mask bbox (bx, by, bw, bh) in a
+ * width x height image, never smaller than min(model_side, long side) and never larger
+ * than the long side; *source receives the part of the window inside the image.
+ * Reference: CropPlan::new / source_rect, src/imaging/crop.rs:30-62 (model_side = IMAGE_SIZE). */
+int32_t mbx_crop_window(uint32_t bx, uint32_t by, uint32_t bw, uint32_t bh, uint32_t width, uint32_t height,
+                        int64_t model_side, int64_t window[3], mbx_rect *source);
+
+/* Host-only: Pillow's Lanczos3 coefficients for in_size -> out_size samples (the formulation
+ * of fast_image_resize's convolution): bounds [out][2] = (first input, count), coeffs
+ * [out][ksize] in 22-bit fixed point. With bounds == NULL only *ksize is written.
+ * Reference: resize_u8, src/imaging/resize.rs:16-25. */
+int32_t mbx_lanczos_table(int64_t in_size, int64_t out_size, int32_t *bounds, int32_t *coeffs, int64_t *ksize);
+
+/* Binarise (>= 128 -> 255, else 0) and dilate n masks [n][h][mask_stride] with a k x k
+ * square, anchor k/2 (k <= 1: binarise only) into out [n][h][w] (packed).
+ * scratch: n*h*w bytes. Reference: dilate, src/imaging/mod.rs:61-89. */
+int32_t mbx_mask_dilate(mbx_ctx *ctx, const uint8_t *mask, int64_t n, int64_t h, int64_t w, int64_t mask_stride,
+                        int64_t k, uint8_t *scratch, uint8_t *out);
+
+/* Bounding box of the pixels >= 128 of each of n masks: box [n][4] = {x0, y0, x1, y1}
+ * (inclusive; x1 = -1 for an empty mask), device int32. Reference: MaskRef::bbox,
+ * src/imaging/mod.rs:38-53. */
+int32_t mbx_mask_bbox(mbx_ctx *ctx, const uint8_t *mask, int64_t n, int64_t h, int64_t w, int64_t mask_stride,
+                      int32_t *box);
+
+/* The window (win_x, win_y, side) -> model-size 8-bit RGB rgb_out [model_side]^2 x 3 and
+ * binary mask bin_out [model_side]^2: edge replication past the image for the colour, zeros
+ * for the mask, Lanczos3 (a copy when side == model_side), the mask re-thresholded at 128.
+ * image / mask hold the region [origin, origin + region size) which must contain the
+ * window's part inside the image. Reference: to_model, src/imaging/resize.rs:27-57. */
+int32_t mbx_window_to_model(mbx_ctx *ctx, const uint8_t *image, int64_t stride, int64_t channels,
+                            const uint8_t *mask, int64_t mask_stride, int64_t origin_x, int64_t origin_y,
+                            int64_t region_w, int64_t region_h, int64_t width, int64_t height, int64_t win_x,
+                            int64_t win_y, int64_t side, int64_t model_side, uint8_t *rgb_out, uint8_t *bin_out);
+
+/* n decoded images [n][model_side]^2 x 3 in [0, 1] -> 8-bit windows out [n][side]^2 x 3
+ * (truncation, then Lanczos3). Reference: from_model, src/imaging/resize.rs:61-67. */
+int32_t mbx_model_to_window(mbx_ctx *ctx, const float *rgb, int64_t n, int64_t model_side, int64_t side,
+                            uint8_t *out);
+
+/* Pastes n window results result [n][side]^2 x 3 into n image regions in place
+ * (image [n][region_h][stride], mask [n][region_h][mask_stride]; the region must
+ * cover the window's source rectangle plus a 16 px margin clipped to the image).
+ * mode: MBX_PASTE_NONE (1) copy, MBX_PASTE_FEATHER (2) or MBX_PASTE_FEATHER_COMPENSATE (3).
+ * Items whose active[i] is 0 are left untouched (active may be NULL).
+ * Reference: paste, src/imaging/blend.rs:104-215. */
+int32_t mbx_paste(mbx_ctx *ctx, uint8_t *image, int64_t n, int64_t stride, int64_t channels, const uint8_t *mask,
+                  int64_t mask_stride, int64_t origin_x, int64_t origin_y, int64_t region_w, int64_t region_h,
+                  int64_t width, int64_t height, int64_t win_x, int64_t win_y, int64_t side, const uint8_t *result,
+                  uint32_t mode, const int32_t *active);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

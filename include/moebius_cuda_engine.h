@@ -1,15 +1,16 @@
 /* moebius-cuda engine API: the moebius-cpu inpainting engine (UNet + VAE +
- * DDIM pipeline) running on the kernels of moebius_cuda.h, for one B200.
+ * DDIM / DPM-Solver++ pipeline) running on the kernels of moebius_cuda.h, for
+ * one B200.
  *
  * Mirrors the reference's outer C ABI, include/moebius_cpu.h:48-67 (status
  * codes, thread-local last error, engine create / destroy / inpaint, a
  * progress callback that can cancel), plus batch and component entry points.
  * Status codes and mbx_last_error() are those of moebius_cuda.h.
  *
- * Images are used whole at the model size (512 x 512 for the shipped
- * network): the crop-window resampling of other sizes (reference
- * src/imaging/resize.rs) is not part of this library, and such inputs are
- * rejected with MBX_ERR_INVALID_ARGUMENT. */
+ * mbx_inpaint takes images of any size (square crop window around the mask,
+ * Lanczos3 to and from the model size, src/imaging/ modules); the batch call takes
+ * model-size images, each used whole. Both presets (Exact, Fast), every paste
+ * mode and mask dilation are built. */
 #ifndef MOEBIUS_CUDA_ENGINE_H
 #define MOEBIUS_CUDA_ENGINE_H
 
@@ -26,12 +27,12 @@ extern "C" {
 #endif
 
 #define MBX_PRESET_EXACT 0u /* reference MOEBIUS_PRESET_EXACT */
-#define MBX_PRESET_FAST  1u /* reference MOEBIUS_PRESET_FAST (not built: MBX_ERR_INVALID_ARGUMENT) */
+#define MBX_PRESET_FAST  1u /* reference MOEBIUS_PRESET_FAST: 10 trailing DPM-Solver++(2M) steps, CFG for 3, ROI encode */
 
 #define MBX_PASTE_DEFAULT            0u
 #define MBX_PASTE_NONE               1u
 #define MBX_PASTE_FEATHER            2u
-#define MBX_PASTE_FEATHER_COMPENSATE 3u /* not built: MBX_ERR_INVALID_ARGUMENT */
+#define MBX_PASTE_FEATHER_COMPENSATE 3u
 
 typedef struct mbx_engine mbx_engine;
 
@@ -39,16 +40,12 @@ typedef struct mbx_engine mbx_engine;
  * MoebiusParams (include/moebius_cpu.h:31-39). */
 typedef struct mbx_inpaint_params {
     uint32_t preset;      /* MBX_PRESET_* */
-    uint32_t steps;       /* 0 = preset default (20) */
+    uint32_t steps;       /* 0 = preset default (20 Exact, 10 Fast) */
     float guidance;       /* <= 0 = preset default (2.5) */
     uint64_t seed;
     uint32_t paste;       /* MBX_PASTE_* */
-    uint32_t mask_dilate; /* px; only 0 is built */
+    uint32_t mask_dilate; /* px, 0 = off */
 } mbx_inpaint_params;
-
-typedef struct mbx_rect {
-    uint32_t x, y, width, height;
-} mbx_rect;
 
 /* stage: 0 encode, 1 denoise, 2 decode. Return non-zero to cancel. When a
  * callback is given the engine waits for each step to finish before
@@ -72,18 +69,28 @@ uint64_t mbx_engine_launch_count(const mbx_engine *engine);
 /* latent side, model image side and the three UNet level widths. */
 int32_t mbx_engine_info(const mbx_engine *engine, int64_t *latent_side, int64_t *image_side, int64_t widths[3]);
 
-/* In-place inpaint of one 8-bit RGB/RGBA host image where mask >= 128; alpha
- * is preserved. width == height == the model side. Noise comes from `seed`
- * (a deterministic generator of this library: the reference's Rust generator
- * cannot be reproduced). params, progress and changed may be NULL. On
- * MBX_ERR_CANCELLED the image is untouched. Reference: moebius_inpaint,
- * include/moebius_cpu.h:60-67, src/pipeline.rs:138-213. */
+/* In-place inpaint of one 8-bit RGB/RGBA host image of any size where mask >= 128;
+ * alpha is preserved; *changed receives the rectangle written (empty for an empty
+ * mask). Noise comes from `seed` (a deterministic generator of this library: the
+ * reference's Rust generator cannot be reproduced). params, progress and changed
+ * may be NULL. On MBX_ERR_CANCELLED the image is untouched. Reference:
+ * moebius_inpaint, include/moebius_cpu.h:60-67, src/pipeline.rs:138-213. */
 int32_t mbx_inpaint(mbx_engine *engine, uint8_t *pixels, uint32_t width, uint32_t height, uint32_t stride,
                     uint32_t channels, const uint8_t *mask, uint32_t mask_stride, const mbx_inpaint_params *params,
                     mbx_progress_fn progress, void *user, mbx_rect *changed);
 
-/* n independent inpaints of side x side images, processed together (the
- * UNet runs at batch 2n for classifier-free guidance). pixels [n][side][side][channels]
+/* mbx_inpaint with caller-supplied host noise (the reference's NoiseSet,
+ * src/pipeline.rs:67-92): noise_vae [2][L][L][4] (image, masked image),
+ * noise_init [L][L][4], noise_offset [4], L = the latent side; all three or none.
+ * Reference: Engine::inpaint_with_noise, src/pipeline.rs:150-161. */
+int32_t mbx_inpaint_with_noise(mbx_engine *engine, uint8_t *pixels, uint32_t width, uint32_t height,
+                               uint32_t stride, uint32_t channels, const uint8_t *mask, uint32_t mask_stride,
+                               const mbx_inpaint_params *params, const float *noise_vae, const float *noise_init,
+                               const float *noise_offset, mbx_progress_fn progress, void *user, mbx_rect *changed);
+
+/* n independent inpaints of side x side images (side = the model side, each image
+ * used whole), processed together (the UNet runs at batch 2n for classifier-free
+ * guidance, n for the Fast preset's conditional-only steps). pixels [n][side][side][channels]
  * (modified in place), masks [n][side][side]. Explicit noise (the reference's
  * NoiseSet, src/pipeline.rs:67-92), or all three NULL for seeded noise
  * (inpaint i uses seed + i):

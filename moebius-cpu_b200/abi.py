@@ -123,6 +123,17 @@ SIGNATURES = {
     "mbx_cfg_ddim_step": (_i32, [_vp, _vp, _i64, _i64, _i64, _f32, _pf32, _vp]),
     "mbx_gaussian_blur_u8": (_i32, [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "mbx_feather_paste": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mbx_cfg_dpm_step": (_i32, [_vp, _vp, _i64, _i64, _i64, _f32, _pf32, _i32, _vp, _vp]),
+    "mbx_dpm_coefficients": (_i32, [_u32, _f64, _i32, _i64, _i64, _pf32, _pi32]),
+    "mbx_crop_window": (_i32, [_u32, _u32, _u32, _u32, _u32, _u32, _i64, _pi64, ctypes.POINTER(Rect)]),
+    "mbx_lanczos_table": (_i32, [_i64, _i64, _pi32, _pi32, _pi64]),
+    "mbx_mask_dilate": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mbx_mask_bbox": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mbx_window_to_model": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                   _i64, _i64, _i64, _vp, _vp]),
+    "mbx_model_to_window": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "mbx_paste": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                         _i64, _vp, _u32, _vp]),
     # include/moebius_cuda_engine.h
     "mbx_engine_create": (_i32, [ctypes.c_char_p, _i32, _pvp]),
     "mbx_engine_destroy": (None, [_vp]),
@@ -131,6 +142,8 @@ SIGNATURES = {
     "mbx_engine_launch_count": (_u64, [_vp]),
     "mbx_inpaint": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, ctypes.POINTER(InpaintParams), PROGRESS_FN,
                            _vp, ctypes.POINTER(Rect)]),
+    "mbx_inpaint_with_noise": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, ctypes.POINTER(InpaintParams),
+                                      _vp, _vp, _vp, PROGRESS_FN, _vp, ctypes.POINTER(Rect)]),
     "mbx_inpaint_batch": (_i32, [_vp, _vp, _vp, _i64, _u32, _u32, ctypes.POINTER(InpaintParams), _vp, _vp, _vp,
                                  _i32, PROGRESS_FN, _vp]),
     "mbx_engine_unet_forward": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp]),

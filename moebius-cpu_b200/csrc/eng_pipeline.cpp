@@ -8,8 +8,10 @@
 //   (replayed from a CUDA graph captured once per batch size), guidance +
 //   DDIM update → VAE decode → Pillow blur of the mask → feathered paste.
 // Everything stays on the device between the input copy and the output copy.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <string>
 
 #include "../../include/moebius_cuda_engine.h"
@@ -97,28 +99,123 @@ struct Normal {
     }
 };
 
-struct ExactParams {
+// Resolved inpaint parameters (reference InpaintParams, src/preset.rs:32-83).
+struct Params {
     int steps = 20;
     double strength = 0.99;
+    bool trailing = false;
+    bool dpm = false;         // Solver::DpmPp2M (else Ddim)
     float guidance = 2.5f;
     float noise_offset = 0.0357f;
+    uint64_t seed = 0;
+    int cfg_steps = -1;       // CFG for the first cfg_steps steps only (-1: every step)
+    bool roi_encode = false;
+    uint32_t paste = MBX_PASTE_FEATHER;
+    uint32_t mask_dilate = 0;
 };
 
-// src/preset.rs:312-338 (Exact) with the caller's overrides (src/ffi.rs).
-ExactParams resolve(const mbx_inpaint_params* p) {
-    ExactParams e;
+// Preset defaults with the caller's overrides (src/preset.rs:55-83, src/ffi.rs:248-271).
+Params resolve(const mbx_inpaint_params* p) {
+    Params e;
     if (!p) return e;
-    MBX_REQUIRE(p->preset == MBX_PRESET_EXACT, "only the Exact preset is built in this library");
-    MBX_REQUIRE(p->paste == MBX_PASTE_DEFAULT || p->paste == MBX_PASTE_FEATHER,
-                "only the Feather paste (the Exact default) is built in this library");
-    MBX_REQUIRE(p->mask_dilate == 0, "mask dilation is not built in this library");
+    if (p->preset == MBX_PRESET_FAST) {  // Preset::Fast: 10 trailing DPM++(2M) steps, CFG for 3, ROI encode
+        e.steps = 10;
+        e.trailing = true;
+        e.dpm = true;
+        e.cfg_steps = 3;
+        e.roi_encode = true;
+    } else {
+        MBX_REQUIRE(p->preset == MBX_PRESET_EXACT, "unknown preset " + std::to_string(p->preset));
+    }
     if (p->steps) {
-        MBX_REQUIRE(p->steps <= 1000, "steps must be 1..=1000");
+        MBX_REQUIRE(p->steps <= 1000, "steps must be 1..=1000, got " + std::to_string(p->steps));
         e.steps = (int)p->steps;
     }
     if (p->guidance > 0.0f) e.guidance = p->guidance;
+    e.seed = p->seed;
+    e.mask_dilate = p->mask_dilate;
+    switch (p->paste) {
+        case MBX_PASTE_DEFAULT:
+            break;
+        case MBX_PASTE_NONE:
+        case MBX_PASTE_FEATHER:
+        case MBX_PASTE_FEATHER_COMPENSATE:
+            e.paste = p->paste;
+            break;
+        default:
+            fail(MBX_ERR_INVALID_ARGUMENT, "unknown paste mode " + std::to_string(p->paste));
+    }
     return e;
 }
+
+// (α_t, σ_t, λ_t = ln α_t − ln σ_t) in f64 (src/scheduler.rs:100-105).
+void dpm_abl(const Ddim& d, int64_t t, double& alpha, double& sigma, double& lambda) {
+    const double a = (double)d.ac[size_t(t)];
+    alpha = std::sqrt(a);
+    sigma = std::sqrt(1.0 - a);
+    lambda = std::log(alpha) - std::log(sigma);
+}
+
+// Coefficients of DPM-Solver++(2M) step i (Dpm2M::step, src/scheduler.rs:121-151) given whether the
+// solver holds the previous step's data prediction (and its λ): coef = {σ, 1/α, σ_n/σ, φ or c0, c1}.
+void dpm_step_coef(const Ddim& d, size_t i, bool has_prev, double lambda_prev, float coef[5], int* order) {
+    const std::vector<int64_t>& ts = d.timesteps;
+    double alpha, sigma, lambda;
+    dpm_abl(d, ts[i], alpha, sigma, lambda);
+    coef[0] = (float)sigma;
+    coef[1] = (float)(1.0 / alpha);
+    coef[2] = coef[3] = coef[4] = 0.0f;
+    if (i + 1 >= ts.size()) {
+        *order = 0;
+        return;
+    }
+    double an, sn, ln;
+    dpm_abl(d, ts[i + 1], an, sn, ln);
+    const double h = ln - lambda;
+    coef[2] = (float)(sn / sigma);
+    const double phi = an * (1.0 - std::exp(-h));
+    if (!has_prev) {
+        *order = 1;
+        coef[3] = (float)phi;
+    } else {
+        const double r = (lambda - lambda_prev) / h;
+        *order = 2;
+        coef[3] = (float)(phi * (1.0 + 0.5 / r));
+        coef[4] = (float)(phi * 0.5 / r);
+    }
+}
+
+// The latent bbox of mask_lat > 0.5 grown by `margin` and clamped (src/vae/mod.rs:64-78).
+struct LatRect {
+    int64_t x = 0, y = 0, w = 0, h = 0;
+    bool empty = true;
+};
+
+LatRect roi_window(const float* m, int64_t L, int64_t margin) {
+    int64_t x0 = L, y0 = L, x1 = -1, y1 = -1;
+    for (int64_t i = 0; i < L * L; ++i)
+        if (m[i] > 0.5f) {
+            const int64_t y = i / L, x = i % L;
+            x0 = std::min(x0, x);
+            y0 = std::min(y0, y);
+            x1 = std::max(x1, x);
+            y1 = std::max(y1, y);
+        }
+    LatRect r;
+    if (x1 < 0) return r;
+    x0 = std::max<int64_t>(x0 - margin, 0);
+    y0 = std::max<int64_t>(y0 - margin, 0);
+    x1 = std::min(x1 + margin, L - 1);
+    y1 = std::min(y1 + margin, L - 1);
+    r.x = x0;
+    r.y = y0;
+    r.w = x1 - x0 + 1;
+    r.h = y1 - y0 + 1;
+    r.empty = false;
+    return r;
+}
+
+constexpr int64_t kRoiMargin = 8;  // src/vae/mod.rs:60
 
 }  // namespace
 
@@ -214,81 +311,146 @@ struct mbx_engine {
         ctx->launches += r.kernels;
     }
 
-    // Device-buffer batch inpaint (src/pipeline.rs:215-373 for n inpaints at once).
-    void inpaint_device(uint8_t* pixels, const uint8_t* masks, int64_t n, int64_t S, int64_t ch,
-                        const mbx_inpaint_params* params, const float* noise_vae, const float* noise_init,
-                        const float* noise_offset, mbx_progress_fn progress, void* user) {
-        const ExactParams ep = resolve(params);
-        MBX_REQUIRE(S == side(), "images must be " + std::to_string(side()) + " x " + std::to_string(side()) +
-                                     " (the model size; crop-window resampling is not part of this library)");
-        MBX_REQUIRE(ch == 3 || ch == 4, "image must be RGB or RGBA");
-        if (n == 0) return;
-        const int64_t L = latent(), lhw = L * L;
-        auto report = [&](uint32_t stage, uint32_t done, uint32_t total) {
+    using Report = std::function<void(uint32_t, uint32_t, uint32_t)>;
+
+    Report reporter(mbx_progress_fn progress, void* user) {
+        return [this, progress, user](uint32_t stage, uint32_t done, uint32_t total) {
             if (!progress) return;
             check_cuda(cudaStreamSynchronize(ctx->stream), "progress");
             if (progress(user, stage, done, total) != 0) fail(MBX_ERR_CANCELLED, "cancelled");
         };
+    }
 
-        // Seeded noise when none is given (NoiseSet::sample order: vae_img, vae_masked, init, offset).
-        std::vector<float> hv, hi, ho;
-        Tensor dv, di, dof;
-        if (!noise_vae && !noise_init && !noise_offset) {
-            const uint64_t seed = params ? params->seed : 0;
-            hv.resize(size_t(2 * n * lhw * 4));
-            hi.resize(size_t(n * lhw * 4));
-            ho.resize(size_t(n * 4));
-            for (int64_t i = 0; i < n; ++i) {
-                Normal g(seed + (uint64_t)i);
-                for (int part = 0; part < 2; ++part)
-                    for (int64_t e = 0; e < lhw * 4; ++e) hv[size_t((2 * i + part) * lhw * 4 + e)] = g();
-                for (int64_t e = 0; e < lhw * 4; ++e) hi[size_t(i * lhw * 4 + e)] = g();
-                for (int e = 0; e < 4; ++e) ho[size_t(i * 4 + e)] = g();
-            }
-            dv = Tensor(ctx, 2 * n, L, L, 4);
-            di = Tensor(ctx, n, L, L, 4);
-            dof = Tensor(ctx, n, 1, 1, 4);
-            check_cuda(cudaMemcpyAsync(dv.data(), hv.data(), hv.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
-            check_cuda(cudaMemcpyAsync(di.data(), hi.data(), hi.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
-            check_cuda(cudaMemcpyAsync(dof.data(), ho.data(), ho.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
-            noise_vae = dv.data();
-            noise_init = di.data();
-            noise_offset = dof.data();
+    // The caller's noise, or seeded noise (NoiseSet::sample order per inpaint: vae_img,
+    // vae_masked, init, offset; inpaint i uses seed + i) uploaded into `keep`.
+    struct Noise {
+        Tensor v, i, o;
+        const float* vae = nullptr;
+        const float* init = nullptr;
+        const float* offset = nullptr;
+    };
+
+    Noise noise_for(int64_t n, uint64_t seed, const float* nv, const float* ni, const float* no) {
+        Noise z;
+        if (nv || ni || no) {
+            MBX_REQUIRE(nv && ni && no, "give all three noise tensors or none");
+            z.vae = nv;
+            z.init = ni;
+            z.offset = no;
+            return z;
         }
-        MBX_REQUIRE(noise_vae && noise_init && noise_offset, "give all three noise tensors or none");
+        const int64_t lhw = latent() * latent();
+        std::vector<float> hv(size_t(2 * n * lhw * 4)), hi(size_t(n * lhw * 4)), ho(size_t(n * 4));
+        for (int64_t i = 0; i < n; ++i) {
+            Normal g(seed + (uint64_t)i);
+            for (int part = 0; part < 2; ++part)
+                for (int64_t e = 0; e < lhw * 4; ++e) hv[size_t((2 * i + part) * lhw * 4 + e)] = g();
+            for (int64_t e = 0; e < lhw * 4; ++e) hi[size_t(i * lhw * 4 + e)] = g();
+            for (int e = 0; e < 4; ++e) ho[size_t(i * 4 + e)] = g();
+        }
+        const int64_t L = latent();
+        z.v = Tensor(ctx, 2 * n, L, L, 4);
+        z.i = Tensor(ctx, n, L, L, 4);
+        z.o = Tensor(ctx, n, 1, 1, 4);
+        // Pageable sources: each copy has read its host buffer when the call returns.
+        check_cuda(cudaMemcpyAsync(z.v.data(), hv.data(), hv.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
+        check_cuda(cudaMemcpyAsync(z.i.data(), hi.data(), hi.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
+        check_cuda(cudaMemcpyAsync(z.o.data(), ho.data(), ho.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "noise");
+        z.vae = z.v.data();
+        z.init = z.i.data();
+        z.offset = z.o.data();
+        return z;
+    }
 
+    // 4: VAE encode into z [2n] = (z_img, z_masked) per inpaint (pipeline.rs:255-289). images holds
+    // [image_0, masked_0, image_1, ...]. ROI encode: z_masked from the masked image alone and z_img =
+    // z_masked with the latents near the mask replaced by an encode of the image window around it.
+    void encode(const Tensor& images, const float* noise_vae, const Tensor& mask_lat, int64_t n, bool roi,
+                Tensor& z) {
+        const int64_t S = side(), L = latent(), lhw = L * L;
+        auto put = [&](const Tensor& t, int64_t item) {
+            check_cuda(cudaMemcpyAsync(z.item(item), t.data(), size_t(t.size()) * 4, cudaMemcpyDeviceToDevice,
+                                       ctx->stream),
+                       "latents");
+        };
+        if (!roi) {
+            for (int64_t b0 = 0; b0 < 2 * n; b0 += vae_chunk) {
+                const int64_t b = std::min(vae_chunk, 2 * n - b0);
+                put(vae->encode(Tensor::view(ctx, images.item(b0), b, S, S, 3), noise_vae + b0 * lhw * 4), b0);
+            }
+            return;
+        }
+        std::vector<float> ml(size_t(n * lhw));
+        check_cuda(cudaMemcpyAsync(ml.data(), mask_lat.data(), ml.size() * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                   "latent masks");
+        check_cuda(cudaStreamSynchronize(ctx->stream), "latent masks");
+        for (int64_t i = 0; i < n; ++i) {
+            const float* mi = ml.data() + i * lhw;
+            const LatRect r = roi_window(mi, L, kRoiMargin);
+            if (r.empty || (r.w == L && r.h == L)) {  // no window: both images whole
+                put(vae->encode(Tensor::view(ctx, images.item(2 * i), 2, S, S, 3), noise_vae + 2 * i * lhw * 4),
+                    2 * i);
+                continue;
+            }
+            {
+                Tensor zm = vae->encode(Tensor::view(ctx, images.item(2 * i + 1), 1, S, S, 3),
+                                        noise_vae + (2 * i + 1) * lhw * 4);
+                put(zm, 2 * i + 1);
+                put(zm, 2 * i);
+            }
+            Tensor crop(ctx, 1, 8 * r.h, 8 * r.w, 3), cn(ctx, 1, r.h, r.w, 4);
+            check_cuda(cudaMemcpy2DAsync(crop.data(), size_t(8 * r.w * 3) * 4,
+                                         images.item(2 * i) + (8 * r.y * S + 8 * r.x) * 3, size_t(S * 3) * 4,
+                                         size_t(8 * r.w * 3) * 4, size_t(8 * r.h), cudaMemcpyDeviceToDevice,
+                                         ctx->stream),
+                       "ROI crop");
+            check_cuda(cudaMemcpy2DAsync(cn.data(), size_t(r.w * 4) * 4, noise_vae + (2 * i * lhw + r.y * L + r.x) * 4,
+                                         size_t(L * 4) * 4, size_t(r.w * 4) * 4, size_t(r.h), cudaMemcpyDeviceToDevice,
+                                         ctx->stream),
+                       "ROI noise");
+            Tensor part = vae->encode(crop, cn.data());
+            // The window's border latents see zero padding: only the part nearer the mask is kept.
+            const LatRect in = roi_window(mi, L, kRoiMargin / 2);
+            check_cuda(cudaMemcpy2DAsync(z.item(2 * i) + (in.y * L + in.x) * 4, size_t(L * 4) * 4,
+                                         part.data() + ((in.y - r.y) * r.w + (in.x - r.x)) * 4, size_t(r.w * 4) * 4,
+                                         size_t(in.w * 4) * 4, size_t(in.h), cudaMemcpyDeviceToDevice, ctx->stream),
+                       "ROI latents");
+        }
+    }
+
+    // Steps 2-9 for n model-size inputs on the device: images8 [n][S][S][ch], masks [n][S][S]
+    // (>= 128 inpaints). Returns the decoded images [n][S][S][3] in [0, 1]; flags[i] = 1 when
+    // mask i has a masked pixel. src/pipeline.rs:215-366 for n inpaints at once.
+    Tensor run_model(const uint8_t* images8, int64_t ch, const uint8_t* masks, int64_t n, const Params& ep,
+                     const Noise& noise, int32_t* flags, const Report& report) {
+        const int64_t S = side(), L = latent(), lhw = L * L;
         // 2-5: model inputs and masks (pipeline.rs:234-252).
         report(0, 0, 1);
         Tensor images(ctx, 2 * n, S, S, 3);
-        PoolBuf bin(ctx, size_t(n * S * S)), flags(ctx, size_t(n) * 4);
         Tensor mask_lat(ctx, n, L, L, 1);
-        ck(mbx_inpaint_prepare(ctx, pixels, masks, n, S, S, ch, images.data(), bin.as<uint8_t>(), mask_lat.data(),
-                               flags.as<int32_t>()));
-        // 4: VAE encode of [image, masked] per inpaint (pipeline.rs:276-289).
-        Tensor z(ctx, 2 * n, L, L, 4);
-        for (int64_t b0 = 0; b0 < 2 * n; b0 += vae_chunk) {
-            const int64_t b = std::min(vae_chunk, 2 * n - b0);
-            Tensor zi = vae->encode(Tensor::view(ctx, images.item(b0), b, S, S, 3), noise_vae + b0 * lhw * 4);
-            check_cuda(cudaMemcpyAsync(z.item(b0), zi.data(), size_t(zi.size()) * 4, cudaMemcpyDeviceToDevice,
-                                       ctx->stream),
-                       "latents");
+        {
+            PoolBuf bin(ctx, size_t(n * S * S));
+            ck(mbx_inpaint_prepare(ctx, images8, masks, n, S, S, ch, images.data(), bin.as<uint8_t>(),
+                                   mask_lat.data(), flags));
         }
+        Tensor z(ctx, 2 * n, L, L, 4);
+        encode(images, noise.vae, mask_lat, n, ep.roi_encode, z);
         images = Tensor();
         report(0, 1, 1);
 
         // 6-7: starting latents.
-        const Ddim ddim(ep.steps, ep.strength, false);
+        const Ddim ddim(ep.steps, ep.strength, ep.trailing);
         const std::vector<int64_t>& ts = ddim.timesteps;
         Tensor x(ctx, n, L, L, 4);
         {
             const float a0 = ddim.ac[size_t(ts.empty() ? 0 : ts[0])];
-            ck(mbx_latents_init(ctx, z.data(), noise_init, noise_offset, n, lhw, ep.noise_offset, std::sqrt(a0),
+            ck(mbx_latents_init(ctx, z.data(), noise.init, noise.offset, n, lhw, ep.noise_offset, std::sqrt(a0),
                                 std::sqrt(1.0f - a0), ddim.pure_noise_start ? 1 : 0, x.data()));
         }
 
-        // 8: denoise (pipeline.rs:313-345), CFG at batch 2n.
+        // 8: denoise (pipeline.rs:313-346): CFG at batch 2n for the first cfg_steps steps (all of
+        // them by default), conditional-only at batch n after; DDIM or DPM-Solver++(2M).
         if (!ts.empty()) {
-            UNetRunner& r = runner(2 * n, 2);
             const int64_t tp = unet->shape().time_proj;
             float* host_sin = nullptr;
             check_cuda(cudaHostAlloc((void**)&host_sin, ts.size() * size_t(2 * n * tp) * 4, cudaHostAllocDefault),
@@ -307,22 +469,41 @@ struct mbx_engine {
                 for (int64_t it = 0; it < 2 * n; ++it)
                     std::memcpy(host_sin + (i * size_t(2 * n) + size_t(it)) * size_t(tp), one.data(), size_t(tp) * 4);
             }
+            Tensor x0_prev;
+            if (ep.dpm) x0_prev = Tensor(ctx, n, L, L, 4);
+            bool has_prev = false;
+            double lambda_prev = 0.0;
             for (size_t i = 0; i < ts.size(); ++i) {
-                check_cuda(cudaMemcpyAsync(r.sin.data(), host_sin + i * size_t(2 * n * tp), size_t(2 * n * tp) * 4,
+                const bool cfg = ep.cfg_steps < 0 || (int64_t)i < ep.cfg_steps;
+                const int copies = cfg ? 2 : 1;
+                UNetRunner& r = runner(copies * n, copies);
+                check_cuda(cudaMemcpyAsync(r.sin.data(), host_sin + i * size_t(2 * n * tp), size_t(copies * n * tp) * 4,
                                            cudaMemcpyHostToDevice, ctx->stream),
                            "timestep embedding");
-                ck(mbx_unet_input(ctx, x.data(), mask_lat.data(), z.data(), n, lhw, 2, r.x.data()));
+                ck(mbx_unet_input(ctx, x.data(), mask_lat.data(), z.data(), n, lhw, copies, r.x.data()));
                 launch(r);
-                float coef[4];
-                ddim.step_coef(ts[i], coef);
-                ck(mbx_cfg_ddim_step(ctx, r.eps.data(), n, lhw, 2, ep.guidance, coef, x.data()));
+                if (!ep.dpm) {
+                    float coef[4];
+                    ddim.step_coef(ts[i], coef);
+                    ck(mbx_cfg_ddim_step(ctx, r.eps.data(), n, lhw, copies, ep.guidance, coef, x.data()));
+                } else {
+                    if (ep.cfg_steps == (int64_t)i) has_prev = false;  // guidance switched off: restart
+                    float coef[5];
+                    int order = 0;
+                    dpm_step_coef(ddim, i, has_prev, lambda_prev, coef, &order);
+                    ck(mbx_cfg_dpm_step(ctx, r.eps.data(), n, lhw, copies, ep.guidance, coef, order, x.data(),
+                                        x0_prev.data()));
+                    double a, sg;
+                    dpm_abl(ddim, ts[i], a, sg, lambda_prev);
+                    has_prev = true;
+                }
                 report(1, (uint32_t)(i + 1), (uint32_t)ts.size());
             }
         }
         z = Tensor();
         mask_lat = Tensor();
 
-        // 9: decode; 10: 8-bit result and feathered paste (pipeline.rs:355-372, blend.rs:174-215).
+        // 9: decode (pipeline.rs:355-366).
         report(2, 0, 1);
         Tensor dec(ctx, n, S, S, 3);
         for (int64_t b0 = 0; b0 < n; b0 += vae_chunk) {
@@ -333,9 +514,36 @@ struct mbx_engine {
                        "decoded images");
         }
         report(2, 1, 1);
-        PoolBuf blurred(ctx, size_t(n * S * S)), scratch(ctx, size_t(n * S * S));
-        ck(mbx_gaussian_blur_u8(ctx, bin.as<uint8_t>(), n, S, S, 3.0f, scratch.as<uint8_t>(), blurred.as<uint8_t>()));
-        ck(mbx_feather_paste(ctx, dec.data(), blurred.as<uint8_t>(), pixels, n, S, S, ch, flags.as<int32_t>()));
+        return dec;
+    }
+
+    // Device-buffer batch inpaint of model-size images, each used whole (src/pipeline.rs:163-373
+    // for n inpaints at once; a model-size window is its own source rectangle, crop.rs:11-14).
+    void inpaint_device(uint8_t* pixels, const uint8_t* masks, int64_t n, int64_t S, int64_t ch,
+                        const mbx_inpaint_params* params, const float* noise_vae, const float* noise_init,
+                        const float* noise_offset, mbx_progress_fn progress, void* user) {
+        const Params ep = resolve(params);
+        MBX_REQUIRE(S == side(), "images must be " + std::to_string(side()) + " x " + std::to_string(side()) +
+                                     " (the model size) in the batch call; mbx_inpaint takes any size");
+        MBX_REQUIRE(ch == 3 || ch == 4, "image must be RGB or RGBA");
+        if (n == 0) return;
+        const Noise noise = noise_for(n, ep.seed, noise_vae, noise_init, noise_offset);
+        const uint8_t* m = masks;
+        PoolBuf dilated;
+        if (ep.mask_dilate > 0) {  // pipeline.rs:191-197
+            dilated = PoolBuf(ctx, size_t(n * S * S));
+            PoolBuf scratch(ctx, size_t(n * S * S));
+            ck(mbx_mask_dilate(ctx, masks, n, S, S, S, ep.mask_dilate, scratch.as<uint8_t>(), dilated.as<uint8_t>()));
+            m = dilated.as<uint8_t>();
+        }
+        PoolBuf flags(ctx, size_t(n) * 4);
+        Tensor dec = run_model(pixels, ch, m, n, ep, noise, flags.as<int32_t>(), reporter(progress, user));
+        // 10: 8-bit result and the paste; an empty mask leaves its image untouched (pipeline.rs:198-200).
+        PoolBuf res(ctx, size_t(n * S * S * 3));
+        ck(mbx_model_to_window(ctx, dec.data(), n, S, S, res.as<uint8_t>()));
+        dec = Tensor();
+        ck(mbx_paste(ctx, pixels, n, S * ch, ch, m, S, 0, 0, S, S, S, S, 0, 0, S, res.as<uint8_t>(), ep.paste,
+                     flags.as<int32_t>()));
     }
 
     void inpaint_host(uint8_t* pixels, const uint8_t* masks, int64_t n, int64_t S, int64_t ch,
@@ -359,6 +567,67 @@ struct mbx_engine {
                        di ? di.data() : nullptr, dof ? dof.data() : nullptr, progress, user);
         check_cuda(cudaMemcpyAsync(pixels, dp.p, size_t(n * S * S * ch), cudaMemcpyDeviceToHost, ctx->stream), "pixels");
         check_cuda(cudaStreamSynchronize(ctx->stream), "inpaint");
+    }
+
+    // One host image of any size (src/pipeline.rs:163-213): dilation, bbox, square crop window,
+    // Lanczos3 to the model size, the model, Lanczos3 back, paste. Only the source rectangle plus
+    // the blur margin travels to the device and only the source rectangle comes back; nothing is
+    // written before the last cancellation point. Returns the changed rectangle.
+    mbx_rect inpaint_any(uint8_t* pixels, int64_t w, int64_t h, int64_t stride, int64_t ch, const uint8_t* mask,
+                         int64_t mask_stride, const mbx_inpaint_params* params, const float* nv, const float* ni,
+                         const float* no, mbx_progress_fn progress, void* user) {
+        const Params ep = resolve(params);
+        const int64_t S = side();
+        PoolBuf dm(ctx, size_t(w * h));
+        check_cuda(cudaMemcpy2DAsync(dm.p, size_t(w), mask, size_t(mask_stride), size_t(w), size_t(h),
+                                     cudaMemcpyHostToDevice, ctx->stream),
+                   "mask");
+        const uint8_t* m = dm.as<uint8_t>();
+        PoolBuf dilated;
+        if (ep.mask_dilate > 0) {
+            dilated = PoolBuf(ctx, size_t(w * h));
+            PoolBuf scratch(ctx, size_t(w * h));
+            ck(mbx_mask_dilate(ctx, m, 1, h, w, w, ep.mask_dilate, scratch.as<uint8_t>(), dilated.as<uint8_t>()));
+            m = dilated.as<uint8_t>();
+        }
+        int32_t hb[4];
+        {
+            PoolBuf box(ctx, 16);
+            ck(mbx_mask_bbox(ctx, m, 1, h, w, w, box.as<int32_t>()));
+            check_cuda(cudaMemcpyAsync(hb, box.p, 16, cudaMemcpyDeviceToHost, ctx->stream), "bbox");
+            check_cuda(cudaStreamSynchronize(ctx->stream), "bbox");
+        }
+        if (hb[2] < 0) return mbx_rect{0, 0, 0, 0};  // empty mask: nothing to do (pipeline.rs:198-200)
+        const CropWindow c = crop_window(hb[0], hb[1], hb[2] - hb[0] + 1, hb[3] - hb[1] + 1, w, h, S);
+        const mbx_rect src = source_rect(c, w, h);
+        const int64_t margin = 16;  // the paste's blur margin (blend.rs:102)
+        const int64_t rx0 = std::max<int64_t>(src.x - margin, 0), ry0 = std::max<int64_t>(src.y - margin, 0);
+        const int64_t rx1 = std::min<int64_t>(src.x + src.width + margin, w);
+        const int64_t ry1 = std::min<int64_t>(src.y + src.height + margin, h);
+        const int64_t rw = rx1 - rx0, rh = ry1 - ry0;
+        PoolBuf img(ctx, size_t(rw * rh * ch));
+        check_cuda(cudaMemcpy2DAsync(img.p, size_t(rw * ch), pixels + ry0 * stride + rx0 * ch, size_t(stride),
+                                     size_t(rw * ch), size_t(rh), cudaMemcpyHostToDevice, ctx->stream),
+                   "pixels");
+        const uint8_t* mr = m + ry0 * w + rx0;
+        PoolBuf rgb8(ctx, size_t(S * S * 3)), bin8(ctx, size_t(S * S));
+        ck(mbx_window_to_model(ctx, img.as<uint8_t>(), rw * ch, ch, mr, w, rx0, ry0, rw, rh, w, h, c.x, c.y, c.side, S,
+                               rgb8.as<uint8_t>(), bin8.as<uint8_t>()));
+        const Noise noise = noise_for(1, ep.seed, nv, ni, no);
+        PoolBuf flags(ctx, 4);
+        Tensor dec = run_model(rgb8.as<uint8_t>(), 3, bin8.as<uint8_t>(), 1, ep, noise, flags.as<int32_t>(),
+                               reporter(progress, user));
+        PoolBuf res(ctx, size_t(c.side * c.side * 3));
+        ck(mbx_model_to_window(ctx, dec.data(), 1, S, c.side, res.as<uint8_t>()));
+        dec = Tensor();
+        ck(mbx_paste(ctx, img.as<uint8_t>(), 1, rw * ch, ch, mr, w, rx0, ry0, rw, rh, w, h, c.x, c.y, c.side,
+                     res.as<uint8_t>(), ep.paste, nullptr));
+        check_cuda(cudaMemcpy2DAsync(pixels + src.y * stride + src.x * ch, size_t(stride),
+                                     img.as<uint8_t>() + ((src.y - ry0) * rw + (src.x - rx0)) * ch, size_t(rw * ch),
+                                     size_t(src.width * ch), size_t(src.height), cudaMemcpyDeviceToHost, ctx->stream),
+                   "pixels");
+        check_cuda(cudaStreamSynchronize(ctx->stream), "inpaint");
+        return src;
     }
 };
 
@@ -442,35 +711,48 @@ int32_t mbx_engine_info(const mbx_engine* engine, int64_t* latent_side, int64_t*
     });
 }
 
-int32_t mbx_inpaint(mbx_engine* engine, uint8_t* pixels, uint32_t width, uint32_t height, uint32_t stride,
-                    uint32_t channels, const uint8_t* mask, uint32_t mask_stride, const mbx_inpaint_params* params,
-                    mbx_progress_fn progress, void* user, mbx_rect* changed) {
+int32_t mbx_inpaint_with_noise(mbx_engine* engine, uint8_t* pixels, uint32_t width, uint32_t height, uint32_t stride,
+                               uint32_t channels, const uint8_t* mask, uint32_t mask_stride,
+                               const mbx_inpaint_params* params, const float* noise_vae, const float* noise_init,
+                               const float* noise_offset, mbx_progress_fn progress, void* user, mbx_rect* changed) {
     return eguard([&] {
         require_engine(engine);
         if (changed) *changed = mbx_rect{0, 0, 0, 0};
+        // Argument checks in the reference's order (src/ffi.rs:207-214, src/pipeline.rs:172-190).
         MBX_REQUIRE(pixels != nullptr && mask != nullptr, "null argument");
+        MBX_REQUIRE(width > 0 && height > 0 && (uint64_t)stride >= (uint64_t)width * channels && mask_stride >= width,
+                    "bad dimensions or stride");
         MBX_REQUIRE(channels == 3 || channels == 4, "image must be RGB or RGBA");
-        MBX_REQUIRE(width > 0 && height > 0, "empty image");
-        MBX_REQUIRE(stride >= width * channels && mask_stride >= width,
-                    "buffer smaller than width, height and stride imply");
         (void)resolve(params);
+        MBX_REQUIRE(!noise_vae == !noise_init && !noise_vae == !noise_offset, "give all three noise tensors or none");
         use(engine);
-        const int64_t S = engine->side();
-        MBX_REQUIRE(width == S && height == S, "image must be " + std::to_string(S) + " x " + std::to_string(S) +
-                                                   " (the model size; crop-window resampling is not part of this library)");
-        // Tightly packed copies; an empty mask changes nothing (src/pipeline.rs:202-204).
-        std::vector<uint8_t> px(size_t(S * S * channels)), mk(size_t(S * S));
-        bool any = false;
-        for (int64_t y = 0; y < S; ++y) {
-            std::memcpy(px.data() + y * S * channels, pixels + y * stride, size_t(S * channels));
-            std::memcpy(mk.data() + y * S, mask + y * mask_stride, size_t(S));
-            for (int64_t x = 0; x < S && !any; ++x) any = mk[size_t(y * S + x)] >= 128;
+        mbx_ctx* ctx = engine->ctx;
+        const int64_t L = engine->latent();
+        Tensor dv, di, dof;
+        if (noise_vae) {
+            dv = Tensor(ctx, 2, L, L, 4);
+            di = Tensor(ctx, 1, L, L, 4);
+            dof = Tensor(ctx, 1, 1, 1, 4);
+            check_cuda(cudaMemcpyAsync(dv.data(), noise_vae, size_t(dv.size()) * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "noise");
+            check_cuda(cudaMemcpyAsync(di.data(), noise_init, size_t(di.size()) * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "noise");
+            check_cuda(cudaMemcpyAsync(dof.data(), noise_offset, size_t(dof.size()) * 4, cudaMemcpyHostToDevice,
+                                       ctx->stream),
+                       "noise");
         }
-        if (!any) return;
-        engine->inpaint_host(px.data(), mk.data(), 1, S, channels, params, nullptr, nullptr, nullptr, progress, user);
-        for (int64_t y = 0; y < S; ++y) std::memcpy(pixels + y * stride, px.data() + y * S * channels, size_t(S * channels));
-        if (changed) *changed = mbx_rect{0, 0, (uint32_t)S, (uint32_t)S};
+        const mbx_rect r = engine->inpaint_any(pixels, width, height, stride, channels, mask, mask_stride, params,
+                                               dv ? dv.data() : nullptr, di ? di.data() : nullptr,
+                                               dof ? dof.data() : nullptr, progress, user);
+        if (changed) *changed = r;
     });
+}
+
+int32_t mbx_inpaint(mbx_engine* engine, uint8_t* pixels, uint32_t width, uint32_t height, uint32_t stride,
+                    uint32_t channels, const uint8_t* mask, uint32_t mask_stride, const mbx_inpaint_params* params,
+                    mbx_progress_fn progress, void* user, mbx_rect* changed) {
+    return mbx_inpaint_with_noise(engine, pixels, width, height, stride, channels, mask, mask_stride, params, nullptr,
+                                  nullptr, nullptr, progress, user, changed);
 }
 
 int32_t mbx_inpaint_batch(mbx_engine* engine, uint8_t* pixels, const uint8_t* masks, int64_t n, uint32_t side,
@@ -550,6 +832,24 @@ int32_t mbx_ddim_timesteps(uint32_t steps, double strength, int32_t trailing, in
         const Ddim d((int)steps, strength, trailing != 0);
         for (size_t i = 0; i < d.timesteps.size(); ++i) out[i] = d.timesteps[i];
         *count = (int64_t)d.timesteps.size();
+    });
+}
+
+int32_t mbx_dpm_coefficients(uint32_t steps, double strength, int32_t trailing, int64_t i, int64_t restart_at,
+                             float coef[5], int32_t* order) {
+    return eguard([&] {
+        MBX_REQUIRE(coef != nullptr && order != nullptr, "null argument");
+        const Ddim d((int)steps, strength, trailing != 0);
+        MBX_REQUIRE(i >= 0 && i < (int64_t)d.timesteps.size(), "step index outside the schedule");
+        double lambda_prev = 0.0;
+        const bool has_prev = i > 0 && i != restart_at;
+        if (has_prev) {
+            double a, s;
+            dpm_abl(d, d.timesteps[size_t(i - 1)], a, s, lambda_prev);
+        }
+        int o = 0;
+        dpm_step_coef(d, size_t(i), has_prev, lambda_prev, coef, &o);
+        *order = o;
     });
 }
 

@@ -14,6 +14,7 @@
 //    (pipeline.rs:318-322, unet/mod.rs:226-231).
 //  * cfg_ddim_step: ε = ε_u + g·(ε_c − ε_u) and the η = 0 DDIM update
 //    (pipeline.rs:323-336, scheduler.rs:87-97).
+//  * cfg_dpm_step: the same ε and one DPM-Solver++(2M) update (scheduler.rs:107-152).
 //  * blur_lines: Pillow's 3-pass fractional box blur along rows or columns in
 //    24-bit fixed point (blend.rs:41-100), byte-exact.
 //  * feather_paste: 8-bit truncation of the decoded image and the feathered
@@ -21,6 +22,8 @@
 // Every f32 / f64 expression is written with explicitly rounded operations so
 // that no multiply-add is contracted: the results follow the reference's
 // operation order exactly.
+#include <cmath>
+
 #include "mbx_device.cuh"
 #include "mbx_internal.h"
 
@@ -116,6 +119,38 @@ __global__ void cfg_ddim_kernel(const float* __restrict__ eps, int64_t n, int64_
     }
 }
 
+// ε (guidance combine, or the cond-only copy), the data prediction x0 = (x − σ·ε)·(1/α) and the
+// DPM-Solver++(2M) update (scheduler.rs:121-151): order 0 = the last step (x = x0); 1 = first
+// order x = keep·x + φ·x0; 2 = second order x = keep·x + c0·x0 − c1·x0_prev. x0 is kept in x0_prev
+// for the next step.
+__global__ void cfg_dpm_kernel(const float* __restrict__ eps, int64_t n, int64_t per, int copies, float guidance,
+                               float sigma, float inv_alpha, float keep, float c0, float c1, int order,
+                               float* __restrict__ x, float* __restrict__ x0_prev) {
+    const int64_t total = n * per;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = e / per, r = e - i * per;
+        float ep;
+        if (copies == 2) {
+            const float u = eps[(2 * i) * per + r], c = eps[(2 * i + 1) * per + r];
+            ep = __fadd_rn(u, __fmul_rn(guidance, __fsub_rn(c, u)));
+        } else {
+            ep = eps[i * per + r];
+        }
+        const float xv = x[e];
+        const float x0 = __fmul_rn(__fsub_rn(xv, __fmul_rn(sigma, ep)), inv_alpha);
+        float out;
+        if (order == 0) {
+            out = x0;
+        } else if (order == 1) {
+            out = __fadd_rn(__fmul_rn(keep, xv), __fmul_rn(c0, x0));
+        } else {
+            out = __fsub_rn(__fadd_rn(__fmul_rn(keep, xv), __fmul_rn(c0, x0)), __fmul_rn(c1, x0_prev[e]));
+        }
+        x[e] = out;
+        if (order != 0) x0_prev[e] = x0;
+    }
+}
+
 // One CTA per line; `passes` fractional box passes with 8-bit rounding after each.
 __global__ void blur_lines_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t lines_per_item,
                                   int64_t item_stride, int64_t line_stride, int64_t elem_stride, int len, int radius,
@@ -201,6 +236,14 @@ void launch_cfg_ddim(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int
     after_launch(ctx, "cfg_ddim_step");
 }
 
+void launch_cfg_dpm(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int copies, float guidance,
+                    const float coef[5], int order, float* x, float* x0_prev) {
+    cfg_dpm_kernel<<<grid_for(ctx, n * per, 256), 256, 0, ctx->stream>>>(eps, n, per, copies, guidance, coef[0],
+                                                                        coef[1], coef[2], coef[3], coef[4], order, x,
+                                                                        x0_prev);
+    after_launch(ctx, "cfg_dpm_step");
+}
+
 void launch_blur_lines(mbx_ctx* ctx, const uint8_t* in, uint8_t* out, int64_t lines, int64_t lines_per_item,
                        int64_t item_stride, int64_t line_stride, int64_t elem_stride, int len, int radius,
                        uint32_t ww, uint32_t fw, int passes) {
@@ -216,6 +259,37 @@ void launch_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blur
     feather_paste_kernel<<<grid_for(ctx, pixels, 256), 256, 0, ctx->stream>>>(result, blurred, image, pixels,
                                                                             item_pixels, ch, nonempty);
     after_launch(ctx, "feather_paste");
+}
+
+namespace {
+// Pillow's _gaussian_blur_radius in f32 with f64 sqrt / floor (src/imaging/blend.rs:26-39).
+float gaussian_box_radius(float sigma, uint32_t passes) {
+    const float sigma2 = sigma * sigma / (float)passes;
+    const float big_l = (float)std::sqrt(12.0 * (double)sigma2 + 1.0);
+    const float l = (float)std::floor(((double)big_l - 1.0) / 2.0);
+    float a = (2.0f * l + 1.0f) * (l * (l + 1.0f) - 3.0f * sigma2);
+    a /= 6.0f * (sigma2 - (l + 1.0f) * (l + 1.0f));
+    return l + a;
+}
+}  // namespace
+
+void gaussian_blur(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t h, int64_t w, float radius, uint8_t* scratch,
+                   uint8_t* out) {
+    MBX_REQUIRE(h <= 16384 && w <= 16384, "blur: sides above 16384");
+    if (n * h * w == 0) return;
+    if (!(radius > 0.0f)) {
+        if (out != in)
+            check_cuda(cudaMemcpyAsync(out, in, size_t(n * h * w), cudaMemcpyDeviceToDevice, ctx->stream),
+                       "blur copy");
+        return;
+    }
+    const uint32_t passes = 3;
+    const float fr = gaussian_box_radius(radius, passes);
+    const int rad = (int)fr;
+    const uint32_t ww = (uint32_t)((float)(1u << 24) / (fr * 2.0f + 1.0f));
+    const uint32_t fw = ((1u << 24) - (uint32_t)(rad * 2 + 1) * ww) / 2;
+    launch_blur_lines(ctx, in, scratch, n * h, h, h * w, w, 1, (int)w, rad, ww, fw, (int)passes);
+    launch_blur_lines(ctx, scratch, out, n * w, w, h * w, 1, w, (int)h, rad, ww, fw, (int)passes);
 }
 
 }  // namespace mbx

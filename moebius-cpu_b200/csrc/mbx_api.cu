@@ -818,18 +818,6 @@ int32_t mbx_cfg_ddim_step(mbx_ctx* ctx, const float* eps, int64_t n, int64_t hw,
     });
 }
 
-namespace {
-// Pillow's _gaussian_blur_radius in f32 with f64 sqrt / floor (src/imaging/blend.rs:26-39).
-float gaussian_box_radius(float sigma, uint32_t passes) {
-    const float sigma2 = sigma * sigma / (float)passes;
-    const float big_l = (float)std::sqrt(12.0 * (double)sigma2 + 1.0);
-    const float l = (float)std::floor(((double)big_l - 1.0) / 2.0);
-    float a = (2.0f * l + 1.0f) * (l * (l + 1.0f) - 3.0f * sigma2);
-    a /= 6.0f * (sigma2 - (l + 1.0f) * (l + 1.0f));
-    return l + a;
-}
-}  // namespace
-
 int32_t mbx_gaussian_blur_u8(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t h, int64_t w, float radius,
                              uint8_t* scratch, uint8_t* out) {
     return guard([&] {
@@ -840,20 +828,8 @@ int32_t mbx_gaussian_blur_u8(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t
         require_ptr(in, "in");
         require_ptr(out, "out");
         use_device(ctx);
-        if (!(radius > 0.0f)) {
-            if (out != in)
-                check_cuda(cudaMemcpyAsync(out, in, size_t(n * h * w), cudaMemcpyDeviceToDevice, ctx->stream),
-                           "blur copy");
-            return;
-        }
-        require_ptr(scratch, "scratch");
-        const uint32_t passes = 3;
-        const float fr = gaussian_box_radius(radius, passes);
-        const int rad = (int)fr;
-        const uint32_t ww = (uint32_t)((float)(1u << 24) / (fr * 2.0f + 1.0f));
-        const uint32_t fw = ((1u << 24) - (uint32_t)(rad * 2 + 1) * ww) / 2;
-        mbx::launch_blur_lines(ctx, in, scratch, n * h, h, h * w, w, 1, (int)w, rad, ww, fw, (int)passes);
-        mbx::launch_blur_lines(ctx, scratch, out, n * w, w, h * w, 1, w, (int)h, rad, ww, fw, (int)passes);
+        if (radius > 0.0f) require_ptr(scratch, "scratch");
+        mbx::gaussian_blur(ctx, in, n, h, w, radius, scratch, out);
     });
 }
 
@@ -869,6 +845,148 @@ int32_t mbx_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blur
         require_ptr(image, "image");
         use_device(ctx);
         mbx::launch_feather_paste(ctx, result, blurred, image, n * h * w, h * w, (int)channels, nonempty);
+    });
+}
+
+int32_t mbx_cfg_dpm_step(mbx_ctx* ctx, const float* eps, int64_t n, int64_t hw, int64_t copies, float guidance,
+                         const float coef[5], int32_t order, float* x, float* x0_prev) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && hw >= 0, "bad shape");
+        MBX_REQUIRE(copies == 1 || copies == 2, "copies must be 1 (cond only) or 2 (uncond, cond)");
+        MBX_REQUIRE(order >= 0 && order <= 2, "order must be 0, 1 or 2");
+        if (n * hw == 0) return;
+        require_ptr(eps, "eps");
+        require_ptr(coef, "coef");
+        require_ptr(x, "x");
+        if (order > 0) require_ptr(x0_prev, "x0_prev");
+        use_device(ctx);
+        mbx::launch_cfg_dpm(ctx, eps, n, hw * 4, (int)copies, guidance, coef, order, x, x0_prev);
+    });
+}
+
+int32_t mbx_crop_window(uint32_t bx, uint32_t by, uint32_t bw, uint32_t bh, uint32_t width, uint32_t height,
+                        int64_t model_side, int64_t window[3], mbx_rect* source) {
+    return guard([&] {
+        MBX_REQUIRE(window != nullptr, "null argument");
+        MBX_REQUIRE(width > 0 && height > 0 && model_side > 0, "empty image");
+        MBX_REQUIRE(bw > 0 && bh > 0 && (uint64_t)bx + bw <= width && (uint64_t)by + bh <= height,
+                    "mask bbox outside the image");
+        const mbx::CropWindow c = mbx::crop_window(bx, by, bw, bh, width, height, model_side);
+        window[0] = c.x;
+        window[1] = c.y;
+        window[2] = c.side;
+        if (source) *source = mbx::source_rect(c, width, height);
+    });
+}
+
+int32_t mbx_lanczos_table(int64_t in_size, int64_t out_size, int32_t* bounds, int32_t* coeffs, int64_t* ksize) {
+    return guard([&] {
+        MBX_REQUIRE(ksize != nullptr, "null argument");
+        MBX_REQUIRE(in_size > 0 && out_size > 0 && in_size <= (1 << 20) && out_size <= (1 << 20), "bad sizes");
+        MBX_REQUIRE(!bounds || coeffs, "coeffs must accompany bounds");
+        mbx::lanczos_table(in_size, out_size, bounds, coeffs, ksize);
+    });
+}
+
+int32_t mbx_mask_dilate(mbx_ctx* ctx, const uint8_t* mask, int64_t n, int64_t h, int64_t w, int64_t mask_stride,
+                        int64_t k, uint8_t* scratch, uint8_t* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0 && mask_stride >= w && k >= 0, "bad shape");
+        if (n * h * w == 0) return;
+        require_ptr(mask, "mask");
+        require_ptr(out, "out");
+        if (k > 1) require_ptr(scratch, "scratch");
+        use_device(ctx);
+        mbx::launch_mask_dilate(ctx, mask, n, h, w, mask_stride, k, scratch, out);
+    });
+}
+
+int32_t mbx_mask_bbox(mbx_ctx* ctx, const uint8_t* mask, int64_t n, int64_t h, int64_t w, int64_t mask_stride,
+                      int32_t* box) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h > 0 && w > 0 && mask_stride >= w, "bad shape");
+        MBX_REQUIRE(h * w < INT32_MAX, "mask too large");
+        if (n == 0) return;
+        require_ptr(mask, "mask");
+        require_ptr(box, "box");
+        MBX_REQUIRE(n <= 65535, "at most 65535 masks per call");
+        use_device(ctx);
+        mbx::launch_mask_bbox(ctx, mask, n, h, w, mask_stride, box);
+    });
+}
+
+namespace {
+void require_region(int64_t stride, int64_t channels, int64_t mask_stride, int64_t origin_x, int64_t origin_y,
+                    int64_t region_w, int64_t region_h, int64_t width, int64_t height) {
+    MBX_REQUIRE(channels == 3 || channels == 4, "image must be RGB or RGBA");
+    MBX_REQUIRE(width > 0 && height > 0, "empty image");
+    MBX_REQUIRE(region_w > 0 && region_h > 0 && origin_x >= 0 && origin_y >= 0 && origin_x + region_w <= width &&
+                    origin_y + region_h <= height,
+                "region outside the image");
+    MBX_REQUIRE(stride >= region_w * channels && mask_stride >= region_w,
+                "buffer smaller than width, height and stride imply");
+}
+}  // namespace
+
+int32_t mbx_window_to_model(mbx_ctx* ctx, const uint8_t* image, int64_t stride, int64_t channels,
+                            const uint8_t* mask, int64_t mask_stride, int64_t origin_x, int64_t origin_y,
+                            int64_t region_w, int64_t region_h, int64_t width, int64_t height, int64_t win_x,
+                            int64_t win_y, int64_t side, int64_t model_side, uint8_t* rgb_out, uint8_t* bin_out) {
+    return guard([&] {
+        require_ctx(ctx);
+        require_region(stride, channels, mask_stride, origin_x, origin_y, region_w, region_h, width, height);
+        MBX_REQUIRE(side > 0 && model_side > 0 && side <= (1 << 16) && model_side <= (1 << 16), "bad window");
+        // Edge replication reads the window's part inside the image: the region must hold it.
+        const int64_t sx0 = std::max<int64_t>(win_x, 0), sy0 = std::max<int64_t>(win_y, 0);
+        const int64_t sx1 = std::min<int64_t>(win_x + side, width), sy1 = std::min<int64_t>(win_y + side, height);
+        MBX_REQUIRE(sx1 > sx0 && sy1 > sy0, "window outside the image");
+        MBX_REQUIRE(sx0 >= origin_x && sy0 >= origin_y && sx1 <= origin_x + region_w && sy1 <= origin_y + region_h,
+                    "region does not cover the window's part inside the image");
+        require_ptr(image, "image");
+        require_ptr(mask, "mask");
+        require_ptr(rgb_out, "rgb_out");
+        require_ptr(bin_out, "bin_out");
+        use_device(ctx);
+        // Clamped coordinates stay inside [sx0, sx1) x [sy0, sy1), which the region covers.
+        mbx::launch_window_to_model(ctx, image, stride, channels, mask, mask_stride, origin_x, origin_y, width, height,
+                                    win_x, win_y, side, model_side, rgb_out, bin_out);
+    });
+}
+
+int32_t mbx_model_to_window(mbx_ctx* ctx, const float* rgb, int64_t n, int64_t model_side, int64_t side,
+                            uint8_t* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && model_side > 0 && side > 0 && side <= (1 << 16) && model_side <= (1 << 16),
+                    "bad shape");
+        if (n == 0) return;
+        require_ptr(rgb, "rgb");
+        require_ptr(out, "out");
+        use_device(ctx);
+        mbx::launch_model_to_window(ctx, rgb, n, model_side, side, out);
+    });
+}
+
+int32_t mbx_paste(mbx_ctx* ctx, uint8_t* image, int64_t n, int64_t stride, int64_t channels, const uint8_t* mask,
+                  int64_t mask_stride, int64_t origin_x, int64_t origin_y, int64_t region_w, int64_t region_h,
+                  int64_t width, int64_t height, int64_t win_x, int64_t win_y, int64_t side, const uint8_t* result,
+                  uint32_t mode, const int32_t* active) {
+    return guard([&] {
+        require_ctx(ctx);
+        require_region(stride, channels, mask_stride, origin_x, origin_y, region_w, region_h, width, height);
+        MBX_REQUIRE(mode >= 1 && mode <= 3, "paste mode must be NONE (1), FEATHER (2) or FEATHER_COMPENSATE (3)");
+        MBX_REQUIRE(n >= 0 && side > 0 && side <= (1 << 16), "bad shape");
+        MBX_REQUIRE(n <= 65535, "at most 65535 images per call");
+        if (n == 0) return;
+        require_ptr(image, "image");
+        require_ptr(mask, "mask");
+        require_ptr(result, "result");
+        use_device(ctx);
+        mbx::launch_paste(ctx, image, n, stride, channels, mask, mask_stride, origin_x, origin_y, region_w, region_h,
+                          width, height, win_x, win_y, side, result, mode, active);
     });
 }
 

@@ -157,6 +157,61 @@ void launch_cfg_ddim(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int
 void launch_blur_lines(mbx_ctx* ctx, const uint8_t* in, uint8_t* out, int64_t lines, int64_t lines_per_item,
                        int64_t item_stride, int64_t line_stride, int64_t elem_stride, int len, int radius,
                        uint32_t ww, uint32_t fw, int passes);
+// The square crop window around a mask bbox (reference CropPlan::new, src/imaging/crop.rs:30-62):
+// the mask's long side plus half of it on each side, at least min(model side, image long
+// side), at most the image long side; centred on the mask and shifted inside the image when
+// it fits, else centred on the image (negative origin = padding).
+struct CropWindow {
+    int64_t x, y, side;
+};
+
+inline int64_t place_window(int64_t start, int64_t len, int64_t side, int64_t extent) {
+    if (side <= extent) {
+        const int64_t centred = (2 * start + len) / 2 - side / 2;
+        return centred < 0 ? 0 : (centred > extent - side ? extent - side : centred);
+    }
+    return -((side - extent) / 2);
+}
+
+inline CropWindow crop_window(int64_t bx, int64_t by, int64_t bw, int64_t bh, int64_t width, int64_t height,
+                              int64_t model_side) {
+    const int64_t lng = bw > bh ? bw : bh;
+    const int64_t img_long = width > height ? width : height;
+    int64_t side = lng + 2 * (lng / 2);
+    const int64_t floor_side = model_side < img_long ? model_side : img_long;
+    if (side < floor_side) side = floor_side;
+    if (side > img_long) side = img_long;
+    return CropWindow{place_window(bx, bw, side, width), place_window(by, bh, side, height), side};
+}
+
+// The part of the window inside the image (CropPlan::source_rect, crop.rs:44-51).
+inline mbx_rect source_rect(const CropWindow& c, int64_t width, int64_t height) {
+    const int64_t x0 = c.x < 0 ? 0 : c.x, y0 = c.y < 0 ? 0 : c.y;
+    const int64_t x1 = c.x + c.side < width ? c.x + c.side : width;
+    const int64_t y1 = c.y + c.side < height ? c.y + c.side : height;
+    return mbx_rect{(uint32_t)x0, (uint32_t)y0, (uint32_t)(x1 - x0), (uint32_t)(y1 - y0)};
+}
+
+// Imaging around the model window (k_imaging.cu).
+void lanczos_table(int64_t in, int64_t out, int32_t* bounds, int32_t* coeffs, int64_t* ksize);
+void launch_mask_dilate(mbx_ctx* ctx, const uint8_t* mask, int64_t n, int64_t h, int64_t w, int64_t stride, int64_t k,
+                        uint8_t* scratch, uint8_t* out);
+void launch_mask_bbox(mbx_ctx* ctx, const uint8_t* mask, int64_t n, int64_t h, int64_t w, int64_t stride,
+                      int32_t* box);
+void launch_window_to_model(mbx_ctx* ctx, const uint8_t* image, int64_t stride, int64_t channels,
+                            const uint8_t* mask, int64_t mask_stride, int64_t origin_x, int64_t origin_y,
+                            int64_t width, int64_t height, int64_t win_x, int64_t win_y, int64_t side, int64_t model,
+                            uint8_t* rgb, uint8_t* bin);
+void launch_model_to_window(mbx_ctx* ctx, const float* rgb, int64_t n, int64_t model, int64_t side, uint8_t* out);
+void launch_paste(mbx_ctx* ctx, uint8_t* image, int64_t n, int64_t stride, int64_t channels, const uint8_t* mask,
+                  int64_t mask_stride, int64_t origin_x, int64_t origin_y, int64_t region_w, int64_t region_h,
+                  int64_t width, int64_t height, int64_t win_x, int64_t win_y, int64_t side, const uint8_t* result,
+                  uint32_t mode, const int32_t* active);
+// Pillow's GaussianBlur(radius) of n single-channel h × w planes (3 box passes per axis).
+void gaussian_blur(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t h, int64_t w, float radius, uint8_t* scratch,
+                   uint8_t* out);
+void launch_cfg_dpm(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int copies, float guidance,
+                    const float coef[5], int order, float* x, float* x0_prev);
 void launch_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blurred, uint8_t* image, int64_t pixels,
                           int64_t item_pixels, int ch, const int32_t* nonempty);
 
@@ -165,14 +220,31 @@ void launch_matmul_simt(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64
 
 // Scoped pool allocation for per-call scratch (stream-ordered reuse).
 struct PoolBuf {
-    mbx_ctx* ctx;
-    void* p;
+    mbx_ctx* ctx = nullptr;
+    void* p = nullptr;
+    PoolBuf() = default;
     PoolBuf(mbx_ctx* c, size_t bytes) : ctx(c), p(c->pool->alloc(bytes)) {}
-    ~PoolBuf() {
-        try {
-            ctx->pool->free(p);
-        } catch (...) {
+    PoolBuf(const PoolBuf&) = delete;
+    PoolBuf& operator=(const PoolBuf&) = delete;
+    PoolBuf(PoolBuf&& o) noexcept : ctx(o.ctx), p(o.p) { o.p = nullptr; }
+    PoolBuf& operator=(PoolBuf&& o) noexcept {
+        if (this != &o) {
+            release();
+            ctx = o.ctx;
+            p = o.p;
+            o.p = nullptr;
         }
+        return *this;
+    }
+    ~PoolBuf() { release(); }
+    void release() {
+        if (p && ctx) {
+            try {
+                ctx->pool->free(p);
+            } catch (...) {
+            }
+        }
+        p = nullptr;
     }
     template <class T>
     T* as() const {

@@ -58,15 +58,24 @@ class Engine:
         check(lib().mbx_engine_set_stream(self.handle, ctypes.c_void_p(stream_ptr or 0)))
 
     def inpaint(self, pixels: np.ndarray, mask: np.ndarray, p: Optional[InpaintParams] = None,
-                progress: Optional[Callable[[int, int, int], bool]] = None):
-        """In place on an [h, w, 3|4] uint8 image (row stride may exceed w·channels); returns the
-        changed rectangle (x, y, width, height)."""
+                progress: Optional[Callable[[int, int, int], bool]] = None, noise=None):
+        """In place on an [h, w, 3|4] uint8 image of any size (row stride may exceed w·channels);
+        returns the changed rectangle (x, y, width, height). noise = (vae [2, L, L, 4], init
+        [L, L, 4], offset [4]) float32 (mbx_inpaint_with_noise) or None (seeded, mbx_inpaint)."""
         assert pixels.dtype == np.uint8 and mask.dtype == np.uint8
+        assert pixels.strides[1] == pixels.shape[2] and pixels.strides[2] == 1 and mask.strides[1] == 1
         h, w, ch = pixels.shape
         rect = abi.Rect()
         cb = abi.PROGRESS_FN(lambda _u, s, d, t: int(bool(progress(s, d, t)))) if progress else abi.PROGRESS_FN()
-        check(lib().mbx_inpaint(self.handle, _ptr(pixels), w, h, pixels.strides[0], ch, _ptr(mask), mask.strides[0],
-                                ctypes.byref(p) if p is not None else None, cb, None, ctypes.byref(rect)))
+        pp = ctypes.byref(p) if p is not None else None
+        if noise is None:
+            check(lib().mbx_inpaint(self.handle, _ptr(pixels), w, h, pixels.strides[0], ch, _ptr(mask),
+                                    mask.strides[0], pp, cb, None, ctypes.byref(rect)))
+        else:
+            nz = [np.ascontiguousarray(a, np.float32) for a in noise]
+            check(lib().mbx_inpaint_with_noise(self.handle, _ptr(pixels), w, h, pixels.strides[0], ch, _ptr(mask),
+                                               mask.strides[0], pp, *[_ptr(a) for a in nz], cb, None,
+                                               ctypes.byref(rect)))
         return rect.x, rect.y, rect.width, rect.height
 
     def inpaint_batch(self, pixels: np.ndarray, masks: np.ndarray, p: Optional[InpaintParams] = None, noise=None,

@@ -1,7 +1,9 @@
 """TEST INFRASTRUCTURE ONLY: numpy f32 restatement of the reference's DDIM
-scheduler (src/scheduler.rs:19-98,155-169), pinned on its test values
-(src/scheduler.rs:181-255)."""
+scheduler (src/scheduler.rs:19-98,155-169) and DPM-Solver++(2M)
+(src/scheduler.rs:100-152), pinned on its test values (src/scheduler.rs:181-255)."""
 from __future__ import annotations
+
+import math
 
 import numpy as np
 
@@ -52,3 +54,43 @@ class Ddim:
         eps = np.asarray(eps, np.float32)
         x0 = (np.asarray(sample, np.float32) - sqrt_b_t * eps) / sqrt_a_t
         return (sqrt_a_prev * x0 + sqrt_b_prev * eps).astype(np.float32)
+
+
+def dpm_coefficients(ddim: Ddim, t: int):
+    """alpha_t, sigma_t, lambda_t = ln(alpha_t / sigma_t) in f64 (src/scheduler.rs:100-105)."""
+    a = float(ddim.ac[t])
+    alpha, sigma = math.sqrt(a), math.sqrt(1.0 - a)
+    return alpha, sigma, math.log(alpha) - math.log(sigma)
+
+
+class Dpm2M:
+    """DPM-Solver++(2M) (src/scheduler.rs:107-152): first order on the first step and after
+    restart(), second order after that, and the last step lands on the data prediction."""
+
+    def __init__(self):
+        self.prev = None
+
+    def restart(self):
+        self.prev = None
+
+    def step(self, ddim: Ddim, eps, i: int, sample):
+        steps = ddim.timesteps
+        alpha, sigma, lam = dpm_coefficients(ddim, steps[i])
+        inv_alpha, sigma_f = f32(1.0 / alpha), f32(sigma)
+        x = np.asarray(sample, np.float32)
+        x0 = ((x - sigma_f * np.asarray(eps, np.float32)) * inv_alpha).astype(np.float32)
+        if i + 1 >= len(steps):
+            return x0
+        alpha_n, sigma_n, lam_n = dpm_coefficients(ddim, steps[i + 1])
+        h = lam_n - lam
+        keep = f32(sigma_n / sigma)
+        phi = alpha_n * (1.0 - math.exp(-h))
+        if self.prev is None:
+            out = keep * x + f32(phi) * x0
+        else:
+            x0_prev, lam_prev = self.prev
+            r = (lam - lam_prev) / h
+            c0, c1 = f32(phi * (1.0 + 0.5 / r)), f32(phi * 0.5 / r)
+            out = keep * x + c0 * x0 - c1 * x0_prev
+        self.prev = (x0, lam)
+        return out.astype(np.float32)

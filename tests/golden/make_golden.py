@@ -14,11 +14,13 @@
    (plain and upsampled), LayerNorm at UNet widths, and the broadcast adds.
 
 3. ``imaging_ref.safetensors``: the reference's Pillow blur fixture
-   (``tests/fixtures/blur.safetensors``, Pillow 10.4 per its generator), copied,
-   plus two model-size cases written here with the installed Pillow: random
-   filled ellipses covering 10-40 % of a 512² mask (the BASELINE mask
-   distribution), blurred with ``GaussianBlur(3)`` as upstream ``_post_process``
-   does.
+   (``tests/fixtures/blur.safetensors``, Pillow 10.4 per its generator) and its
+   upstream compensated-paste fixture (``tests/fixtures/compensate.safetensors``,
+   names prefixed ``comp.``), copied, plus cases written here with the installed
+   Pillow: two model-size masks of random filled ellipses covering 10-40 % (the
+   BASELINE mask distribution) blurred with ``GaussianBlur(3)`` as upstream
+   ``_post_process`` does, and four Lanczos3 resizes (``lz*``; upstream resizes
+   the crop window with ``Image.LANCZOS``).
 4. ``weights_manifest.json``: every tensor of the converted UNet and VAE
    (name -> shape), derived from the reference's ``docs/weights-manifest.txt``
    with the converter's transformations (BatchNorms folded into new ``.bias``
@@ -152,6 +154,20 @@ def imaging_cases(reference_root):
         blurred = np.asarray(Image.fromarray(m).convert("RGB").filter(ImageFilter.GaussianBlur(radius=3)))[:, :, 0]
         t[f"{k}.mask"] = m
         t[f"{k}.blurred"] = np.ascontiguousarray(blurred, np.uint8)
+    # The reference's upstream paste_compensate fixture (tests/fixtures/compensate.safetensors).
+    comp = load_file(os.path.join(reference_root, "tests", "fixtures", "compensate.safetensors"))
+    for k, v in comp.items():
+        t[f"comp.{k}"] = np.ascontiguousarray(v)
+    # Lanczos3 resizes with Pillow (Image.LANCZOS, the filter upstream resizes the crop window
+    # with): RGB down and up, a mask channel, and a model-size result back to a small window.
+    rng = np.random.default_rng(7)
+    for k, (src, dst, ch) in {"lz1": (300, 128, 3), "lz2": (96, 128, 3), "lz3": (77, 64, 1),
+                              "lz4": (128, 45, 3)}.items():
+        a = rng.integers(0, 256, (src, src, ch), dtype=np.uint8)
+        img = Image.fromarray(a[..., 0] if ch == 1 else a)
+        t[f"{k}.src"] = a
+        out = np.asarray(img.resize((dst, dst), Image.LANCZOS))
+        t[f"{k}.dst"] = np.ascontiguousarray(out.reshape(dst, dst, ch))
     return t, PIL.__version__
 
 
@@ -203,8 +219,8 @@ def main():
     img, pil_version = imaging_cases(args.reference_root)
     save_file(img, os.path.join(HERE, "imaging_ref.safetensors"),
               metadata={"format": "moebius-b200-fixture/1", "generator": "tests/golden/make_golden.py",
-                        "source": "moebius-cpu tests/fixtures/blur.safetensors (a, b, c); e1, e2 from Pillow "
-                                  + pil_version})
+                        "source": "moebius-cpu tests/fixtures/blur.safetensors (a, b, c) and "
+                                  "compensate.safetensors (comp.*); e1, e2, lz* from Pillow " + pil_version})
     import json
     with open(os.path.join(HERE, "weights_manifest.json"), "w") as f:
         json.dump(converted_manifest(args.reference_root), f, indent=0, sort_keys=True)

@@ -1,7 +1,8 @@
 """GPU parity of the engine (include/moebius_cuda_engine.h) against the CPU
 oracle composed in the reference's order: the UNet (src/unet/*), the VAE
-encoder (src/vae/encoder.rs) and the whole Exact inpaint (src/pipeline.rs)
-with caller-supplied noise, on seeded random-init weights in the converter's
+encoder (src/vae/encoder.rs) and whole inpaints (src/pipeline.rs): both
+presets, every paste mode, mask dilation and images of any size, with
+caller-supplied noise, on seeded random-init weights in the converter's
 format. Scaled-down networks of the same structure (widths 64/128/256,
 latent 16; VAE widths 32/64/128/128) keep the oracle fast; the full-size
 network runs one UNet step and a 2-step inpaint. Gates (BASELINE
@@ -159,18 +160,99 @@ def test_single_image_api(mbx, tiny):
     assert np.array_equal(blank, img[0])
 
 
-def test_engine_rejects_unsupported_requests(mbx, tiny):
+def test_engine_rejects_bad_requests(mbx, tiny):
     eng = tiny[0]
     img = np.zeros((64, 64, 3), np.uint8)
-    with pytest.raises(mbx.MbxError) as e:
-        eng.inpaint(img, np.full((64, 64), 255, np.uint8))
-    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
-    img = np.zeros((128, 128, 3), np.uint8)
-    for p in (mbx.engine.params(preset=mbx.abi.PRESET_FAST), mbx.engine.params(mask_dilate=3),
-              mbx.engine.params(steps=1001)):
+    full = np.full((64, 64), 255, np.uint8)
+    for p in (mbx.engine.params(preset=7), mbx.engine.params(paste=9), mbx.engine.params(steps=1001)):
         with pytest.raises(mbx.MbxError) as e:
-            eng.inpaint(img, np.full((128, 128), 255, np.uint8), p)
+            eng.inpaint(img, full, p)
         assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+    with pytest.raises(mbx.MbxError) as e:
+        mbx.check(mbx.abi.lib().mbx_inpaint(eng.handle, img.ctypes.data, 64, 64, 64 * 3 - 1, 3, full.ctypes.data, 64,
+                                            None, mbx.abi.PROGRESS_FN(), None, None))
+    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+    with pytest.raises(mbx.MbxError) as e:
+        mbx.check(mbx.abi.lib().mbx_inpaint(eng.handle, img.ctypes.data, 64, 64, 64 * 2, 2, full.ctypes.data, 64,
+                                            None, mbx.abi.PROGRESS_FN(), None, None))
+    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+    with pytest.raises(mbx.MbxError) as e:  # batch call: model-size images only
+        eng.inpaint_batch(np.zeros((1, 64, 64, 3), np.uint8), full[None])
+    assert e.value.code == mbx.abi.ERR_INVALID_ARGUMENT
+
+
+def _single_noise(rng, lat):
+    return (rng.standard_normal((2, lat, lat, 4)).astype(np.float32),
+            rng.standard_normal((lat, lat, 4)).astype(np.float32),
+            rng.standard_normal(4).astype(np.float32))
+
+
+# Image sizes other than the model side (128 here): a window as large as the image's long
+# side, padded above and below (300 x 200, RGBA with a row stride), a window inside a larger
+# image (700 x 500), an image smaller than the model (90 x 60: upscaled window), each through
+# the crop window, Lanczos3 both ways and the paste.
+@pytest.mark.parametrize("w,h,ch,paste,r", [(300, 200, 4, 0, 0.3), (700, 500, 3, 3, 0.1), (90, 60, 3, 1, 0.2)])
+def test_any_size_inpaint_matches_oracle(mbx, tiny, w, h, ch, paste, r):
+    from oracle import pipeline_ref, unet_ref
+    eng, wu, wv, _ = tiny
+    rng = np.random.default_rng(w + h)
+    img = rng.integers(0, 256, (h, w, ch), dtype=np.uint8)
+    yy, xx = np.mgrid[:h, :w]
+    cy, cx = rng.uniform(0.3, 0.7) * h, rng.uniform(0.3, 0.7) * w
+    mask = (((((yy - cy) / (r * h)) ** 2 + ((xx - cx) / (r * w)) ** 2) <= 1) * 200).astype(np.uint8)
+    noise = _single_noise(rng, 16)
+    canvas = np.zeros((h, w * ch + 9), np.uint8)
+    view = canvas[:, :w * ch].reshape(h, w, ch)
+    view[...] = img
+    rect = eng.inpaint(view, mask, mbx.engine.params(steps=4, paste=paste), noise=noise)
+    want, want_rect = pipeline_ref.run(wu, wv, img, mask, *noise, params=dict(steps=4, paste=paste or 2),
+                                       ehs=unet_ref.conditioning(wu))
+    assert rect == want_rect
+    assert psnr8(view, want) >= 45.0
+    x, y, rw, rh = rect
+    outside = np.ones((h, w), bool)
+    outside[y:y + rh, x:x + rw] = False
+    assert np.array_equal(view[outside], img[outside]), "only the changed rectangle is written"
+    assert not canvas[:, w * ch:].any(), "bytes past the row width are untouched"
+    if ch == 4:
+        assert np.array_equal(view[..., 3], img[..., 3])
+
+
+def test_fast_preset_matches_oracle(mbx, tiny):
+    """Fast: trailing DPM-Solver++(2M), CFG for the first 3 steps then conditional only, ROI
+    encode; here 5 steps so the oracle stays quick (3 CFG + 2 conditional-only, one restart)."""
+    from oracle import pipeline_ref, unet_ref
+    eng, wu, wv, _ = tiny
+    rng = np.random.default_rng(41)
+    img, masks, nv, ni, no = _inputs(rng, 2, 128)
+    masks[1] = 0
+    masks[1, 20:40, 30:50] = 255  # a small mask: its ROI window is smaller than the latent
+    got = img.copy()
+    p = mbx.engine.params(preset=mbx.abi.PRESET_FAST, steps=5)
+    eng.inpaint_batch(got, masks, p, noise=(nv, ni, no))
+    ehs = unet_ref.conditioning(wu)
+    for i in range(2):
+        want = pipeline_ref.run(wu, wv, img[i], masks[i], nv[2 * i:2 * i + 2], ni[i], no[i],
+                                params=dict(pipeline_ref.FAST, steps=5), ehs=ehs)[0]
+        assert psnr8(got[i], want) >= 45.0, i
+    single = img[1].copy()
+    eng.inpaint(single, masks[1], p, noise=(nv[2:4], ni[1], no[1]))
+    assert np.array_equal(single, got[1]), "single and batch calls agree"
+
+
+def test_batch_paste_modes_and_dilation_match_oracle(mbx, tiny):
+    from oracle import pipeline_ref, unet_ref
+    eng, wu, wv, _ = tiny
+    rng = np.random.default_rng(43)
+    img, masks, nv, ni, no = _inputs(rng, 2, 128, ch=4)
+    ehs = unet_ref.conditioning(wu)
+    for paste, dilate in ((1, 0), (3, 5)):
+        got = img.copy()
+        eng.inpaint_batch(got, masks, mbx.engine.params(steps=3, paste=paste, mask_dilate=dilate), noise=(nv, ni, no))
+        for i in range(2):
+            want = pipeline_ref.run(wu, wv, img[i], masks[i], nv[2 * i:2 * i + 2], ni[i], no[i],
+                                    params=dict(steps=3, paste=paste, mask_dilate=dilate), ehs=ehs)[0]
+            assert psnr8(got[i], want) >= 45.0, (paste, dilate, i)
 
 
 def test_progress_reports_and_cancel_leaves_image_untouched(mbx, tiny):
