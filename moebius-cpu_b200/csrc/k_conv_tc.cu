@@ -52,9 +52,10 @@ constexpr int BM = 128;
 constexpr int BK = 32;                  // f32 elements per 128-byte swizzle row
 constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int kThreads = 448;  // 14 warps; see the role map above
-constexpr int kStgSlots = 3;   // raw A staging slots (16 KB each)
+constexpr int kMinStgSlots = 3;  // raw A staging slots (16 KB each): at least, and at most
+constexpr int kMaxStgSlots = 6;
 constexpr int kSegChunks = 8;  // K chunks (of 32) per accumulator segment
-constexpr int kMaxBn = 128;       // 2 · bn accumulator columns + 4 A stages of 64 columns ≤ 512
+constexpr int kMaxBn = 160;  // 2 · bn accumulator columns + A stages of 64 columns ≤ 512 (3 stages at 160)
 constexpr int kMaxAStages = 4;
 constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
 constexpr int kMaxSmem = 232448;             // 227 KB opt-in limit per CTA
@@ -66,6 +67,7 @@ struct ConvArgs {
     int cin_chunks, k_chunks;
     int flat;  // 1×1 conv: input pixel = output pixel (no padding, stride or upsample)
     int c_out, bn, n_tiles, stages, a_stages, tmem_cols;
+    int stg_slots;  // raw A staging slots: as many as shared memory holds (more chunks in flight)
     int64_t tiles;  // m tiles × n tiles
     const float* bias;
     const float* residual;
@@ -273,14 +275,15 @@ __global__ void __maxnreg__(128)
     // Running sums of the finished K segments: 128 rows × (bn + 4) floats (the 4-float pad
     // staggers rows across banks for the row-per-thread float4 accesses of the drain warps).
     const uint32_t sum_stride = (uint32_t)(bn + 4) * 4u;
-    const uint32_t sum_base = stg_base + (uint32_t)kStgSlots * A_BYTES;
+    const int nstg = args.stg_slots;
+    const uint32_t sum_base = stg_base + (uint32_t)nstg * A_BYTES;
     const uint32_t bars = sum_base + 128u * sum_stride;
     auto b_full_bar = [&](int s) { return bars + 8u * s; };
     auto b_empty_bar = [&](int s) { return bars + 8u * (bstages + s); };
     const uint32_t sbars = bars + 16u * bstages;
     auto sfull_bar = [&](int q) { return sbars + 8u * q; };
-    auto sempty_bar = [&](int q) { return sbars + 8u * (kStgSlots + q); };
-    const uint32_t tbars = sbars + 16u * kStgSlots;
+    auto sempty_bar = [&](int q) { return sbars + 8u * (kMaxStgSlots + q); };
+    const uint32_t tbars = sbars + 16u * kMaxStgSlots;
     auto a_full_bar = [&](int a) { return b_full_bar(a); };
     auto a_empty_bar = [&](int a) { return b_empty_bar(a); };
     const uint32_t abars = tbars + 16u * kMaxAStages;
@@ -309,7 +312,7 @@ __global__ void __maxnreg__(128)
             mbar_init(b_full_bar(s), 129);
             mbar_init(b_empty_bar(s), 1);
         }
-        for (int q = 0; q < kStgSlots; ++q) {
+        for (int q = 0; q < nstg; ++q) {
             mbar_init(sfull_bar(q), 128);
             mbar_init(sempty_bar(q), 128);
         }
@@ -364,7 +367,7 @@ __global__ void __maxnreg__(128)
         // ------------------------------------------------------------ loaders
         // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
         // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
-        // never waits on its data and keeps up to kStgSlots chunks in flight.
+        // never waits on its data and keeps up to nstg chunks in flight.
         const int tid = threadIdx.x;
         const int j = tid & 7;       // 16-byte chunk (4 channels) of the 128-byte row
         const int rbase = tid >> 3;  // rows rbase + 16·i
@@ -410,7 +413,7 @@ __global__ void __maxnreg__(128)
                     }
                 }
                 cp_async_mbar_arrive(sfull_bar(q));
-                if (++q == kStgSlots) {
+                if (++q == nstg) {
                     q = 0;
                     qphase ^= 1;
                 }
@@ -487,7 +490,7 @@ __global__ void __maxnreg__(128)
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(a_full_bar(a));
-                if (++q == kStgSlots) {
+                if (++q == nstg) {
                     q = 0;
                     qphase ^= 1;
                 }
@@ -720,14 +723,14 @@ int sum_bytes(int bn) { return 128 * (bn + 4) * 4; }
 
 int stage_count(bool f32w, int bn) {
     const int stage = (f32w ? 2 : 1) * bn * 128;
-    return std::min(8, (kMaxSmem - 2048 - kStgSlots * (int)A_BYTES - sum_bytes(bn)) / stage);
+    return std::min(8, (kMaxSmem - 2048 - kMinStgSlots * (int)A_BYTES - sum_bytes(bn)) / stage);
 }
 
 template <bool F32W, bool VEC4, bool FLAT>
 void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_tiles) {
     auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
     const int stage = (F32W ? 2 : 1) * a.bn * 128;
-    const int smem = a.stages * stage + kStgSlots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
+    const int smem = a.stages * stage + a.stg_slots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
     static bool configured = false;
     if (!configured) {
         check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
@@ -748,10 +751,11 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_til
 
 }  // namespace
 
-int choose_bn(int64_t c_out) {
+int choose_bn(int64_t c_out, bool f32_weights) {
+    // Fewest padded columns, with a per-tile cost for tiles that re-read the same A rows.
     int best = 32;
     int64_t best_cost = INT64_MAX;
-    for (int bn = kMaxBn; bn >= 32; bn -= 32) {
+    for (int bn = 128; bn >= 32; bn -= 32) {
         const int64_t tiles = (c_out + bn - 1) / bn;
         const int64_t cost = tiles * bn + 32 * tiles;
         if (cost < best_cost) {
@@ -759,6 +763,9 @@ int choose_bn(int64_t c_out) {
             best = bn;
         }
     }
+    // 160-wide tiles (three pipeline stages instead of four) only where they pad less
+    // than the 128-wide ones: 320, 800, 1600 ... output channels.
+    if (!f32_weights && best == 128 && (c_out + 159) / 160 * 160 < (c_out + 127) / 128 * 128) best = kMaxBn;
     return best;
 }
 
@@ -796,6 +803,11 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.stages = std::min(stage_count(f32w, p->bn), std::min(kMaxAStages, (512 - 2 * p->bn) / 64));
     // The MMA thread waits for two consecutive stages at once: the ring needs at least two.
     if (a.stages < 2) fail(MBX_ERR_INTERNAL, "conv: fewer than two pipeline stages fit");
+    {
+        const int stage = (f32w ? 2 : 1) * p->bn * 128;
+        a.stg_slots = std::min(kMaxStgSlots, (kMaxSmem - 2048 - a.stages * stage - sum_bytes(p->bn)) / (int)A_BYTES);
+        if (a.stg_slots < kMinStgSlots) fail(MBX_ERR_INTERNAL, "conv: fewer than three staging slots fit");
+    }
     a.tmem_cols = 512;
     a.a_stages = a.stages;
     a.bias = bias;

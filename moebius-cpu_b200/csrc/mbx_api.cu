@@ -322,7 +322,7 @@ int32_t mbx_param_create(mbx_ctx* ctx, const void* host_data, int32_t dtype, int
         p->taps = taps;
         p->c_in = c_in;
         p->cin_pad = int((c_in + 31) / 32 * 32);
-        p->bn = mbx::choose_bn(c_out);
+        p->bn = mbx::choose_bn(c_out, dtype == MBX_DTYPE_F32);
         p->cout_pad = int((c_out + p->bn - 1) / p->bn * p->bn);
         const size_t kdim = size_t(taps) * p->cin_pad;
         const size_t elems = size_t(p->cout_pad) * kdim;
@@ -650,7 +650,7 @@ int32_t mbx_gemm(mbx_ctx* ctx, float* c, const float* a, int64_t m, int64_t k, c
         p.taps = 1;
         p.c_in = k;
         p.cin_pad = int((k + 31) / 32 * 32);
-        p.bn = mbx::choose_bn(n);
+        p.bn = mbx::choose_bn(n, true);
         p.cout_pad = int((n + p.bn - 1) / p.bn * p.bn);
         const size_t elems = size_t(p.cout_pad) * p.cin_pad;
         mbx::PoolBuf hi(ctx, elems * 4), lo(ctx, elems * 4);

@@ -126,7 +126,9 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
                     float* out, int act = 0);
 // Tensor maps for a param's hi / lo arrays (TMA, 128-byte swizzle).
 void encode_param_tmaps(mbx_param* p);
-int choose_bn(int64_t c_out);
+// N tile for c_out output channels: 160 at most with f16 weights, 128 with f32 (3×TF32 keeps
+// a lo weight tile too, so wider tiles would leave too few pipeline stages).
+int choose_bn(int64_t c_out, bool f32_weights);
 
 void launch_softmax_rows(mbx_ctx* ctx, float* x, int64_t rows, int64_t n, float scale, float flush);
 void launch_split_to_param(mbx_ctx* ctx, const float* b, int64_t n, int64_t k, bool b_is_kn, mbx_param* p);
