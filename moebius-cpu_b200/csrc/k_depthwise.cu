@@ -2,8 +2,8 @@
 // (reference src/engine/depthwise.rs:31-185).
 //
 // Each thread owns one channel vector (4 channels, or 1 for channel counts
-// that are not multiples of 4) at one x position and walks a 64-row strip of
-// output rows in blocks of 4 (2 for GLU): each block loads its 6 (4) input rows
+// that are not multiples of 4) at one x position and walks a strip of 16 or 64
+// output rows in blocks of 4 (1 for GLU): each block loads its 6 (3) input rows
 // at once, so many loads are in flight per thread (the left and right pixels
 // are the neighbouring threads' centre pixels and the block-overlap rows were
 // loaded by the previous block, so both come from L1). A CTA covers 8 channel vectors × 16 x-positions; the x-halo columns
@@ -18,7 +18,9 @@ namespace mbx {
 namespace {
 
 constexpr int kDwThreads = 128;
-constexpr int kDwRows = 64;  // output rows per thread strip (y-halo re-read: 2/64)
+// Output rows per thread strip: 64 on large maps (y-halo re-read 2/64), 16 on the UNet's
+// small ones (64² and below), where more, shorter strips keep more loads in flight.
+inline int strip_rows(int64_t h) { return h >= 256 ? 64 : 16; }
 constexpr int kDwQuads = 8;  // channel vectors per CTA row (16 x-positions per CTA)
 
 template <int V>
@@ -89,10 +91,10 @@ __device__ __forceinline__ Vec<V> taps(const Vec<V> (&win)[3][3], const Vec<V> (
 // grid: x = output channel-vector blocks, y = x-position blocks, z = item × strip.
 // The CTA's taps and bias sit in shared memory (read with warp broadcasts).
 template <int V, int EPI, int RB>
-__global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restrict__ x, int h, int w, int c,
+__global__ void __launch_bounds__(kDwThreads, 4) dw3x3_kernel(const float* __restrict__ x, int h, int w, int c,
                                                            const float* __restrict__ weight,
                                                            const float* __restrict__ bias, float* __restrict__ out,
-                                                           int qb, int strips) {
+                                                           int qb, int strips, int rows) {
     constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
     constexpr int kSets = kGlu ? 2 : 1;  // value (and gate) channel sets
     __shared__ Vec<V> s_w[kSets][9][kDwQuads];
@@ -120,8 +122,8 @@ __global__ void __launch_bounds__(kDwThreads) dw3x3_kernel(const float* __restri
     const int ox = blockIdx.y * xb + t / qb;
     if (qv >= cvo || ox >= w) return;
     const int b = blockIdx.z / strips;
-    const int y0 = (blockIdx.z % strips) * kDwRows;
-    const int y1 = min(y0 + kDwRows, h);
+    const int y0 = (blockIdx.z % strips) * rows;
+    const int y1 = min(y0 + rows, h);
     const int ch = qv * V;
     const float* xb_ = x + (int64_t)b * h * w * c;
 
@@ -175,16 +177,17 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
     const int64_t cvo = c_out / V;
     const int qb = (int)std::min<int64_t>(cvo, kDwQuads);
     const int xb = kDwThreads / qb;
-    const int64_t strips = (h + kDwRows - 1) / kDwRows;
+    const int rows = strip_rows(h);
+    const int64_t strips = (h + rows - 1) / rows;
     MBX_REQUIRE(n * strips < (int64_t(1) << 31) && (cvo + qb - 1) / qb < (int64_t(1) << 31),
                 "depthwise: grid too large");
     MBX_REQUIRE((w + xb - 1) / xb < 65536 && n * strips < 65536 * 32768LL, "depthwise: grid too large");
     dim3 grid((unsigned)((cvo + qb - 1) / qb), (unsigned)((w + xb - 1) / xb), (unsigned)(n * strips));
-    MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h/64) must be <= 65535)");
+    MBX_REQUIRE(grid.z <= 65535, "depthwise: too many row strips (n * ceil(h / strip rows) must be <= 65535)");
     const int hh = (int)h, ww = (int)w, cc = (int)c, st = (int)strips;
 #define MBX_DW(VV, EE)                                                                                      \
-    dw3x3_kernel<VV, EE, EE == MBX_EPILOGUE_GLU_SILU ? 2 : 4><<<grid, kDwThreads, 0, ctx->stream>>>( \
-        x, hh, ww, cc, weight, bias, out, qb, st)
+    dw3x3_kernel<VV, EE, EE == MBX_EPILOGUE_GLU_SILU ? 1 : 4><<<grid, kDwThreads, 0, ctx->stream>>>( \
+        x, hh, ww, cc, weight, bias, out, qb, st, rows)
     if (V == 4) {
         if (epilogue == MBX_EPILOGUE_NONE) MBX_DW(4, MBX_EPILOGUE_NONE);
         else if (epilogue == MBX_EPILOGUE_RELU) MBX_DW(4, MBX_EPILOGUE_RELU);
