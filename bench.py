@@ -57,7 +57,7 @@ STEPS_EXACT = 20
 INPAINT_TFLOP = 16.76
 SWEEP_SHAPE = (8, 512, 512, 512)
 BYTES_PER_ELT = {"group_norm_silu": 8, "bias_temb_add": 8, "residual_add": 12, "depthwise3x3": 8}
-CONV_SHAPE = (8, 256, 256, 512, 512)  # n, h, w, c_in, c_out: the conv sweep's largest 3×3 case
+CONV_SHAPE = (8, 256, 256, 512, 512, 9)  # n, h, w, c_in, c_out, taps: the conv sweep's largest 3×3 case
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -252,29 +252,33 @@ def tf32_peak(torch):
 
 
 def bench_conv(mbx, ctx, torch, dev, small):
-    """The tcgen05 implicit-GEMM conv on the conv sweep's largest 3×3 shape (f16 and f32 weights)."""
-    cn, chh, cww, cci, cco = CONV_SHAPE
+    """The tcgen05 implicit-GEMM conv on the conv sweep's largest 3×3 shape (f16 and f32 weights);
+    --conv-shape selects another shape, a 1×1 conv with taps = 1."""
+    cn, chh, cww, cci, cco, taps = CONV_SHAPE
     gen = torch.Generator(device=dev).manual_seed(7)
     cx = torch.randn(cn, chh, cww, cci, device=dev, generator=gen)
     cy = torch.empty(cn, chh, cww, cco, device=dev)
-    wt = (torch.randn(cco, 3, 3, cci, generator=torch.Generator().manual_seed(7)) / (9 * cci) ** 0.5).numpy()
+    wshape = (cco, 3, 3, cci) if taps == 9 else (cco, cci)
+    wt = (torch.randn(*wshape, generator=torch.Generator().manual_seed(7)) / (taps * cci) ** 0.5).numpy()
+    conv = mbx.conv3x3 if taps == 9 else mbx.conv1x1
     cb = 0.01 * torch.randn(cco, device=dev, generator=gen)
     W = lambda t: mbx.DeviceTensor.wrap(ctx, t.data_ptr(), tuple(t.shape))  # noqa: E731
     CX, CY, CB = W(cx), W(cy), W(cb)
-    flops = 2.0 * cn * chh * cww * 9 * cci * cco
+    flops = 2.0 * cn * chh * cww * taps * cci * cco
     tf32 = tf32_peak(torch)
-    out = {"shape": f"[{cn},{chh},{cww},{cci}] -> {cco}, 3x3 pad 1, bias", "tf32_dense_peak_tflops": round(tf32, 1),
+    kind = "3x3 pad 1" if taps == 9 else "1x1"
+    out = {"shape": f"[{cn},{chh},{cww},{cci}] -> {cco}, {kind}, bias", "tf32_dense_peak_tflops": round(tf32, 1),
            "tf32_peak_source": "measured here: cuBLAS 8192^3 TF32 matmul, best of 10", "flops_per_launch": flops}
     for dtype in ("f16", "f32"):
         p = mbx.Param(ctx, wt, dtype)
         for _ in range(2):
-            mbx.conv3x3(CX, p, CB, out=CY)
+            conv(CX, p, CB, out=CY)
         torch.cuda.synchronize()
         reps = 5
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record()
         for _ in range(reps):
-            mbx.conv3x3(CX, p, CB, out=CY)
+            conv(CX, p, CB, out=CY)
         e_ev.record()
         e_ev.synchronize()
         cms = s_ev.elapsed_time(e_ev) / reps
@@ -495,7 +499,7 @@ def run_ours(args):
                     "peak_kind": "measured here (cuBLAS TF32 dense, burst); MEASURED_PEAKS.json holds no TF32 figure",
                     "issued_frac": conv["f16"]["issued_frac_of_tf32_peak"],
                     "algorithmic_flops_per_launch": conv["flops_per_launch"], "shape": conv["shape"],
-                    "traffic": traffic_from_profiles("conv_tc")}
+                    "traffic": traffic_from_profiles("conv_tc_3x3")}
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 2), "higher_is_better": True, "scaling": "weak",
@@ -655,15 +659,19 @@ def main():
     ap.add_argument("--skip-components", action="store_true")
     ap.add_argument("--component", choices=["unet", "vae_encode", "vae_decode"], default=None,
                     help="time one pipeline component alone (profiling case)")
-    ap.add_argument("--conv-shape", default=None, help="n,h,w,c_in,c_out of the conv measurement")
+    ap.add_argument("--conv-shape", default=None,
+                    help="n,h,w,c_in,c_out[,taps] of the conv measurement (taps 9: 3x3, 1: 1x1)")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a scaled-down network (64/128/256, 128x128 images) and small sweeps")
     args = ap.parse_args()
     global CONV_SHAPE
     if args.conv_shape:
-        CONV_SHAPE = tuple(int(v) for v in args.conv_shape.split(","))
+        vals = tuple(int(v) for v in args.conv_shape.split(","))
+        if len(vals) not in (5, 6) or (len(vals) == 6 and vals[5] not in (1, 9)):
+            ap.error("--conv-shape takes n,h,w,c_in,c_out[,taps] with taps 1 or 9")
+        CONV_SHAPE = vals if len(vals) == 6 else vals + (9,)
     elif args.small:
-        CONV_SHAPE = (1, 128, 128, 512, 512)
+        CONV_SHAPE = (1, 128, 128, 512, 512, 9)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

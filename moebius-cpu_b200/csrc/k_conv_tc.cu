@@ -8,31 +8,40 @@
 // materialising the patch matrix, and replaces its Winograd path
 // (src/engine/winograd.rs) for stride 1 / pad 1.
 //
-// CTA = one 128 × bn output tile (bn ≤ 160); 14 warps:
+// CTA = one 128 × bn output tile at a time (bn ≤ 160); persistent: one CTA per
+// SM walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... (N tile fastest) with
+// every ring carried across tiles, so one tile's epilogue overlaps the next
+// tile's loads and MMAs. 14 warps:
 //   warps 0-3   loaders: gather the A tile (128 output pixels × 32 channels of
 //               one tap) from NHWC global memory with 16-byte cp.async into a
-//               raw staging ring; zero padding (src-size 0), stride and the
-//               nearest-2× upsample are all address arithmetic here.
+//               raw staging ring (as many 16 KB slots as shared memory holds);
+//               zero padding (src-size 0), stride and the nearest-2× upsample
+//               are all address arithmetic here.
 //   warps 10-13 converters: apply the optional GroupNorm prologue
 //               [SiLU](x·scale + shift) at spatially valid taps, split each value
-//               into a TF32-rounded high part and a TF32-rounded remainder, and
-//               store both into 128-byte-swizzled K-major MMA tiles.
-//   warp 4      MMA issuer (one thread) + TMEM allocation.
+//               v into hi = v (the tensor core reads it truncated to TF32) and
+//               lo = v − trunc_TF32(v) (exact), and tcgen05.st both into TMEM.
+//   warp 4      MMA issuer (one thread) + TMEM allocation; K chunks go out in
+//               pairs, one barrier wait and one fence per 16 or 24 MMAs.
 //   warp 5      TMA issuer (one thread) for the pre-split weight tiles.
 //   warps 6-9   accumulator drain + epilogue (TMEM lane quadrant = warp % 4).
-// Loading and converting are separate warps because the converters' proxy
-// fence (generic smem writes → tensor-core reads) would otherwise wait for
-// every global load still in flight.
-// Precision: f32 weights → 3×TF32 (a_lo·w_hi + a_hi·w_lo + a_hi·w_hi),
-// f16 weights (exact in TF32) → 2×TF32 (a_lo·w + a_hi·w). The tensor core
+// One ring of K-chunk stages: stage s holds the weight tile (shared memory, by
+// TMA) and the A tile (TMEM, by the converters) behind one full barrier (128
+// converter arrivals + the TMA's expect-tx) and one empty barrier (the MMA's commit).
+// Loading and converting are separate warps because the converters' waits on
+// their staging slot would otherwise serialise with every global load in flight.
+// Precision: f32 weights → 3×TF32 (a_lo·w_hi + a_hi·w_lo + a_hi·w_hi, weights
+// split round-to-nearest at load), f16 weights (exact in TF32) → 2×TF32
+// (a_lo·w + a_hi·w). The truncation split leaves at most the lo part's own
+// truncation (≤ 2^-21 of |a|) per product. The tensor core
 // adds each MMA's products into its f32 accumulator with truncation, which
 // biases long sums toward zero (about 1e-4 relative at K = 11520). So K is
 // cut into segments of kSegChunks chunks (256 K-elements): the MMA warp
 // alternates between two TMEM accumulators, and the drain warps fold each
 // finished segment into a running sum in shared memory with round-to-nearest
 // f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).
-// TMEM (512 columns) holds the two accumulators (2·bn) and a ring of A stages
-// (64 columns each: TF32 high parts, then low parts; lane = tile row) that the
+// TMEM (512 columns) holds the two accumulators (2·bn) and the A stages
+// (64 columns each: high parts, then low parts; lane = tile row) that the
 // MMA reads directly (A from tensor memory), so the converted activations never
 // pass through shared memory.
 // The last segment is folded straight into the epilogue: + bias (+ residual)
