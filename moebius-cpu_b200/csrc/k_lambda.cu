@@ -211,13 +211,17 @@ __global__ void __launch_bounds__(512, 1)
             acc[j + 3] = fmaf(coef, v4.w, acc[j + 3]);
         }
     };
+    // The coefficients stream from global memory four taps at a time; the next group's load is
+    // issued before this group's FMAs so its latency hides behind them.
+    float4 c4 = __ldg(reinterpret_cast<const float4*>(arow));
 #pragma unroll 1
     for (int d = 0; d < kTaps - 1; d += 4) {
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(arow + d));
-        tap(d, c4.x);
-        tap(d + 1, c4.y);
-        tap(d + 2, c4.z);
-        tap(d + 3, c4.w);
+        const float4 cur = c4;
+        if (d + 4 < kTaps - 1) c4 = __ldg(reinterpret_cast<const float4*>(arow + d + 4));
+        tap(d, cur.x);
+        tap(d + 1, cur.y);
+        tap(d + 2, cur.z);
+        tap(d + 3, cur.w);
     }
     tap(kTaps - 1, last.x);
     float* o = out + pix * c + h * k + j0;
