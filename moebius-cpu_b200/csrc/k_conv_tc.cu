@@ -77,6 +77,11 @@ struct ConvArgs {
     int flat;  // 1×1 conv: input pixel = output pixel (no padding, stride or upsample)
     int c_out, bn, n_tiles, stages, a_stages, tmem_cols;
     int stg_slots;  // raw A staging slots: as many as shared memory holds (more chunks in flight)
+    // A-operand loads: 0 = cp.async gather by the loader warps; 1 = one TMA box per chunk from a
+    // 2-D map [m_total][c_in] (1×1 convs); 2 = one TMA box {32 channels, a_bw, a_bh, 1} per chunk
+    // and tap from a 4-D map [n][h][w][c_in] (3×3, stride 1, no upsample; the box's zero fill
+    // outside the map is the padding).
+    int a_tma, a_bw;
     int64_t tiles;  // m tiles × n tiles
     const float* bias;
     const float* residual;
@@ -140,6 +145,10 @@ __device__ __forceinline__ void fence_mbarrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -148,6 +157,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
         "[%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
 
@@ -264,7 +282,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
 template <bool F32W, bool VEC4, bool FLAT>
 __global__ void __maxnreg__(128)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
-                   const ConvArgs args) {
+                   const __grid_constant__ CUtensorMap tmap_a, const ConvArgs args) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -322,7 +340,7 @@ __global__ void __maxnreg__(128)
             mbar_init(b_empty_bar(s), 1);
         }
         for (int q = 0; q < nstg; ++q) {
-            mbar_init(sfull_bar(q), 128);
+            mbar_init(sfull_bar(q), args.a_tma ? 1 : 128);
             mbar_init(sempty_bar(q), 128);
         }
         for (int b = 0; b < 2; ++b) {
@@ -372,7 +390,49 @@ __global__ void __maxnreg__(128)
         }
     };
 
-    if (warp < 4) {
+    if (warp < 4 && args.a_tma) {
+        // ------------------------------------------------------------ A loads by TMA
+        // One thread issues one 16 KB box per K chunk into the staging ring (the 128-byte swizzle
+        // gives the same layout the cp.async gather writes).
+        if (threadIdx.x == 0) {
+            int q = 0, qphase = 0;
+            bool live = true;
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+                const int64_t m0 = tile_m0(t);
+                int item = 0, y0 = 0, x0 = 0;
+                if (args.a_tma == 2) {
+                    item = (int)(m0 / hw_out);
+                    const int64_t rem = m0 - (int64_t)item * hw_out;
+                    y0 = (int)(rem / args.wo);
+                    x0 = (int)(rem - (int64_t)y0 * args.wo);
+                }
+                int tap = 0, cchunk = 0;
+                for (int kc = 0; kc < K; ++kc) {
+                    if (!mbar_wait(sempty_bar(q), (uint32_t)(qphase ^ 1), args.err, 8, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+                    mbar_arrive_expect_tx(sfull_bar(q), A_BYTES);
+                    if (args.a_tma == 1) {
+                        tma_load_2d(stg, &tmap_a, cchunk * BK, (int)m0, sfull_bar(q));
+                    } else {
+                        const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+                        tma_load_4d(stg, &tmap_a, cchunk * BK, x0 + kx - args.pad_l, y0 + ky - args.pad_t, item,
+                                    sfull_bar(q));
+                    }
+                    if (++q == nstg) {
+                        q = 0;
+                        qphase ^= 1;
+                    }
+                    if (++cchunk == args.cin_chunks) {
+                        cchunk = 0;
+                        ++tap;
+                    }
+                }
+            }
+        }
+    } else if (warp < 4) {
         // ------------------------------------------------------------ loaders
         // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
         // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
@@ -471,7 +531,7 @@ __global__ void __maxnreg__(128)
                     v[4 * jj + 2] = f.z;
                     v[4 * jj + 3] = f.w;
                 }
-                mbar_arrive(sempty_bar(q));  // the staging row is in registers
+                if (!args.a_tma) mbar_arrive(sempty_bar(q));  // the staging row is in registers
                 if (pro) {
                     const int cb = cchunk * BK;
                     bool ok;
@@ -495,6 +555,12 @@ __global__ void __maxnreg__(128)
                 float lo[32];
 #pragma unroll
                 for (int e = 0; e < 32; ++e) lo[e] = tf32_split_lo(v[e]);
+                if (args.a_tma) {
+                    // The next TMA write into this slot is an async-proxy access: the row's generic
+                    // loads (complete here, their values are in use) are ordered before it.
+                    fence_proxy_async_smem();
+                    mbar_arrive(sempty_bar(q));
+                }
                 tmem_st32(lane_base + a_col(a) + 32u, lo);
                 tmem_wait_st();
                 tc_fence_before();
@@ -728,6 +794,17 @@ void encode_one(CUtensorMap* map, const float* data, int64_t kdim, int64_t rows,
     if (r != CUDA_SUCCESS) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
 }
 
+// Tensor map over the activations x (f32, channels innermost) for the A-operand boxes; reads
+// outside the map fill with zeros.
+void encode_a_map(CUtensorMap* map, const float* x, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                  const cuuint32_t* box) {
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(x), dims,
+                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (" + std::to_string((int)r) + ")");
+}
+
 int sum_bytes(int bn) { return 128 * (bn + 4) * 4; }
 
 int stage_count(bool f32w, int bn) {
@@ -736,7 +813,7 @@ int stage_count(bool f32w, int bn) {
 }
 
 template <bool F32W, bool VEC4, bool FLAT>
-void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_tiles) {
+void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtensorMap& tmap_a, int64_t m_tiles) {
     auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
     const int stage = (F32W ? 2 : 1) * a.bn * 128;
     const int smem = a.stages * stage + a.stg_slots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
@@ -755,7 +832,7 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, int64_t m_til
     (void)m_tiles;
     // Persistent: one CTA per SM (the shared-memory footprint allows one), tiles strided over them.
     const int64_t blocks = std::min<int64_t>(a.tiles, (int64_t)ctx->sm_count);
-    kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, a);
+    kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, tmap_a, a);
 }
 
 }  // namespace
@@ -839,17 +916,44 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
                              (!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
     MBX_REQUIRE(aligned_out || (p->c_out & 3) != 0,
                 "conv: out, residual and bias must be 16-byte aligned when c_out is a multiple of 4");
+    // A by TMA where one box per chunk covers the tile's 128 rows: 1×1 convs (a 2-D view of x), and
+    // 3×3 stride-1 convs whose tiles are whole image rows or 128-pixel pieces of one row.
+    CUtensorMap tmap_a = p->tmap_hi;  // unused when a_tma == 0
+    a.a_tma = 0;
+    a.a_bw = 0;
+    if (vec4 && s.c_in >= BK && a.m_total < (int64_t(1) << 31)) {  // boxes no wider than the map
+        const int64_t hw = s.h * s.w;
+        if (a.flat) {
+            a.a_tma = 1;
+            cuuint64_t dims[2] = {(cuuint64_t)s.c_in, (cuuint64_t)a.m_total};
+            cuuint64_t strides[1] = {(cuuint64_t)s.c_in * 4};
+            cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+            encode_a_map(&tmap_a, x, 2, dims, strides, box);
+        } else if (s.stride == 1 && s.up == 0 && s.ho == s.h && s.wo == s.w && hw % BM == 0 &&
+                   (s.w % BM == 0 || BM % s.w == 0) && s.h < (1 << 30) && s.w < (1 << 30) && s.n < (1 << 30)) {
+            a.a_tma = 2;
+            a.a_bw = (int)std::min<int64_t>(s.w, BM);
+            cuuint64_t dims[4] = {(cuuint64_t)s.c_in, (cuuint64_t)s.w, (cuuint64_t)s.h, (cuuint64_t)s.n};
+            cuuint64_t strides[3] = {(cuuint64_t)s.c_in * 4, (cuuint64_t)(s.w * s.c_in) * 4,
+                                     (cuuint64_t)(hw * s.c_in) * 4};
+            cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)a.a_bw, (cuuint32_t)(BM / a.a_bw), 1};
+            encode_a_map(&tmap_a, x, 4, dims, strides, box);
+        }
+    }
     if (a.flat) {
         if (f32w)
-            vec4 ? run_conv<true, true, true>(ctx, p, a, m_tiles) : run_conv<true, false, true>(ctx, p, a, m_tiles);
+            vec4 ? run_conv<true, true, true>(ctx, p, a, tmap_a, m_tiles)
+                 : run_conv<true, false, true>(ctx, p, a, tmap_a, m_tiles);
         else
-            vec4 ? run_conv<false, true, true>(ctx, p, a, m_tiles) : run_conv<false, false, true>(ctx, p, a, m_tiles);
+            vec4 ? run_conv<false, true, true>(ctx, p, a, tmap_a, m_tiles)
+                 : run_conv<false, false, true>(ctx, p, a, tmap_a, m_tiles);
     } else {
         if (f32w)
-            vec4 ? run_conv<true, true, false>(ctx, p, a, m_tiles) : run_conv<true, false, false>(ctx, p, a, m_tiles);
+            vec4 ? run_conv<true, true, false>(ctx, p, a, tmap_a, m_tiles)
+                 : run_conv<true, false, false>(ctx, p, a, tmap_a, m_tiles);
         else
-            vec4 ? run_conv<false, true, false>(ctx, p, a, m_tiles)
-                 : run_conv<false, false, false>(ctx, p, a, m_tiles);
+            vec4 ? run_conv<false, true, false>(ctx, p, a, tmap_a, m_tiles)
+                 : run_conv<false, false, false>(ctx, p, a, tmap_a, m_tiles);
     }
     after_launch(ctx, "conv (tcgen05)");
 }
