@@ -248,6 +248,19 @@ struct mbx_engine {
     std::unique_ptr<Vae> vae;
     std::map<std::pair<int64_t, int>, std::unique_ptr<UNetRunner>> runners;
     int64_t vae_chunk = 16;  // items per VAE call (bounds the 512² feature maps)
+    DevBuf sin_table;        // [1000][time_proj]: the timestep embedding of every train step
+
+    // The embeddings on the device, built on first use, so a denoising loop copies them on the
+    // device and never waits for the host.
+    const float* sinusoids() {
+        if (!sin_table.get()) {
+            const int64_t tp = unet->shape().time_proj;
+            std::vector<float> h(size_t(kTrainSteps * tp));
+            for (int64_t t = 0; t < kTrainSteps; ++t) unet->sinusoid(t, h.data() + t * tp);
+            sin_table = DevBuf(h.data(), h.size() * 4);
+        }
+        return sin_table.f();
+    }
 
     ~mbx_engine() {
         runners.clear();
@@ -452,23 +465,7 @@ struct mbx_engine {
         // them by default), conditional-only at batch n after; DDIM or DPM-Solver++(2M).
         if (!ts.empty()) {
             const int64_t tp = unet->shape().time_proj;
-            float* host_sin = nullptr;
-            check_cuda(cudaHostAlloc((void**)&host_sin, ts.size() * size_t(2 * n * tp) * 4, cudaHostAllocDefault),
-                       "timestep table");
-            struct HostFree {
-                float* p;
-                mbx_ctx* ctx;
-                ~HostFree() {
-                    cudaStreamSynchronize(ctx->stream);
-                    cudaFreeHost(p);
-                }
-            } host_free{host_sin, ctx};
-            std::vector<float> one((size_t)tp);
-            for (size_t i = 0; i < ts.size(); ++i) {
-                unet->sinusoid(ts[i], one.data());
-                for (int64_t it = 0; it < 2 * n; ++it)
-                    std::memcpy(host_sin + (i * size_t(2 * n) + size_t(it)) * size_t(tp), one.data(), size_t(tp) * 4);
-            }
+            const float* table = sinusoids();
             Tensor x0_prev;
             if (ep.dpm) x0_prev = Tensor(ctx, n, L, L, 4);
             bool has_prev = false;
@@ -477,9 +474,7 @@ struct mbx_engine {
                 const bool cfg = ep.cfg_steps < 0 || (int64_t)i < ep.cfg_steps;
                 const int copies = cfg ? 2 : 1;
                 UNetRunner& r = runner(copies * n, copies);
-                check_cuda(cudaMemcpyAsync(r.sin.data(), host_sin + i * size_t(2 * n * tp), size_t(copies * n * tp) * 4,
-                                           cudaMemcpyHostToDevice, ctx->stream),
-                           "timestep embedding");
+                launch_broadcast_rows(ctx, table + ts[i] * tp, tp, copies * n, r.sin.data());
                 ck(mbx_unet_input(ctx, x.data(), mask_lat.data(), z.data(), n, lhw, copies, r.x.data()));
                 launch(r);
                 if (!ep.dpm) {

@@ -151,6 +151,14 @@ __global__ void cfg_dpm_kernel(const float* __restrict__ eps, int64_t n, int64_t
     }
 }
 
+// out[i][:] = row[:] for i < copies (the timestep embedding of every item of a UNet batch).
+__global__ void broadcast_rows_kernel(const float* __restrict__ row, int64_t len, int64_t copies,
+                                      float* __restrict__ out) {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < len * copies;
+         e += (int64_t)gridDim.x * blockDim.x)
+        out[e] = row[e % len];
+}
+
 // One CTA per line; `passes` fractional box passes with 8-bit rounding after each.
 __global__ void blur_lines_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t lines_per_item,
                                   int64_t item_stride, int64_t line_stride, int64_t elem_stride, int len, int radius,
@@ -242,6 +250,11 @@ void launch_cfg_dpm(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int 
                                                                         coef[1], coef[2], coef[3], coef[4], order, x,
                                                                         x0_prev);
     after_launch(ctx, "cfg_dpm_step");
+}
+
+void launch_broadcast_rows(mbx_ctx* ctx, const float* row, int64_t len, int64_t copies, float* out) {
+    broadcast_rows_kernel<<<grid_for(ctx, len * copies, 256), 256, 0, ctx->stream>>>(row, len, copies, out);
+    after_launch(ctx, "broadcast_rows");
 }
 
 void launch_blur_lines(mbx_ctx* ctx, const uint8_t* in, uint8_t* out, int64_t lines, int64_t lines_per_item,

@@ -212,6 +212,7 @@ void launch_paste(mbx_ctx* ctx, uint8_t* image, int64_t n, int64_t stride, int64
 // Pillow's GaussianBlur(radius) of n single-channel h × w planes (3 box passes per axis).
 void gaussian_blur(mbx_ctx* ctx, const uint8_t* in, int64_t n, int64_t h, int64_t w, float radius, uint8_t* scratch,
                    uint8_t* out);
+void launch_broadcast_rows(mbx_ctx* ctx, const float* row, int64_t len, int64_t copies, float* out);
 void launch_cfg_dpm(mbx_ctx* ctx, const float* eps, int64_t n, int64_t per, int copies, float guidance,
                     const float coef[5], int order, float* x, float* x0_prev);
 void launch_feather_paste(mbx_ctx* ctx, const float* result, const uint8_t* blurred, uint8_t* image, int64_t pixels,
