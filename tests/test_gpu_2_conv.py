@@ -117,7 +117,8 @@ def lcg(seed):
     return nxt
 
 
-@pytest.mark.parametrize("n,h,w,ci,groups,co", [(2, 7, 9, 40, 8, 24), (2, 37, 23, 768, 32, 16)])
+@pytest.mark.parametrize("n,h,w,ci,groups,co", [(2, 7, 9, 40, 8, 24), (2, 37, 23, 768, 32, 16),
+                                                 (2, 32, 32, 64, 32, 48)])  # the last: TMA-fed A tiles
 @pytest.mark.parametrize("upx", [False, True])
 def test_prologue_matches_group_norm_then_conv(mbx, ctx, n, h, w, ci, groups, co, upx):
     # tests/kernels.rs:233-264, both sides on the GPU.
@@ -189,6 +190,13 @@ def test_conv_sweep_matches_oracle(mbx, ctx, oracle, k, hw, ci, co, dtype):
     ((2, 16, 16, 1280), 1, (1, 1, 1, 1), True, 1280),    # UNet Upsample2D, level 2
     ((1, 64, 64, 4), 1, (1, 1, 1, 1), False, 512),       # VAE decoder conv_in (4 channels)
     ((1, 64, 64, 128), 1, (1, 1, 1, 1), False, 3),       # VAE conv_out (3 channels)
+    # Upsampled inputs through the TMA boxes of each tile geometry: 128 / wo output rows per tile
+    # (wo 32, 64, 128) and 128-pixel pieces of a row (wo 256, 512).
+    ((2, 16, 16, 64), 1, (1, 1, 1, 1), True, 96),
+    ((1, 32, 32, 64), 1, (1, 1, 1, 1), True, 160),
+    ((2, 64, 64, 96), 1, (1, 1, 1, 1), True, 64),
+    ((1, 128, 128, 32), 1, (1, 1, 1, 1), True, 64),
+    ((1, 256, 256, 32), 1, (1, 1, 1, 1), True, 32),
 ])
 def test_unet_vae_conv_shapes(mbx, ctx, oracle, shape, stride, pad, upx, co):
     rng = np.random.default_rng(shape[-1] + co)
