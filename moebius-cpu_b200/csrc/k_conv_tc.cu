@@ -243,6 +243,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // The A-operand split: the tensor core reads an f32 operand as TF32 by dropping
@@ -322,6 +331,11 @@ __global__ void __maxnreg__(128)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Converters: warps 10-13, plus warps 0-3 for 1×1 convs with TMA-fed A rows (the loader warps are
+    // free then; short-K 1×1 tiles gain from the faster hand-off, long 3×3 ones do not); with
+    // eight, each thread converts half of its row's 32 channels.
+    const bool split = args.a_tma == 1;
+    const int conv_threads = split ? 256 : 128;
     const int K = args.k_chunks;
     const int nseg = (K + kSegChunks - 1) / kSegChunks;
     // Persistent CTA: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (N tile fastest, so the CTAs
@@ -336,12 +350,12 @@ __global__ void __maxnreg__(128)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < bstages; ++s) {
-            mbar_init(b_full_bar(s), 129);
+            mbar_init(b_full_bar(s), (uint32_t)conv_threads + 1u);
             mbar_init(b_empty_bar(s), 1);
         }
         for (int q = 0; q < nstg; ++q) {
             mbar_init(sfull_bar(q), args.a_tma ? 1 : 128);
-            mbar_init(sempty_bar(q), 128);
+            mbar_init(sempty_bar(q), (uint32_t)conv_threads);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full_bar(b), 1);
@@ -390,49 +404,7 @@ __global__ void __maxnreg__(128)
         }
     };
 
-    if (warp < 4 && args.a_tma) {
-        // ------------------------------------------------------------ A loads by TMA
-        // One thread issues one 16 KB box per K chunk into the staging ring (the 128-byte swizzle
-        // gives the same layout the cp.async gather writes).
-        if (threadIdx.x == 0) {
-            int q = 0, qphase = 0;
-            bool live = true;
-            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
-                const int64_t m0 = tile_m0(t);
-                int item = 0, y0 = 0, x0 = 0;
-                if (args.a_tma == 2) {
-                    item = (int)(m0 / hw_out);
-                    const int64_t rem = m0 - (int64_t)item * hw_out;
-                    y0 = (int)(rem / args.wo);
-                    x0 = (int)(rem - (int64_t)y0 * args.wo);
-                }
-                int tap = 0, cchunk = 0;
-                for (int kc = 0; kc < K; ++kc) {
-                    if (!mbar_wait(sempty_bar(q), (uint32_t)(qphase ^ 1), args.err, 8, abort_flag, true)) {
-                        live = false;
-                        break;
-                    }
-                    const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
-                    mbar_arrive_expect_tx(sfull_bar(q), A_BYTES);
-                    if (args.a_tma == 1) {
-                        tma_load_2d(stg, &tmap_a, cchunk * BK, (int)m0, sfull_bar(q));
-                    } else {
-                        const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-                        tma_load_4d(stg, &tmap_a, cchunk * BK, x0 + kx - args.pad_l, y0 + ky - args.pad_t, item,
-                                    sfull_bar(q));
-                    }
-                    if (++q == nstg) {
-                        q = 0;
-                        qphase ^= 1;
-                    }
-                    if (++cchunk == args.cin_chunks) {
-                        cchunk = 0;
-                        ++tap;
-                    }
-                }
-            }
-        }
-    } else if (warp < 4) {
+    if (warp < 4 && !args.a_tma) {
         // ------------------------------------------------------------ loaders
         // cp.async 16-byte copies (zero-filled at padding) into the raw staging ring;
         // completion is signalled per thread with cp.async.mbarrier.arrive, so a loader
@@ -493,12 +465,14 @@ __global__ void __maxnreg__(128)
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
-    } else if (warp >= 10) {
+    } else if (warp >= 10 || (split && warp < 4)) {
         // ------------------------------------------------------------ converters
         // One tile row per thread (its TMEM lane): staging row → [SiLU](x·scale + shift) at a
         // spatially valid tap (padding stays zero; channel padding beyond c_in meets zero
-        // weights) → TF32 high and low parts written to the A stage in TMEM.
+        // weights) → TF32 high and low parts written to the A stage in TMEM. With eight
+        // converter warps, warps 10-13 take channels 0-15 and warps 0-3 16-31.
         const int qd = warp & 3;
+        const int half = warp < 4 ? 1 : 0;
         const int r = qd * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
         const bool pro = args.pro_scale != nullptr;
@@ -522,25 +496,28 @@ __global__ void __maxnreg__(128)
                     break;
                 }
                 const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
-                float v[32];
+                bool ok = true;
+                if (pro) (void)tap_pixel(m0, r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
+                // Loads 4·NV channels (16-byte units j0 …) of the row, applies the prologue, stores the
+                // high parts, releases the staging slot and stores the low parts at column c0.
+                auto convert = [&](auto nv_tag, int j0, uint32_t c0) {
+                    constexpr int NV = decltype(nv_tag)::value;
+                    float v[4 * NV];
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    const float4 f = ld_shared_v4(stg + ((uint32_t)(jj ^ (r & 7)) << 4));
-                    v[4 * jj] = f.x;
-                    v[4 * jj + 1] = f.y;
-                    v[4 * jj + 2] = f.z;
-                    v[4 * jj + 3] = f.w;
-                }
-                if (!args.a_tma) mbar_arrive(sempty_bar(q));  // the staging row is in registers
-                if (pro) {
-                    const int cb = cchunk * BK;
-                    bool ok;
-                    (void)tap_pixel(m0, r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
-                    if (ok) {
+                    for (int jj = 0; jj < NV; ++jj) {
+                        const float4 f = ld_shared_v4(stg + ((uint32_t)((j0 + jj) ^ (r & 7)) << 4));
+                        v[4 * jj] = f.x;
+                        v[4 * jj + 1] = f.y;
+                        v[4 * jj + 2] = f.z;
+                        v[4 * jj + 3] = f.w;
+                    }
+                    if (!args.a_tma) mbar_arrive(sempty_bar(q));  // the staging row is in registers
+                    if (pro && ok) {
+                        const int cb = cchunk * BK + 4 * j0;
                         const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
                         const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
+                        for (int e = 0; e < 4 * NV; ++e) {
                             if (cb + e < args.c_in) {
                                 float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
                                 if (args.pro_silu) y = dev_silu(y);
@@ -548,20 +525,26 @@ __global__ void __maxnreg__(128)
                             }
                         }
                     }
-                }
-                // High part: the value itself (the tensor core reads its TF32 truncation); low part:
-                // v − trunc_tf32(v), exact in f32 (again read truncated). See tf32_split_lo.
-                tmem_st32(lane_base + a_col(a), v);  // v stays untouched until the wait below
-                float lo[32];
+                    // High part: the value itself (the tensor core reads its TF32 truncation); low
+                    // part: v − trunc_tf32(v), exact in f32 (again read truncated).
+                    if constexpr (NV == 8) tmem_st32(lane_base + a_col(a) + c0, v);
+                    else tmem_st16(lane_base + a_col(a) + c0, v);  // v stays untouched until the wait
+                    float lo[4 * NV];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) lo[e] = tf32_split_lo(v[e]);
-                if (args.a_tma) {
-                    // The next TMA write into this slot is an async-proxy access: the row's generic
-                    // loads (complete here, their values are in use) are ordered before it.
-                    fence_proxy_async_smem();
-                    mbar_arrive(sempty_bar(q));
-                }
-                tmem_st32(lane_base + a_col(a) + 32u, lo);
+                    for (int e = 0; e < 4 * NV; ++e) lo[e] = tf32_split_lo(v[e]);
+                    if (args.a_tma) {
+                        // The next TMA write into this slot is an async-proxy access: the row's
+                        // generic loads (complete here, their values are in use) are ordered before it.
+                        fence_proxy_async_smem();
+                        mbar_arrive(sempty_bar(q));
+                    }
+                    if constexpr (NV == 8) tmem_st32(lane_base + a_col(a) + 32u + c0, lo);
+                    else tmem_st16(lane_base + a_col(a) + 32u + c0, lo);
+                };
+                if (split)
+                    convert(std::integral_constant<int, 4>{}, 4 * half, 16u * (uint32_t)half);
+                else
+                    convert(std::integral_constant<int, 8>{}, 0, 0u);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(a_full_bar(a));
@@ -661,7 +644,47 @@ __global__ void __maxnreg__(128)
         }
         __syncwarp();
     } else if (warp == 5) {
-        // ------------------------------------------------------------ TMA issuer
+        // ------------------------------------------------------------ TMA issuers
+        // Lane 1: the A boxes (one 16 KB box per K chunk into the staging ring; the 128-byte
+        // swizzle gives the same layout the cp.async gather writes). Lane 0: the weight tiles.
+        if (lane == 1 && args.a_tma) {
+            int q = 0, qphase = 0;
+            bool live = true;
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+                const int64_t m0 = tile_m0(t);
+                int item = 0, y0 = 0, x0 = 0;
+                if (args.a_tma == 2) {
+                    item = (int)(m0 / hw_out);
+                    const int64_t rem = m0 - (int64_t)item * hw_out;
+                    y0 = (int)(rem / args.wo);
+                    x0 = (int)(rem - (int64_t)y0 * args.wo);
+                }
+                int tap = 0, cchunk = 0;
+                for (int kc = 0; kc < K; ++kc) {
+                    if (!mbar_wait(sempty_bar(q), (uint32_t)(qphase ^ 1), args.err, 8, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
+                    mbar_arrive_expect_tx(sfull_bar(q), A_BYTES);
+                    if (args.a_tma == 1) {
+                        tma_load_2d(stg, &tmap_a, cchunk * BK, (int)m0, sfull_bar(q));
+                    } else {
+                        const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+                        tma_load_4d(stg, &tmap_a, cchunk * BK, x0 + kx - args.pad_l, y0 + ky - args.pad_t, item,
+                                    sfull_bar(q));
+                    }
+                    if (++q == nstg) {
+                        q = 0;
+                        qphase ^= 1;
+                    }
+                    if (++cchunk == args.cin_chunks) {
+                        cchunk = 0;
+                        ++tap;
+                    }
+                }
+            }
+        }
         if (lane == 0) {
             int s = 0, sphase = 0;
             bool live = true;
