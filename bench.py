@@ -155,8 +155,11 @@ def init_dist():
     if world > 1:
         import datetime
 
+        import torch
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
     return world, rank, local, dist
 
 
