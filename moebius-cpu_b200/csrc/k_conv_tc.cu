@@ -860,6 +860,22 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtenso
 
 }  // namespace
 
+void encode_tensor_map_f32(CUtensorMap* map, const float* base, int rank, const uint64_t* dims,
+                           const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+    cuuint64_t d[5], st[4];
+    cuuint32_t b[5], estr[5] = {1, 1, 1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        if (i + 1 < rank) st[i] = strides[i];
+    }
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, st,
+                             b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(MBX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+}
+
 int choose_bn(int64_t c_out, bool f32_weights) {
     // Fewest padded columns, with a per-tile cost for tiles that re-read the same A rows.
     int best = 32;

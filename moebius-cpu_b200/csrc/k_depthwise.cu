@@ -163,6 +163,140 @@ __global__ void __launch_bounds__(kDwThreads, 4) dw3x3_kernel(const float* __res
     }
 }
 
+
+// ---------------------------------------------------------------- TMA-tiled variant
+// A CTA owns a 16 × 16 output tile of 32 channels (both channel sets for GLU): one TMA box
+// {32, 18, 18, 1} per set brings the tile with its halo, read once from global memory (the box's
+// zero fill past the map is never used: padding taps are skipped as above). Each thread then
+// walks 8 output rows of one 4-channel vector at one x, sliding a 3-row window through shared
+// memory; its taps and bias sit in registers.
+constexpr int kTT = 16;                                           // tile side (output pixels)
+constexpr int kTC = 32;                                           // channels per tile
+constexpr int kTH = kTT + 2;                                      // halo tile side
+constexpr int kTileThreads = 256;                                 // 8 vectors × 16 columns × 2 row groups
+constexpr uint32_t kSetBytes = (uint32_t)kTH * kTH * kTC * 4;    // 41472
+constexpr long long kDwWaitLimit = 4ll << 30;                     // clock cycles (about 2 s)
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kTileThreads, 2) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
+                                                                 int w, int c, const float* __restrict__ weight,
+                                                                 const float* __restrict__ bias,
+                                                                 float* __restrict__ out, int tiles_x, int* err) {
+    constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
+    constexpr int kSets = kGlu ? 2 : 1;
+    extern __shared__ __align__(1024) float tile[];  // [set][kTH][kTH][kTC]
+    __shared__ uint64_t bar;
+    const int c_out = kGlu ? c / 2 : c;
+    const int c0 = blockIdx.x * kTC;
+    const int ty = blockIdx.y / tiles_x, tx = blockIdx.y - (blockIdx.y / tiles_x) * tiles_x;
+    const int y0 = ty * kTT, x0 = tx * kTT, item = blockIdx.z;
+    const uint32_t b = smem_addr(&bar);
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(b),
+                     "r"((uint32_t)kSets * kSetBytes)
+                     : "memory");
+#pragma unroll
+        for (int set = 0; set < kSets; ++set)
+            asm volatile(
+                "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+                "%3, %4, %5}], [%6];" ::"r"(smem_addr(tile + set * kTH * kTH * kTC)),
+                "l"(reinterpret_cast<uint64_t>(&map)), "r"(c0 + set * c_out), "r"(x0 - 1), "r"(y0 - 1), "r"(item),
+                "r"(b)
+                : "memory");
+    }
+    // Bounded wait for the boxes; on timeout the error is recorded and the CTA writes nothing.
+    {
+        const long long t0 = clock64();
+        while (true) {
+            uint32_t ok;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, "
+                "p;\n\t}"
+                : "=r"(ok)
+                : "r"(b)
+                : "memory");
+            if (ok) break;
+            if (clock64() - t0 > kDwWaitLimit) {
+                if (threadIdx.x == 0 && atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
+                return;
+            }
+        }
+    }
+    const int j = threadIdx.x & 7, xl = (threadIdx.x >> 3) & 15, rg = threadIdx.x >> 7;
+    const int ch = c0 + 4 * j, ox = x0 + xl;
+    if (ch >= c_out || ox >= w) return;
+    // Taps in registers for one channel set; with GLU's two sets they are re-read per row through the
+    // read-only cache instead (registers for two windows and two tap sets would halve the CTAs per SM).
+    Vec<4> wt[kGlu ? 1 : 9], bs[kSets];
+    if constexpr (!kGlu) {
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wt[k] = vload<4>(weight + k * c + ch);
+    }
+#pragma unroll
+    for (int set = 0; set < kSets; ++set) bs[set] = vload<4>(bias + set * c_out + ch);
+    const bool left = ox > 0, right = ox + 1 < w;
+    auto at = [&](int set, int row, int col) -> Vec<4> {
+        const float4 f = *reinterpret_cast<const float4*>(tile + (((set * kTH + row) * kTH + col) * kTC + 4 * j));
+        Vec<4> r;
+        r.v[0] = f.x;
+        r.v[1] = f.y;
+        r.v[2] = f.z;
+        r.v[3] = f.w;
+        return r;
+    };
+    const int r_begin = rg * (kTT / 2), r_end = min(r_begin + kTT / 2, h - y0);
+    Vec<4> win[kSets][3][3];
+#pragma unroll
+    for (int set = 0; set < kSets; ++set)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) win[set][rr][k] = at(set, r_begin + rr, xl + k);
+    for (int r = r_begin; r < r_end; ++r) {
+        const int oy = y0 + r;
+#pragma unroll
+        for (int set = 0; set < kSets; ++set)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) win[set][2][k] = at(set, r + 2, xl + k);
+        const bool top = oy > 0, bottom = oy + 1 < h;
+        Vec<4> acc[kSets];
+        if constexpr (kGlu) {
+#pragma unroll
+            for (int set = 0; set < kSets; ++set) {
+                Vec<4> ws[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) ws[k] = vload<4>(weight + k * c + set * c_out + ch);
+                acc[set] = taps<4>(win[set], ws, bs[set], top, bottom, left, right);
+            }
+        } else {
+            acc[0] = taps<4>(win[0], wt, bs[0], top, bottom, left, right);
+        }
+        Vec<4> res = acc[0];
+        if constexpr (EPI == MBX_EPILOGUE_RELU) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
+        } else if constexpr (kGlu) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
+        }
+        vstore<4>(out + (((int64_t)item * h + oy) * w + ox) * c_out + ch, res);
+#pragma unroll
+        for (int set = 0; set < kSets; ++set)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                win[set][0][k] = win[set][1][k];
+                win[set][1][k] = win[set][2][k];
+            }
+    }
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -173,6 +307,35 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
     const int64_t c_out = epilogue == MBX_EPILOGUE_GLU_SILU ? c / 2 : c;
     const bool vec = c % 4 == 0 && c_out % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(weight) &&
                      aligned16(bias);
+    // TMA-tiled kernel where the halo box fits inside the map and one channel box inside c.
+    if (vec && c >= kTC && h >= kTH && w >= kTH && n < 65536 && h < (1 << 20) && w < (1 << 20)) {
+        const int64_t tiles_x = (w + kTT - 1) / kTT, tiles_y = (h + kTT - 1) / kTT;
+        const int64_t cblocks = (c_out + kTC - 1) / kTC;
+        if (tiles_x * tiles_y < 65536 && cblocks < 65536) {
+            CUtensorMap map;
+            const uint64_t dims[4] = {(uint64_t)c, (uint64_t)w, (uint64_t)h, (uint64_t)n};
+            const uint64_t strides[3] = {(uint64_t)c * 4, (uint64_t)(w * c) * 4, (uint64_t)(h * w * c) * 4};
+            const uint32_t box[4] = {(uint32_t)kTC, (uint32_t)kTH, (uint32_t)kTH, 1};
+            encode_tensor_map_f32(&map, x, 4, dims, strides, box, false);
+            const dim3 grid((unsigned)cblocks, (unsigned)(tiles_x * tiles_y), (unsigned)n);
+            auto launch = [&](auto kern, int sets) {
+                const int smem = sets * (int)kSetBytes;
+                static bool configured[3] = {false, false, false};
+                if (!configured[epilogue]) {
+                    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                               "depthwise smem attribute");
+                    configured[epilogue] = true;
+                }
+                kern<<<grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias, out,
+                                                                (int)tiles_x, ctx->dev_err);
+            };
+            if (epilogue == MBX_EPILOGUE_NONE) launch(dw3x3_tma_kernel<MBX_EPILOGUE_NONE>, 1);
+            else if (epilogue == MBX_EPILOGUE_RELU) launch(dw3x3_tma_kernel<MBX_EPILOGUE_RELU>, 1);
+            else launch(dw3x3_tma_kernel<MBX_EPILOGUE_GLU_SILU>, 2);
+            after_launch(ctx, "depthwise3x3");
+            return;
+        }
+    }
     const int V = vec ? 4 : 1;
     const int64_t cvo = c_out / V;
     const int qb = (int)std::min<int64_t>(cvo, kDwQuads);

@@ -39,7 +39,7 @@ inline void check_cuda(cudaError_t e, const char* what) {
 // Device-side error record written by kernels whose bounded waits gave up:
 // [0] = code (0 = none), [1] = kernel id, [2] = detail (barrier / stage).
 enum DeviceErr : int { kErrNone = 0, kErrWaitTimeout = 1 };
-enum KernelId : int { kKConvTc = 1, kKGnSlab = 2 };
+enum KernelId : int { kKConvTc = 1, kKGnSlab = 2, kKDepthwise = 3 };
 
 // Stream-ordered best-fit caching allocator (device analogue of the
 // reference's Scratch pool). All blocks are used on the context stream, so a
@@ -124,6 +124,10 @@ struct ConvShape {
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
                     float* out, int act = 0);
+// A tiled TMA map over f32 data: dims innermost first, strides in bytes for dims 1.., box in
+// elements; reads outside the map fill with zeros.
+void encode_tensor_map_f32(CUtensorMap* map, const float* base, int rank, const uint64_t* dims,
+                           const uint64_t* strides, const uint32_t* box, bool swizzle128);
 // Tensor maps for a param's hi / lo arrays (TMA, 128-byte swizzle).
 void encode_param_tmaps(mbx_param* p);
 // N tile for c_out output channels: 160 at most with f16 weights, 128 with f32 (3×TF32 keeps

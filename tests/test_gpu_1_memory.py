@@ -119,7 +119,10 @@ def test_depthwise_tails(mbx, ctx, extra_fixture):
 @pytest.mark.parametrize("shape,ep", [((1, 32, 32, 64), "none"), ((8, 64, 64, 128), "relu"),
                                       ((2, 64, 64, 1600), "glu_silu"), ((2, 16, 16, 6400), "glu_silu"),
                                       ((1, 5, 7, 9), "relu"), ((2, 33, 17, 13), "none"), ((1, 1, 1, 8), "relu"),
-                                      ((1, 40, 3, 26), "glu_silu")])
+                                      ((1, 40, 3, 26), "glu_silu"),
+                                      # TMA-tiled kernel: ragged 16 × 16 tiles and a partial channel box
+                                      ((1, 37, 45, 72), "glu_silu"), ((2, 20, 50, 96), "relu"),
+                                      ((1, 18, 18, 36), "none")])
 def test_depthwise_matches_oracle(mbx, ctx, oracle, shape, ep):
     rng = np.random.default_rng(shape[-1] + len(ep))
     c = shape[-1]
