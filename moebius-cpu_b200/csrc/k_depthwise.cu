@@ -180,7 +180,7 @@ constexpr long long kDwWaitLimit = 4ll << 30;                     // clock cycle
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 template <int EPI>
-__global__ void __launch_bounds__(kTileThreads, 2) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
+__global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
                                                                  int w, int c, const float* __restrict__ weight,
                                                                  const float* __restrict__ bias,
                                                                  float* __restrict__ out, int tiles_x, int* err) {
@@ -232,15 +232,14 @@ __global__ void __launch_bounds__(kTileThreads, 2) dw3x3_tma_kernel(const __grid
     const int j = threadIdx.x & 7, xl = (threadIdx.x >> 3) & 15, rg = threadIdx.x >> 7;
     const int ch = c0 + 4 * j, ox = x0 + xl;
     if (ch >= c_out || ox >= w) return;
-    // Taps in registers for one channel set; with GLU's two sets they are re-read per row through the
-    // read-only cache instead (registers for two windows and two tap sets would halve the CTAs per SM).
-    Vec<4> wt[kGlu ? 1 : 9], bs[kSets];
-    if constexpr (!kGlu) {
+    // All taps of this thread's channel quad (both GLU sets) stay in registers for the whole tile.
+    Vec<4> wt[kSets][9], bs[kSets];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wt[k] = vload<4>(weight + k * c + ch);
+    for (int set = 0; set < kSets; ++set) {
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wt[set][k] = vload<4>(weight + k * c + set * c_out + ch);
+        bs[set] = vload<4>(bias + set * c_out + ch);
     }
-#pragma unroll
-    for (int set = 0; set < kSets; ++set) bs[set] = vload<4>(bias + set * c_out + ch);
     const bool left = ox > 0, right = ox + 1 < w;
     auto at = [&](int set, int row, int col) -> Vec<4> {
         const float4 f = *reinterpret_cast<const float4*>(tile + (((set * kTH + row) * kTH + col) * kTC + 4 * j));
@@ -267,17 +266,8 @@ __global__ void __launch_bounds__(kTileThreads, 2) dw3x3_tma_kernel(const __grid
             for (int k = 0; k < 3; ++k) win[set][2][k] = at(set, r + 2, xl + k);
         const bool top = oy > 0, bottom = oy + 1 < h;
         Vec<4> acc[kSets];
-        if constexpr (kGlu) {
 #pragma unroll
-            for (int set = 0; set < kSets; ++set) {
-                Vec<4> ws[9];
-#pragma unroll
-                for (int k = 0; k < 9; ++k) ws[k] = vload<4>(weight + k * c + set * c_out + ch);
-                acc[set] = taps<4>(win[set], ws, bs[set], top, bottom, left, right);
-            }
-        } else {
-            acc[0] = taps<4>(win[0], wt, bs[0], top, bottom, left, right);
-        }
+        for (int set = 0; set < kSets; ++set) acc[set] = taps<4>(win[set], wt[set], bs[set], top, bottom, left, right);
         Vec<4> res = acc[0];
         if constexpr (EPI == MBX_EPILOGUE_RELU) {
 #pragma unroll
