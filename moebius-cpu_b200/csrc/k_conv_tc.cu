@@ -36,7 +36,8 @@
 // truncation (≤ 2^-21 of |a|) per product. The tensor core
 // adds each MMA's products into its f32 accumulator with truncation, which
 // biases long sums toward zero (about 1e-4 relative at K = 11520). So K is
-// cut into segments of kSegChunks chunks (256 K-elements): the MMA warp
+// cut into equal segments of at most kSegMaxChunks chunks (512 K-elements; a
+// K of up to 512 is one segment): the MMA warp
 // alternates between two TMEM accumulators, and the drain warps fold each
 // finished segment into a running sum in shared memory with round-to-nearest
 // f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).
@@ -63,7 +64,13 @@ constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int kThreads = 448;  // 14 warps; see the role map above
 constexpr int kMinStgSlots = 3;  // raw A staging slots (16 KB each): at least, and at most
 constexpr int kMaxStgSlots = 6;
-constexpr int kSegChunks = 8;  // K chunks (of 32) per accumulator segment
+constexpr int kSegMaxChunks = 16;  // at most this many K chunks (of 32) per accumulator segment
+
+// Chunks per segment: K split into the fewest segments of at most kSegMaxChunks, as equal as possible.
+__device__ __forceinline__ int seg_chunks(int k_chunks) {
+    const int n = (k_chunks + kSegMaxChunks - 1) / kSegMaxChunks;
+    return (k_chunks + n - 1) / n;
+}
 constexpr int kMaxBn = 160;  // 2 · bn accumulator columns + A stages of 64 columns ≤ 512 (3 stages at 160)
 constexpr int kMaxAStages = 4;
 constexpr long long kWaitLimit = 4ll << 30;  // clock cycles (about 2 s)
@@ -337,7 +344,8 @@ __global__ void __maxnreg__(128)
     const bool split = args.a_tma == 1;
     const int conv_threads = split ? 256 : 128;
     const int K = args.k_chunks;
-    const int nseg = (K + kSegChunks - 1) / kSegChunks;
+    const int seg_len = seg_chunks(K);
+    const int nseg = (K + seg_len - 1) / seg_len;
     // Persistent CTA: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (N tile fastest, so the CTAs
     // in flight share A rows through L2). Every ring keeps its position and phase across tiles,
     // so the next tile's loads and MMAs overlap this tile's epilogue.
@@ -600,7 +608,7 @@ __global__ void __maxnreg__(128)
                 for (int kc = 0; kc < K;) {
                     const int b = seg & 1;
                     const bool seg_first = kin == 0;
-                    const int left = min(kSegChunks - kin, K - kc);
+                    const int left = min(seg_len - kin, K - kc);
                     const int g = left >= 2 ? 2 : 1;
                     const int s1 = s + 1 == bstages ? 0 : s + 1;
                     const int ph1 = s + 1 == bstages ? sphase ^ 1 : sphase;
@@ -622,7 +630,7 @@ __global__ void __maxnreg__(128)
                     if (g == 2) mma_commit(b_empty_bar(s1));
                     kc += g;
                     kin += g;
-                    if (kin == kSegChunks || kc == K) {
+                    if (kin == seg_len || kc == K) {
                         mma_commit(acc_full_bar(b));
                         kin = 0;
                         ++seg;
