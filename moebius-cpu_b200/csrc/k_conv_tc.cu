@@ -35,9 +35,10 @@
 // (a_lo·w + a_hi·w). The truncation split leaves at most the lo part's own
 // truncation (≤ 2^-21 of |a|) per product. The tensor core
 // adds each MMA's products into its f32 accumulator with truncation, which
-// biases long sums toward zero (about 1e-4 relative at K = 11520). So K is
-// cut into equal segments of at most kSegMaxChunks chunks (512 K-elements; a
-// K of up to 512 is one segment): the MMA warp
+// biases long sums toward zero (about 1e-4 relative at K = 11520; the error
+// grows with the length of each unbroken sum). So K is cut into equal segments
+// of at most kSegMaxChunks chunks (512 K-elements; a K of up to 512 is one
+// segment, so short-K tiles skip the fold and hold one accumulator): the MMA warp
 // alternates between two TMEM accumulators, and the drain warps fold each
 // finished segment into a running sum in shared memory with round-to-nearest
 // f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).

@@ -12,9 +12,10 @@
 //    out[p, h·k + v] += Σ_kk Q[p,h,kk]·λc[kk][v] + A[p,h,225]
 //                       + Σ_δ A[p,h,δ]·V[p+δ, v]      (15×15 window, zero pad 7)
 //    with A = Q·W_aug computed beforehand by the tensor-core GEMM. One CTA per
-//    8×8 pixel tile and v-slice; a thread owns one (pixel, head) and VS value
-//    channels in registers, so A is read once per slice and the window of V
-//    (22×22 pixels × VS channels) comes from shared memory.
+//    8×8 pixel tile and v-slice; a thread owns one pixel, two heads and half of
+//    the VS value channels in registers, so A is read once per slice, the
+//    window of V (22×22 pixels × VS channels) comes from shared memory and each
+//    V vector read there serves both heads.
 //  * cross_position (CrossLambda::forward + position_term, lambda.rs:252-294):
 //    out[p, h·k + v] += Σ_kk Q[p,h,kk]·λc[b][kk][v] + Σ_m (Σ_kk Q[p,h,kk]·E[p,m,kk])·V[b][m][v]
 //    for the item's conditioning branch b; λc and V are load-time constants.
@@ -132,16 +133,23 @@ __global__ void lambda_finalize_kernel(const float* __restrict__ plam, const flo
 
 // ---------------------------------------------------------------- self-λ position term
 
-// Shared layout: V window [kHalo²][VS + 4] (4 floats of padding keep the four pixels a
-// warp reads in distinct banks), then λc slice [k][VS].
+// Halo row stride in floats: at least VS and ≡ 8 or 24 (mod 32), so the eight 16-byte reads of a
+// warp (four neighbouring pixels × two interleaved float4 groups) fall in distinct banks.
+__host__ __device__ constexpr int halo_stride(int vs) { return vs + (vs % 16 == 0 ? 8 : 0); }
+
+// Shared layout: V window [kHalo²][HS], then λc slice [k][VS]. A thread owns one pixel, two heads
+// (2·hp and 2·hp + 1) and every other float4 group of the VS value channels (groups of parity jh),
+// so each V vector read from shared memory feeds both heads: 8 FMAs per 16-byte read.
 template <int VS>
 __global__ void __launch_bounds__(512, 1)
     self_position_kernel(const float* __restrict__ q, const float* __restrict__ lam, const float* __restrict__ a,
                          int a_stride, const float* __restrict__ v, int64_t v_stride, int H, int W, int k,
                          int tiles_x, float* __restrict__ out) {
+    static_assert(VS % 8 == 0, "a thread takes every other float4 group of the slice");
+    constexpr int HS = halo_stride(VS);
+    constexpr int NG = VS / 8;  // float4 groups per thread
     extern __shared__ float4 smem4[];
     float* halo = reinterpret_cast<float*>(smem4);
-    constexpr int HS = VS + 4;
     float* lam_s = halo + kHalo * kHalo * HS;
     const int item = blockIdx.z, j0 = blockIdx.y * VS;
     const int ty0 = (blockIdx.x / tiles_x) * kTile, tx0 = (blockIdx.x % tiles_x) * kTile;
@@ -166,83 +174,117 @@ __global__ void __launch_bounds__(512, 1)
     }
     __syncthreads();
 
-    const int h = tid & 7, p = tid >> 3;
-    const int ty = p >> 3, tx = p & 7;
+    // Lane = (pixel of four, group parity, head pair); warp = half a tile row.
+    const int lane = tid & 31, wid = tid >> 5;
+    const int hp = lane & 3, jh = (lane >> 2) & 1;
+    const int ty = wid >> 1, tx = (wid & 1) * 4 + (lane >> 3);
     const int y = ty0 + ty, x = tx0 + tx;
     if (y >= H || x >= W) return;
     const int64_t pix = item_px + (int64_t)y * W + x;
+    const int h0 = 2 * hp;
 
-    float acc[VS];
+    // acc0 / acc1: heads h0 / h0 + 1; element 4·i + e is value channel j0 + 8·i + 4·jh + e.
+    float acc0[4 * NG], acc1[4 * NG];
 #pragma unroll
-    for (int j = 0; j < VS; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < 4 * NG; ++j) acc0[j] = acc1[j] = 0.0f;
     // Content term Yc = Q·λc.
-    const float* qrow = q + pix * c + h * k;
+    const float* q0 = q + pix * c + h0 * k;
+    const float* q1 = q0 + k;
     for (int kk = 0; kk < k; kk += 4) {
-        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qrow + kk));
-        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float4 a4 = __ldg(reinterpret_cast<const float4*>(q0 + kk));
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(q1 + kk));
+        const float qa[4] = {a4.x, a4.y, a4.z, a4.w}, qb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float* lr = lam_s + (kk + u) * VS;
+            const float* lr = lam_s + (kk + u) * VS + 4 * jh;
 #pragma unroll
-            for (int j = 0; j < VS; j += 4) {
-                const float4 l4 = *reinterpret_cast<const float4*>(lr + j);
-                acc[j] = fmaf(qv[u], l4.x, acc[j]);
-                acc[j + 1] = fmaf(qv[u], l4.y, acc[j + 1]);
-                acc[j + 2] = fmaf(qv[u], l4.z, acc[j + 2]);
-                acc[j + 3] = fmaf(qv[u], l4.w, acc[j + 3]);
+            for (int i = 0; i < NG; ++i) {
+                const float4 l4 = *reinterpret_cast<const float4*>(lr + 8 * i);
+                acc0[4 * i] = fmaf(qa[u], l4.x, acc0[4 * i]);
+                acc0[4 * i + 1] = fmaf(qa[u], l4.y, acc0[4 * i + 1]);
+                acc0[4 * i + 2] = fmaf(qa[u], l4.z, acc0[4 * i + 2]);
+                acc0[4 * i + 3] = fmaf(qa[u], l4.w, acc0[4 * i + 3]);
+                acc1[4 * i] = fmaf(qb[u], l4.x, acc1[4 * i]);
+                acc1[4 * i + 1] = fmaf(qb[u], l4.y, acc1[4 * i + 1]);
+                acc1[4 * i + 2] = fmaf(qb[u], l4.z, acc1[4 * i + 2]);
+                acc1[4 * i + 3] = fmaf(qb[u], l4.w, acc1[4 * i + 3]);
             }
         }
     }
     // Position term: the Q·b column first, then the 225 taps in (ky, kx) order.
-    const float* arow = a + (pix * kHeads + h) * (int64_t)a_stride;
-    const float4 last = __ldg(reinterpret_cast<const float4*>(arow + kTaps - 1));  // tap 224, Q·b, 0, 0
+    const float* arow0 = a + (pix * kHeads + h0) * (int64_t)a_stride;
+    const float* arow1 = arow0 + a_stride;
+    const float4 last0 = __ldg(reinterpret_cast<const float4*>(arow0 + kTaps - 1));  // tap 224, Q·b, 0, 0
+    const float4 last1 = __ldg(reinterpret_cast<const float4*>(arow1 + kTaps - 1));
 #pragma unroll
-    for (int j = 0; j < VS; ++j) acc[j] += last.y;
-    const float* hbase = halo + (ty * kHalo + tx) * HS;
-    auto tap = [&](int d, float coef) {
+    for (int j = 0; j < 4 * NG; ++j) {
+        acc0[j] += last0.y;
+        acc1[j] += last1.y;
+    }
+    const float* hbase = halo + (ty * kHalo + tx) * HS + 4 * jh;
+    auto tap = [&](int d, float ca, float cb) {
         const int ky = d / kWin, kx = d - ky * kWin;
         const float* hr = hbase + (ky * kHalo + kx) * HS;
 #pragma unroll
-        for (int j = 0; j < VS; j += 4) {
-            const float4 v4 = *reinterpret_cast<const float4*>(hr + j);
-            acc[j] = fmaf(coef, v4.x, acc[j]);
-            acc[j + 1] = fmaf(coef, v4.y, acc[j + 1]);
-            acc[j + 2] = fmaf(coef, v4.z, acc[j + 2]);
-            acc[j + 3] = fmaf(coef, v4.w, acc[j + 3]);
+        for (int i = 0; i < NG; ++i) {
+            const float4 v4 = *reinterpret_cast<const float4*>(hr + 8 * i);
+            acc0[4 * i] = fmaf(ca, v4.x, acc0[4 * i]);
+            acc0[4 * i + 1] = fmaf(ca, v4.y, acc0[4 * i + 1]);
+            acc0[4 * i + 2] = fmaf(ca, v4.z, acc0[4 * i + 2]);
+            acc0[4 * i + 3] = fmaf(ca, v4.w, acc0[4 * i + 3]);
+            acc1[4 * i] = fmaf(cb, v4.x, acc1[4 * i]);
+            acc1[4 * i + 1] = fmaf(cb, v4.y, acc1[4 * i + 1]);
+            acc1[4 * i + 2] = fmaf(cb, v4.z, acc1[4 * i + 2]);
+            acc1[4 * i + 3] = fmaf(cb, v4.w, acc1[4 * i + 3]);
         }
     };
-    // The coefficients stream from global memory four taps at a time; the next group's load is
-    // issued before this group's FMAs so its latency hides behind them.
-    float4 c4 = __ldg(reinterpret_cast<const float4*>(arow));
+    // The coefficients stream from global memory four taps at a time; the next group's loads are
+    // issued before this group's FMAs so their latency hides behind them.
+    float4 ca4 = __ldg(reinterpret_cast<const float4*>(arow0));
+    float4 cb4 = __ldg(reinterpret_cast<const float4*>(arow1));
 #pragma unroll 1
     for (int d = 0; d < kTaps - 1; d += 4) {
-        const float4 cur = c4;
-        if (d + 4 < kTaps - 1) c4 = __ldg(reinterpret_cast<const float4*>(arow + d + 4));
-        tap(d, cur.x);
-        tap(d + 1, cur.y);
-        tap(d + 2, cur.z);
-        tap(d + 3, cur.w);
+        const float4 ca = ca4, cb = cb4;
+        if (d + 4 < kTaps - 1) {
+            ca4 = __ldg(reinterpret_cast<const float4*>(arow0 + d + 4));
+            cb4 = __ldg(reinterpret_cast<const float4*>(arow1 + d + 4));
+        }
+        tap(d, ca.x, cb.x);
+        tap(d + 1, ca.y, cb.y);
+        tap(d + 2, ca.z, cb.z);
+        tap(d + 3, ca.w, cb.w);
     }
-    tap(kTaps - 1, last.x);
-    float* o = out + pix * c + h * k + j0;
+    tap(kTaps - 1, last0.x, last1.x);
+    float* o0 = out + pix * c + h0 * k + j0 + 4 * jh;
+    float* o1 = o0 + k;
 #pragma unroll
-    for (int j = 0; j < VS; j += 4) {
-        float4 r = *reinterpret_cast<float4*>(o + j);
-        r.x += acc[j];
-        r.y += acc[j + 1];
-        r.z += acc[j + 2];
-        r.w += acc[j + 3];
-        *reinterpret_cast<float4*>(o + j) = r;
+    for (int i = 0; i < NG; ++i) {
+        float4 r = *reinterpret_cast<float4*>(o0 + 8 * i);
+        r.x += acc0[4 * i];
+        r.y += acc0[4 * i + 1];
+        r.z += acc0[4 * i + 2];
+        r.w += acc0[4 * i + 3];
+        *reinterpret_cast<float4*>(o0 + 8 * i) = r;
+        float4 t = *reinterpret_cast<float4*>(o1 + 8 * i);
+        t.x += acc1[4 * i];
+        t.y += acc1[4 * i + 1];
+        t.z += acc1[4 * i + 2];
+        t.w += acc1[4 * i + 3];
+        *reinterpret_cast<float4*>(o1 + 8 * i) = t;
     }
 }
 
 // ---------------------------------------------------------------- cross-λ
 
+// Shared layout: λc slice [k][VS], then the branch's values [kTokens][VS]. Threads map as in
+// self_position_kernel: one pixel, two heads, every other float4 group of the slice.
 template <int VS>
 __global__ void __launch_bounds__(512, 1)
     cross_position_kernel(const float* __restrict__ q, const float* __restrict__ e_table,
                           const float* __restrict__ lam, const float* __restrict__ vtab, int period, int64_t hw,
                           int k, float* __restrict__ out) {
+    static_assert(VS % 8 == 0, "a thread takes every other float4 group of the slice");
+    constexpr int NG = VS / 8;
     extern __shared__ float4 smem4[];
     float* lam_s = reinterpret_cast<float*>(smem4);  // [k][VS]
     float* v_s = lam_s + k * VS;                     // [kTokens][VS]
@@ -260,63 +302,94 @@ __global__ void __launch_bounds__(512, 1)
         v_s[i] = __ldg(v_b + (int64_t)m * k + j0 + j);
     }
     __syncthreads();
-    const int h = tid & 7;
-    const int64_t p = (int64_t)blockIdx.x * 64 + (tid >> 3);
+    const int lane = tid & 31, wid = tid >> 5;
+    const int hp = lane & 3, jh = (lane >> 2) & 1;
+    const int64_t p = (int64_t)blockIdx.x * 64 + wid * 4 + (lane >> 3);
     if (p >= hw) return;
     const int c = kHeads * k;
+    const int h0 = 2 * hp;
     const int64_t pix = (int64_t)item * hw + p;
-    const float* qrow = q + pix * c + h * k;
+    const float* q0 = q + pix * c + h0 * k;
+    const float* q1 = q0 + k;
     const float* erow = e_table + p * kTokens * k;
 
-    // B[m] = Q_h · E[p, m]
-    float bm[kTokens];
+    // B[m] = Q_h · E[p, m] for both heads.
+    float bm0[kTokens], bm1[kTokens];
 #pragma unroll
-    for (int m = 0; m < kTokens; ++m) bm[m] = 0.0f;
+    for (int m = 0; m < kTokens; ++m) bm0[m] = bm1[m] = 0.0f;
     for (int kk = 0; kk < k; kk += 4) {
-        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qrow + kk));
+        const float4 a4 = __ldg(reinterpret_cast<const float4*>(q0 + kk));
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(q1 + kk));
 #pragma unroll
         for (int m = 0; m < kTokens; ++m) {
             const float4 e4 = __ldg(reinterpret_cast<const float4*>(erow + m * k + kk));
-            bm[m] = fmaf(q4.x, e4.x, bm[m]);
-            bm[m] = fmaf(q4.y, e4.y, bm[m]);
-            bm[m] = fmaf(q4.z, e4.z, bm[m]);
-            bm[m] = fmaf(q4.w, e4.w, bm[m]);
+            bm0[m] = fmaf(a4.x, e4.x, bm0[m]);
+            bm0[m] = fmaf(a4.y, e4.y, bm0[m]);
+            bm0[m] = fmaf(a4.z, e4.z, bm0[m]);
+            bm0[m] = fmaf(a4.w, e4.w, bm0[m]);
+            bm1[m] = fmaf(b4.x, e4.x, bm1[m]);
+            bm1[m] = fmaf(b4.y, e4.y, bm1[m]);
+            bm1[m] = fmaf(b4.z, e4.z, bm1[m]);
+            bm1[m] = fmaf(b4.w, e4.w, bm1[m]);
         }
     }
-    float acc[VS];
+    // acc0 / acc1: heads h0 / h0 + 1; element 4·i + e is value channel j0 + 8·i + 4·jh + e.
+    float acc0[4 * NG], acc1[4 * NG];
 #pragma unroll
-    for (int j = 0; j < VS; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < 4 * NG; ++j) acc0[j] = acc1[j] = 0.0f;
     for (int kk = 0; kk < k; kk += 4) {
-        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qrow + kk));
-        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float4 a4 = __ldg(reinterpret_cast<const float4*>(q0 + kk));
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(q1 + kk));
+        const float qa[4] = {a4.x, a4.y, a4.z, a4.w}, qb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float* lr = lam_s + (kk + u) * VS;
+            const float* lr = lam_s + (kk + u) * VS + 4 * jh;
 #pragma unroll
-            for (int j = 0; j < VS; j += 4) {
-                const float4 l4 = *reinterpret_cast<const float4*>(lr + j);
-                acc[j] = fmaf(qv[u], l4.x, acc[j]);
-                acc[j + 1] = fmaf(qv[u], l4.y, acc[j + 1]);
-                acc[j + 2] = fmaf(qv[u], l4.z, acc[j + 2]);
-                acc[j + 3] = fmaf(qv[u], l4.w, acc[j + 3]);
+            for (int i = 0; i < NG; ++i) {
+                const float4 l4 = *reinterpret_cast<const float4*>(lr + 8 * i);
+                acc0[4 * i] = fmaf(qa[u], l4.x, acc0[4 * i]);
+                acc0[4 * i + 1] = fmaf(qa[u], l4.y, acc0[4 * i + 1]);
+                acc0[4 * i + 2] = fmaf(qa[u], l4.z, acc0[4 * i + 2]);
+                acc0[4 * i + 3] = fmaf(qa[u], l4.w, acc0[4 * i + 3]);
+                acc1[4 * i] = fmaf(qb[u], l4.x, acc1[4 * i]);
+                acc1[4 * i + 1] = fmaf(qb[u], l4.y, acc1[4 * i + 1]);
+                acc1[4 * i + 2] = fmaf(qb[u], l4.z, acc1[4 * i + 2]);
+                acc1[4 * i + 3] = fmaf(qb[u], l4.w, acc1[4 * i + 3]);
             }
         }
     }
 #pragma unroll
     for (int m = 0; m < kTokens; ++m) {
-        const float* vr = v_s + m * VS;
+        const float* vr = v_s + m * VS + 4 * jh;
 #pragma unroll
-        for (int j = 0; j < VS; ++j) acc[j] = fmaf(bm[m], vr[j], acc[j]);
+        for (int i = 0; i < NG; ++i) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vr + 8 * i);
+            acc0[4 * i] = fmaf(bm0[m], v4.x, acc0[4 * i]);
+            acc0[4 * i + 1] = fmaf(bm0[m], v4.y, acc0[4 * i + 1]);
+            acc0[4 * i + 2] = fmaf(bm0[m], v4.z, acc0[4 * i + 2]);
+            acc0[4 * i + 3] = fmaf(bm0[m], v4.w, acc0[4 * i + 3]);
+            acc1[4 * i] = fmaf(bm1[m], v4.x, acc1[4 * i]);
+            acc1[4 * i + 1] = fmaf(bm1[m], v4.y, acc1[4 * i + 1]);
+            acc1[4 * i + 2] = fmaf(bm1[m], v4.z, acc1[4 * i + 2]);
+            acc1[4 * i + 3] = fmaf(bm1[m], v4.w, acc1[4 * i + 3]);
+        }
     }
-    float* o = out + pix * c + h * k + j0;
+    float* o0 = out + pix * c + h0 * k + j0 + 4 * jh;
+    float* o1 = o0 + k;
 #pragma unroll
-    for (int j = 0; j < VS; j += 4) {
-        float4 r = *reinterpret_cast<float4*>(o + j);
-        r.x += acc[j];
-        r.y += acc[j + 1];
-        r.z += acc[j + 2];
-        r.w += acc[j + 3];
-        *reinterpret_cast<float4*>(o + j) = r;
+    for (int i = 0; i < NG; ++i) {
+        float4 r = *reinterpret_cast<float4*>(o0 + 8 * i);
+        r.x += acc0[4 * i];
+        r.y += acc0[4 * i + 1];
+        r.z += acc0[4 * i + 2];
+        r.w += acc0[4 * i + 3];
+        *reinterpret_cast<float4*>(o0 + 8 * i) = r;
+        float4 t = *reinterpret_cast<float4*>(o1 + 8 * i);
+        t.x += acc1[4 * i];
+        t.y += acc1[4 * i + 1];
+        t.z += acc1[4 * i + 2];
+        t.w += acc1[4 * i + 3];
+        *reinterpret_cast<float4*>(o1 + 8 * i) = t;
     }
 }
 
@@ -386,7 +459,7 @@ void launch_self_position(mbx_ctx* ctx, const float* q, const float* lam, const 
     MBX_REQUIRE(n < 65536 && (int64_t)tiles_x * tiles_y < (int64_t(1) << 31), "self lambda: grid too large");
     dispatch_vs(vs, [&](auto c) {
         constexpr int VS = decltype(c)::value;
-        const int smem = (kHalo * kHalo * (VS + 4) + (int)k * VS) * 4;
+        const int smem = (kHalo * kHalo * halo_stride(VS) + (int)k * VS) * 4;
         MBX_REQUIRE(smem <= 227 * 1024, "self lambda: head width too large");
         auto kern = self_position_kernel<VS>;
         static bool configured = false;
