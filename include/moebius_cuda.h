@@ -170,6 +170,15 @@ int32_t mbx_layer_norm(mbx_ctx *ctx, const float *x, int64_t tokens, int64_t c, 
  * Reference: depthwise3x3, src/engine/depthwise.rs:31-59. */
 int32_t mbx_depthwise3x3(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c,
                          const float *weight, const float *bias, int32_t epilogue, float *out);
+/* mbx_depthwise3x3 with a GroupNorm prologue: the input is read as
+ * [SiLU](x*pro_scale[item,c] + pro_shift[item,c]) at in-image taps while padding
+ * stays zero (pro_scale/pro_shift [n, c], e.g. from mbx_group_norm_affine); the
+ * results equal mbx_group_norm_apply followed by mbx_depthwise3x3, bit for bit.
+ * No single reference counterpart: GroupNorm::forward (with SiLU) feeding
+ * DWConv2d::forward inside DwResnet::forward, src/unet/blocks.rs:84-112. */
+int32_t mbx_depthwise3x3_fused(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c,
+                               const float *pro_scale, const float *pro_shift, int32_t pro_silu,
+                               const float *weight, const float *bias, int32_t epilogue, float *out);
 
 /* out[p] = x[p] . W^T + bias (+ residual[p]); W is a taps=1 param [c_out, c_in].
  * Reference: Conv1x1::forward, src/engine/conv.rs:38-55. */

@@ -274,11 +274,17 @@ def layer_norm(x: DeviceTensor, gamma: DeviceTensor, beta: DeviceTensor, eps: fl
 
 
 def depthwise3x3(x: DeviceTensor, weight: DeviceTensor, bias: DeviceTensor, epilogue: str = "none",
-                 out: Optional[DeviceTensor] = None) -> DeviceTensor:
+                 out: Optional[DeviceTensor] = None, prologue=None) -> DeviceTensor:
+    """prologue = (scale [n, c], shift [n, c], silu): the input is read as [SiLU](x*scale + shift)."""
     n, h, w, c = _nhwc(x)
     ep = EPILOGUES[epilogue]
     out = out or x.ctx.empty((n, h, w, c // 2 if ep == abi.EPILOGUE_GLU_SILU else c))
-    check(lib().mbx_depthwise3x3(x.ctx.handle, x.vp, n, h, w, c, weight.vp, bias.vp, ep, out.vp))
+    if prologue is None:
+        check(lib().mbx_depthwise3x3(x.ctx.handle, x.vp, n, h, w, c, weight.vp, bias.vp, ep, out.vp))
+    else:
+        sc, sh, silu = prologue
+        check(lib().mbx_depthwise3x3_fused(x.ctx.handle, x.vp, n, h, w, c, sc.vp, sh.vp, int(silu), weight.vp,
+                                           bias.vp, ep, out.vp))
     return out
 
 

@@ -104,6 +104,7 @@ SIGNATURES = {
                                               _vp]),
     "mbx_layer_norm": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _f32, _vp]),
     "mbx_depthwise3x3": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp]),
+    "mbx_depthwise3x3_fused": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp, _i32, _vp]),
     "mbx_conv1x1": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "mbx_conv3x3_output_hw": (_i32, [_i64, _i64, _i64, _pi64, _i32, _pi64, _pi64]),
     "mbx_conv3x3": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _pi64, _i32, _vp, _vp, _i32, _vp,

@@ -32,7 +32,9 @@ struct DwConv2d {
     DevBuf dw_w, dw_b;
     Conv pw;
     static DwConv2d load(const Loader& l, int64_t c_in, int64_t c_out);
-    Tensor forward(const Tensor& x) const;
+    // gn_scale / gn_shift [n, c_in]: the block's input is SiLU(x*gn_scale + gn_shift), applied on
+    // the fly (a GroupNorm + SiLU in front of the block).
+    Tensor forward(const Tensor& x, const float* gn_scale = nullptr, const float* gn_shift = nullptr) const;
 };
 
 struct DwResnet {

@@ -8,7 +8,8 @@
 //
 // Fusions relative to the reference's op sequence (same arithmetic, fewer
 // passes over HBM): the MixTransformer's GroupNorm is applied in proj_in's
-// operand gather; to_k / to_v run as one GEMM; the MixFFN SiLU is the inverted
+// operand gather; a GroupNorm + SiLU in front of a DWConv2d without a skip is
+// applied in the depthwise kernel's window; to_k / to_v run as one GEMM; the MixFFN SiLU is the inverted
 // conv's epilogue; the λ outputs are added straight into the hidden state; all
 // resnets' time_emb_proj run as one GEMM per step.
 #include <cmath>
@@ -31,16 +32,15 @@ Tensor layer_norm(const Tensor& x, const DevBuf& g, const DevBuf& b) {
     return out;
 }
 
-Tensor depthwise(const Tensor& x, const DevBuf& w, const DevBuf& b, int epilogue) {
+// gn_scale / gn_shift: the input is read as SiLU(x*gn_scale + gn_shift) (GroupNorm + SiLU prologue).
+Tensor depthwise(const Tensor& x, const DevBuf& w, const DevBuf& b, int epilogue, const float* gn_scale = nullptr,
+                 const float* gn_shift = nullptr) {
     Tensor out(x.ctx(), x.n, x.h, x.w, epilogue == MBX_EPILOGUE_GLU_SILU ? x.c / 2 : x.c);
-    ck(mbx_depthwise3x3(x.ctx(), x.data(), x.n, x.h, x.w, x.c, w.f(), b.f(), epilogue, out.data()));
-    return out;
-}
-
-Tensor group_norm(const Tensor& x, const GroupNormP& g, const float* add, bool silu) {
-    Tensor out(x.ctx(), x.n, x.h, x.w, x.c);
-    ck(mbx_group_norm_forward(x.ctx(), x.data(), x.n, x.h, x.w, x.c, g.groups, g.eps, g.gamma.f(), g.beta.f(), add,
-                              silu ? 1 : 0, out.data()));
+    if (gn_scale)
+        ck(mbx_depthwise3x3_fused(x.ctx(), x.data(), x.n, x.h, x.w, x.c, gn_scale, gn_shift, 1, w.f(), b.f(),
+                                  epilogue, out.data()));
+    else
+        ck(mbx_depthwise3x3(x.ctx(), x.data(), x.n, x.h, x.w, x.c, w.f(), b.f(), epilogue, out.data()));
     return out;
 }
 
@@ -102,10 +102,19 @@ DwConv2d DwConv2d::load(const Loader& l, int64_t c_in, int64_t c_out) {
     return d;
 }
 
-// y = pw1x1(relu(dw3x3(x) + b1)) + b2 (+ x when c_in == c_out), src/unet/blocks.rs:46-53.
-Tensor DwConv2d::forward(const Tensor& x) const {
-    Tensor mid = depthwise(x, dw_w, dw_b, MBX_EPILOGUE_RELU);
-    return conv1x1(mid, pw, c_in == c_out ? x.data() : nullptr);
+// y = pw1x1(relu(dw3x3(a) + b1)) + b2 (+ a when c_in == c_out), src/unet/blocks.rs:47-53, with a = x
+// or a = SiLU(x*gn_scale + gn_shift). Without the skip, a is built inside the depthwise kernel's window
+// and never stored; with it, a is stored once for the 1×1 conv's residual read (rebuilding it in the
+// conv's epilogue cost that kernel more than the saved pass).
+Tensor DwConv2d::forward(const Tensor& x, const float* gn_scale, const float* gn_shift) const {
+    const bool skip = c_in == c_out;
+    if (gn_scale && skip) {
+        Tensor a(x.ctx(), x.n, x.h, x.w, x.c);
+        ck(mbx_group_norm_apply(x.ctx(), x.data(), x.n, x.h * x.w, x.c, gn_scale, gn_shift, 1, nullptr, a.data()));
+        return forward(a);
+    }
+    Tensor mid = depthwise(x, dw_w, dw_b, MBX_EPILOGUE_RELU, gn_scale, gn_shift);
+    return conv1x1(mid, pw, skip ? x.data() : nullptr);
 }
 
 DwResnet DwResnet::load(const Loader& l, int64_t c_in, int64_t c_out) {
@@ -126,12 +135,15 @@ DwResnet DwResnet::load(const Loader& l, int64_t c_in, int64_t c_out) {
 // src/unet/blocks.rs:84-112; the time embedding projection arrives precomputed.
 Tensor DwResnet::forward(const Tensor& x, const float* temb_proj) const {
     MBX_REQUIRE(x.c == c_in, "DwResnet input channels");
-    Tensor a = group_norm(x, norm1, nullptr, true);
-    Tensor b = conv1.forward(a);
-    a = group_norm(b, norm2, temb_proj, true);
+    // Each GroupNorm + SiLU is applied by the DWConv2d that follows it (statistics pass here).
+    Tensor scale, shift;
+    gn_affine(x, norm1, nullptr, scale, shift);
+    Tensor b = conv1.forward(x, scale.data(), shift.data());
+    gn_affine(b, norm2, temb_proj, scale, shift);
+    Tensor out = conv2.forward(b, scale.data(), shift.data());
     b = Tensor();
-    Tensor out = conv2.forward(a);
-    a = Tensor();
+    scale = Tensor();
+    shift = Tensor();
     if (has_shortcut) return conv1x1(x, shortcut, out.data());
     ck(mbx_add_inplace(x.ctx(), out.data(), x.data(), out.size()));
     return out;
@@ -444,9 +456,9 @@ Tensor UNet::forward(const Tensor& x, const float* t_sinusoid, int branch_period
         if (lv.has_sample) h = conv3x3(h, lv.sample);
     }
     MBX_REQUIRE(skips.empty(), "skip stack not consumed");
-    Tensor a = group_norm(h, norm_out, nullptr, true);
-    h = Tensor();
-    return conv_out.forward(a);
+    Tensor scale, shift;
+    gn_affine(h, norm_out, nullptr, scale, shift);
+    return conv_out.forward(h, scale.data(), shift.data());
 }
 
 }  // namespace eng

@@ -179,10 +179,13 @@ constexpr long long kDwWaitLimit = 4ll << 30;                     // clock cycle
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-template <int EPI>
+// PRO: GroupNorm prologue, the input read as [SiLU](x*pro_scale[item,c] + pro_shift[item,c]).
+template <int EPI, bool PRO>
 __global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
                                                                  int w, int c, const float* __restrict__ weight,
                                                                  const float* __restrict__ bias,
+                                                                 const float* __restrict__ pro_scale,
+                                                                 const float* __restrict__ pro_shift, int pro_silu,
                                                                  float* __restrict__ out, int tiles_x, int* err) {
     constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
     constexpr int kSets = kGlu ? 2 : 1;
@@ -211,9 +214,11 @@ __global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_co
                 "r"(b)
                 : "memory");
     }
-    // Bounded wait for the boxes; on timeout the error is recorded and the CTA writes nothing.
+    // Bounded wait for the boxes; on timeout (any thread's) the error is recorded and the CTA
+    // writes nothing.
     {
         const long long t0 = clock64();
+        int timed_out = 0;
         while (true) {
             uint32_t ok;
             asm volatile(
@@ -224,10 +229,40 @@ __global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_co
                 : "memory");
             if (ok) break;
             if (clock64() - t0 > kDwWaitLimit) {
-                if (threadIdx.x == 0 && atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
-                return;
+                timed_out = 1;
+                break;
             }
         }
+        if (__syncthreads_or(timed_out)) {
+            if (threadIdx.x == 0 && atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
+            return;
+        }
+    }
+    if constexpr (PRO) {
+        // GroupNorm prologue on the landed window, in place, at in-image pixels of real channels (the
+        // padding taps are skipped below and channels past c are never stored, so their zero fill
+        // stays). Same arithmetic as the GroupNorm apply kernel: fmaf(x, scale, shift), then SiLU.
+        const int q4 = threadIdx.x & 7;
+#pragma unroll
+        for (int set = 0; set < kSets; ++set) {
+            const int cc = c0 + set * c_out + 4 * q4;
+            if (cc >= c) continue;
+            const float4 sc = __ldg(reinterpret_cast<const float4*>(pro_scale + (int64_t)item * c + cc));
+            const float4 sh = __ldg(reinterpret_cast<const float4*>(pro_shift + (int64_t)item * c + cc));
+            float* base = tile + set * kTH * kTH * kTC + 4 * q4;
+            for (int px = threadIdx.x >> 3; px < kTH * kTH; px += kTileThreads / 8) {
+                const int row = px / kTH, col = px - row * kTH;
+                const int gy = y0 - 1 + row, gx = x0 - 1 + col;
+                if (gy < 0 || gy >= h || gx < 0 || gx >= w) continue;
+                float4* e = reinterpret_cast<float4*>(base + px * kTC);
+                float4 t = *e;
+                t = make_float4(fmaf(t.x, sc.x, sh.x), fmaf(t.y, sc.y, sh.y), fmaf(t.z, sc.z, sh.z),
+                                fmaf(t.w, sc.w, sh.w));
+                if (pro_silu) t = make_float4(dev_silu(t.x), dev_silu(t.y), dev_silu(t.z), dev_silu(t.w));
+                *e = t;
+            }
+        }
+        __syncthreads();
     }
     const int j = threadIdx.x & 7, xl = (threadIdx.x >> 3) & 15, rg = threadIdx.x >> 7;
     const int ch = c0 + 4 * j, ox = x0 + xl;
@@ -292,13 +327,17 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 }  // namespace
 
 void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
-                         const float* weight, const float* bias, int epilogue, float* out) {
+                         const float* weight, const float* bias, int epilogue, float* out, const float* pro_scale,
+                         const float* pro_shift, bool pro_silu) {
     MBX_REQUIRE(h < (1 << 20) && w < (1 << 20) && c < (1 << 20), "depthwise: dimension too large");
+    MBX_REQUIRE((pro_scale == nullptr) == (pro_shift == nullptr), "depthwise: prologue needs scale and shift");
+    const bool pro = pro_scale != nullptr;
     const int64_t c_out = epilogue == MBX_EPILOGUE_GLU_SILU ? c / 2 : c;
     const bool vec = c % 4 == 0 && c_out % 4 == 0 && aligned16(x) && aligned16(out) && aligned16(weight) &&
                      aligned16(bias);
     // TMA-tiled kernel where the halo box fits inside the map and one channel box inside c.
-    if (vec && c >= kTC && h >= kTH && w >= kTH && n < 65536 && h < (1 << 20) && w < (1 << 20)) {
+    if (vec && c >= kTC && h >= kTH && w >= kTH && n < 65536 && h < (1 << 20) && w < (1 << 20) &&
+        (!pro || (aligned16(pro_scale) && aligned16(pro_shift)))) {
         const int64_t tiles_x = (w + kTT - 1) / kTT, tiles_y = (h + kTT - 1) / kTT;
         const int64_t cblocks = (c_out + kTC - 1) / kTC;
         if (tiles_x * tiles_y < 65536 && cblocks < 65536) {
@@ -310,21 +349,35 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
             const dim3 grid((unsigned)cblocks, (unsigned)(tiles_x * tiles_y), (unsigned)n);
             auto launch = [&](auto kern, int sets) {
                 const int smem = sets * (int)kSetBytes;
-                static bool configured[3] = {false, false, false};
-                if (!configured[epilogue]) {
+                static bool configured[2][3] = {};
+                if (!configured[pro][epilogue]) {
                     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                                "depthwise smem attribute");
-                    configured[epilogue] = true;
+                    configured[pro][epilogue] = true;
                 }
-                kern<<<grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias, out,
+                kern<<<grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
+                                                                pro_scale, pro_shift, pro_silu ? 1 : 0, out,
                                                                 (int)tiles_x, ctx->dev_err);
             };
-            if (epilogue == MBX_EPILOGUE_NONE) launch(dw3x3_tma_kernel<MBX_EPILOGUE_NONE>, 1);
-            else if (epilogue == MBX_EPILOGUE_RELU) launch(dw3x3_tma_kernel<MBX_EPILOGUE_RELU>, 1);
-            else launch(dw3x3_tma_kernel<MBX_EPILOGUE_GLU_SILU>, 2);
+            if (pro) {
+                if (epilogue == MBX_EPILOGUE_NONE) launch(dw3x3_tma_kernel<MBX_EPILOGUE_NONE, true>, 1);
+                else if (epilogue == MBX_EPILOGUE_RELU) launch(dw3x3_tma_kernel<MBX_EPILOGUE_RELU, true>, 1);
+                else launch(dw3x3_tma_kernel<MBX_EPILOGUE_GLU_SILU, true>, 2);
+            } else {
+                if (epilogue == MBX_EPILOGUE_NONE) launch(dw3x3_tma_kernel<MBX_EPILOGUE_NONE, false>, 1);
+                else if (epilogue == MBX_EPILOGUE_RELU) launch(dw3x3_tma_kernel<MBX_EPILOGUE_RELU, false>, 1);
+                else launch(dw3x3_tma_kernel<MBX_EPILOGUE_GLU_SILU, false>, 2);
+            }
             after_launch(ctx, "depthwise3x3");
             return;
         }
+    }
+    if (pro) {
+        // Shapes the tiled kernel does not take: the GroupNorm goes to scratch first.
+        PoolBuf normed(ctx, size_t(n * h * w * c) * sizeof(float));
+        launch_gn_apply(ctx, x, n, h * w, c, pro_scale, pro_shift, pro_silu, nullptr, normed.as<float>());
+        launch_depthwise3x3(ctx, normed.as<float>(), n, h, w, c, weight, bias, epilogue, out);
+        return;
     }
     const int V = vec ? 4 : 1;
     const int64_t cvo = c_out / V;

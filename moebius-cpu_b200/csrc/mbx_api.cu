@@ -537,6 +537,30 @@ int32_t mbx_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
     });
 }
 
+int32_t mbx_depthwise3x3_fused(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                               const float* pro_scale, const float* pro_shift, int32_t pro_silu,
+                               const float* weight, const float* bias, int32_t epilogue, float* out) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(n >= 0 && h >= 0 && w >= 0 && c > 0, "bad shape");
+        MBX_REQUIRE(epilogue == MBX_EPILOGUE_NONE || epilogue == MBX_EPILOGUE_RELU ||
+                        epilogue == MBX_EPILOGUE_GLU_SILU,
+                    "unknown epilogue");
+        MBX_REQUIRE(epilogue != MBX_EPILOGUE_GLU_SILU || c % 2 == 0, "GLU needs an even channel count");
+        if (n * h * w == 0) return;
+        require_ptr(x, "x");
+        require_ptr(pro_scale, "pro_scale");
+        require_ptr(pro_shift, "pro_shift");
+        require_ptr(weight, "weight");
+        require_ptr(bias, "bias");
+        require_ptr(out, "out");
+        MBX_REQUIRE(out != x, "depthwise3x3: out must not alias x");
+        use_device(ctx);
+        mbx::launch_depthwise3x3(ctx, x, n, h, w, c, weight, bias, epilogue, out, pro_scale, pro_shift,
+                                 pro_silu != 0);
+    });
+}
+
 int32_t mbx_conv1x1(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in,
                     const mbx_param* weight, const float* bias, const float* residual, float* out) {
     return guard([&] {

@@ -114,7 +114,8 @@ void launch_layer_norm(mbx_ctx* ctx, const float* x, int64_t tokens, int64_t c, 
                        const float* beta, float eps, float* out);
 
 void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
-                         const float* weight, const float* bias, int epilogue, float* out);
+                         const float* weight, const float* bias, int epilogue, float* out,
+                         const float* pro_scale = nullptr, const float* pro_shift = nullptr, bool pro_silu = false);
 
 struct ConvShape {
     int64_t n, h, w, c_in;

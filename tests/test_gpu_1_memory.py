@@ -135,6 +135,32 @@ def test_depthwise_matches_oracle(mbx, ctx, oracle, shape, ep):
     assert max_rel_err(got, want) <= GATE
 
 
+@pytest.mark.parametrize("shape,ep,silu", [((2, 20, 50, 96), "relu", True), ((1, 37, 45, 72), "none", True),
+                                           ((1, 40, 40, 64), "glu_silu", False), ((2, 64, 64, 320), "relu", True),
+                                           # shapes the tiled kernel does not take: GroupNorm to scratch first
+                                           ((2, 9, 9, 40), "relu", True), ((1, 20, 20, 12), "none", True)])
+def test_depthwise_group_norm_prologue(mbx, ctx, oracle, shape, ep, silu):
+    """mbx_depthwise3x3_fused equals GroupNorm apply + depthwise bit for bit, and the oracle's
+    GroupNorm (with a per-item add, as the resnets' time embedding) + depthwise at the gate."""
+    import math
+    rng = np.random.default_rng(sum(shape) + len(ep))
+    n, h, w, c = shape
+    groups = math.gcd(c, 32)
+    x = (rng.standard_normal(shape) * 2 + 0.5).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    beta = rng.normal(0, 0.2, c).astype(np.float32)
+    add = rng.normal(0, 0.5, (n, c)).astype(np.float32)
+    wt = (rng.standard_normal((3, 3, c)) / np.sqrt(3.0)).astype(np.float32)
+    b = rng.normal(0, 0.01, c).astype(np.float32)
+    xd, wd, bd = up(ctx, x), up(ctx, wt), up(ctx, b)
+    sc, sh = mbx.group_norm_affine(xd, groups, 1e-5, up(ctx, gamma), up(ctx, beta), add=up(ctx, add))
+    two_pass = mbx.depthwise3x3(mbx.group_norm_apply(xd, sc, sh, silu), wd, bd, ep).numpy()
+    got = mbx.depthwise3x3(xd, wd, bd, ep, prologue=(sc, sh, silu)).numpy()
+    assert np.array_equal(got, two_pass)
+    want = oracle.depthwise3x3(oracle.group_norm(x, groups, 1e-5, gamma, beta, add=add, silu=silu), wt, b, ep)
+    assert max_rel_err(got, want) <= GATE
+
+
 def test_elementwise_fixture(mbx, ctx, extra_fixture):
     f = extra_fixture
     x = up(ctx, f["bt.x"])
