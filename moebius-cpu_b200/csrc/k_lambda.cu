@@ -34,29 +34,49 @@ constexpr int kPad = kWin / 2;
 constexpr int kTile = 8;                    // 8×8 output pixels per CTA
 constexpr int kHalo = kTile + kWin - 1;     // 22
 constexpr int kLamChunk = 256;              // rows per partial (the reference's SOFTMAX_CHUNK)
-constexpr int kLamRows = 32;                // rows staged in shared memory at a time
+constexpr int kColmaxThreads = 256;         // column-max CTA: row slices × columns
 constexpr int kLamCols = 40;                // λ columns per CTA of the partial pass
 constexpr int kTokens = 10;
 
 // ---------------------------------------------------------------- content λ
 
-__global__ void lambda_colmax_kernel(const float* __restrict__ keys, int64_t ks, int64_t rows, int k, int chunks,
-                                     float* __restrict__ pmax) {
+// Per 256-row chunk column maxima. The CTA's threads split into P = max(1, 256 / k) row slices
+// of k columns each (max is exact, so the split does not change the result), then fold the
+// slices in shared memory.
+__global__ void __launch_bounds__(kColmaxThreads) lambda_colmax_kernel(const float* __restrict__ keys, int64_t ks,
+                                                                        int64_t rows, int k, int chunks,
+                                                                        float* __restrict__ pmax) {
+    __shared__ float part[kColmaxThreads];
     const int chunk = blockIdx.x, item = blockIdx.y;
     const float* kb = keys + (int64_t)item * rows * ks;
     const int64_t r0 = (int64_t)chunk * kLamChunk;
     const int64_t r1 = r0 + kLamChunk < rows ? r0 + kLamChunk : rows;
-    for (int kk = threadIdx.x; kk < k; kk += blockDim.x) {
+    const int slices = k < kColmaxThreads ? kColmaxThreads / k : 1;
+    for (int c0 = 0; c0 < k; c0 += kColmaxThreads) {
+        const int cols = min(k - c0, kColmaxThreads);
+        const int p = threadIdx.x / cols, kk = c0 + threadIdx.x - p * cols;
         float m = -FLT_MAX;
-        for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, __ldg(kb + r * ks + kk));
-        pmax[((int64_t)item * chunks + chunk) * k + kk] = m;
+        if (p < slices) {
+#pragma unroll 4
+            for (int64_t r = r0 + p; r < r1; r += slices) m = fmaxf(m, __ldg(kb + r * ks + kk));
+        }
+        part[threadIdx.x] = m;
+        __syncthreads();
+        if (threadIdx.x < cols) {
+            float v = part[threadIdx.x];
+            for (int q = 1; q < slices; ++q) v = fmaxf(v, part[q * cols + threadIdx.x]);
+            pmax[((int64_t)item * chunks + chunk) * k + c0 + threadIdx.x] = v;
+        }
+        __syncthreads();
     }
 }
 
 // Block: k·G threads (G = column groups of 8 in this CTA's slab); thread (kk, g)
-// accumulates λ[kk][j0 + 8g .. +8] over the chunk's rows.
+// accumulates λ[kk][j0 + 8g .. +8] over the chunk's rows. The rows are staged in shared memory
+// `stage` at a time (the whole chunk where it fits), so the loads of a stage are all in flight
+// together.
 __global__ void lambda_partial_kernel(const float* __restrict__ keys, int64_t ks, const float* __restrict__ vals,
-                                      int64_t vs, int64_t rows, int k, int vd, int chunks,
+                                      int64_t vs, int64_t rows, int k, int vd, int chunks, int stage,
                                       const float* __restrict__ pmax, float* __restrict__ plam,
                                       float* __restrict__ psum) {
     extern __shared__ float smem[];
@@ -64,8 +84,8 @@ __global__ void lambda_partial_kernel(const float* __restrict__ keys, int64_t ks
     const int ncols = vd - j0 < kLamCols ? vd - j0 : kLamCols;
     const int groups = (ncols + 7) / 8;
     float* colmax = smem;                          // [k]
-    float* e_t = colmax + k;                       // [kLamRows][k]
-    float* v_t = e_t + kLamRows * k;               // [kLamRows][kLamCols]
+    float* e_t = colmax + k;                       // [stage][k]
+    float* v_t = e_t + stage * k;                  // [stage][kLamCols]
     const int tid = threadIdx.x, nthr = blockDim.x;
     for (int kk = tid; kk < k; kk += nthr) {
         float m = -FLT_MAX;
@@ -83,12 +103,14 @@ __global__ void lambda_partial_kernel(const float* __restrict__ keys, int64_t ks
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
     float s = 0.0f;
     __syncthreads();
-    for (int64_t rt = r0; rt < r1; rt += kLamRows) {
-        const int nr = (int)(r1 - rt < kLamRows ? r1 - rt : kLamRows);
+    for (int64_t rt = r0; rt < r1; rt += stage) {
+        const int nr = (int)(r1 - rt < stage ? r1 - rt : stage);
+#pragma unroll 4
         for (int i = tid; i < nr * k; i += nthr) {
             const int rr = i / k, c = i - rr * k;
             e_t[rr * k + c] = expf(__ldg(kb + (rt + rr) * ks + c) - colmax[c]);
         }
+#pragma unroll 4
         for (int i = tid; i < nr * kLamCols; i += nthr) {
             const int rr = i / kLamCols, c = i - rr * kLamCols;
             v_t[rr * kLamCols + c] = c < ncols ? __ldg(vb + (rt + rr) * vs + j0 + c) : 0.0f;
@@ -429,22 +451,30 @@ void launch_lambda_content(mbx_ctx* ctx, const float* keys, int64_t ks, const fl
     MBX_REQUIRE(items < 65536, "lambda: too many items");
     const int64_t chunks = lambda_chunks(rows);
     MBX_REQUIRE(chunks < (int64_t(1) << 31), "lambda: too many rows");
-    lambda_colmax_kernel<<<dim3((unsigned)chunks, (unsigned)items), (unsigned)std::min<int64_t>(k, 256), 0,
-                           ctx->stream>>>(keys, ks, rows, (int)k, (int)chunks, pmax);
+    lambda_colmax_kernel<<<dim3((unsigned)chunks, (unsigned)items), kColmaxThreads, 0, ctx->stream>>>(
+        keys, ks, rows, (int)k, (int)chunks, pmax);
     after_launch(ctx, "lambda_colmax");
     const int slabs = (int)((vd + kLamCols - 1) / kLamCols);
     const int groups = (int)(std::min<int64_t>(vd, kLamCols) + 7) / 8;
     const int threads = (int)k * groups;
     MBX_REQUIRE(threads <= 1024, "lambda: k too large for one CTA");
-    const int smem = (int)(k + kLamRows * k + kLamRows * kLamCols) * 4;
+    // Rows per staging pass: the whole chunk where its exponentials and values fit (in 100 KB, for
+    // two CTAs per SM, when the grid is larger than one CTA per SM), else the largest power of two
+    // down to 32.
+    const int64_t ctas = chunks * items * slabs;
+    const int limit = ctas <= ctx->sm_count ? 227 * 1024 : 100 * 1024;
+    int stage = kLamChunk;
+    auto stage_bytes = [&](int r) { return (int)(k + (int64_t)r * k + (int64_t)r * kLamCols) * 4; };
+    while (stage > 32 && stage_bytes(stage) > limit) stage /= 2;
+    const int smem = stage_bytes(stage);
     static bool configured = false;
     if (!configured) {
-        set_smem(lambda_partial_kernel, 64 * 1024);
+        set_smem(lambda_partial_kernel, 227 * 1024);
         configured = true;
     }
-    MBX_REQUIRE(smem <= 64 * 1024, "lambda: k too large for the staging tile");
+    MBX_REQUIRE(smem <= 227 * 1024, "lambda: k too large for the staging tile");
     lambda_partial_kernel<<<dim3((unsigned)chunks, (unsigned)items, (unsigned)slabs), threads, smem, ctx->stream>>>(
-        keys, ks, vals, vs, rows, (int)k, (int)vd, (int)chunks, pmax, plam, psum);
+        keys, ks, vals, vs, rows, (int)k, (int)vd, (int)chunks, stage, pmax, plam, psum);
     after_launch(ctx, "lambda_partial");
     lambda_finalize_kernel<<<grid_for(ctx, items * k * vd, 256), 256, 0, ctx->stream>>>(plam, psum, items, (int)k,
                                                                                         (int)vd, (int)chunks, lam);
