@@ -34,13 +34,13 @@ constexpr int kPad = kWin / 2;
 constexpr int kTile = 8;                    // 8×8 output pixels per CTA
 constexpr int kHalo = kTile + kWin - 1;     // 22
 constexpr int kLamChunk = 256;              // rows per partial (the reference's SOFTMAX_CHUNK)
-constexpr int kColmaxThreads = 256;         // column-max CTA: row slices × columns
+constexpr int kColmaxThreads = 1024;        // column-max CTA: row slices × columns
 constexpr int kLamCols = 40;                // λ columns per CTA of the partial pass
 constexpr int kTokens = 10;
 
 // ---------------------------------------------------------------- content λ
 
-// Per 256-row chunk column maxima. The CTA's threads split into P = max(1, 256 / k) row slices
+// Per 256-row chunk column maxima. The CTA's threads split into P = max(1, 1024 / k) row slices
 // of k columns each (max is exact, so the split does not change the result), then fold the
 // slices in shared memory.
 __global__ void __launch_bounds__(kColmaxThreads) lambda_colmax_kernel(const float* __restrict__ keys, int64_t ks,
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kColmaxThreads) lambda_colmax_kernel(const flo
         const int p = threadIdx.x / cols, kk = c0 + threadIdx.x - p * cols;
         float m = -FLT_MAX;
         if (p < slices) {
-#pragma unroll 4
+#pragma unroll 8
             for (int64_t r = r0 + p; r < r1; r += slices) m = fmaxf(m, __ldg(kb + r * ks + kk));
         }
         part[threadIdx.x] = m;
