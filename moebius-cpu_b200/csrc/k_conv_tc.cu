@@ -37,8 +37,8 @@
 // adds each MMA's products into its f32 accumulator with truncation, which
 // biases long sums toward zero (about 1e-4 relative at K = 11520; the error
 // grows with the length of each unbroken sum). So K is cut into equal segments
-// of at most kSegMaxChunks chunks (512 K-elements; a K of up to 512 is one
-// segment, so short-K tiles skip the fold and hold one accumulator): the MMA warp
+// of at most 512 K-elements for f16 weights, 256 for f32 weights (a shorter K
+// is one segment, so short-K tiles skip the fold and hold one accumulator): the MMA warp
 // alternates between two TMEM accumulators, and the drain warps fold each
 // finished segment into a running sum in shared memory with round-to-nearest
 // f32 adds while the next segment accumulates (error then ≈ an f32 FMA loop).
@@ -65,11 +65,16 @@ constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int kThreads = 448;  // 14 warps; see the role map above
 constexpr int kMinStgSlots = 3;  // raw A staging slots (16 KB each): at least, and at most
 constexpr int kMaxStgSlots = 6;
-constexpr int kSegMaxChunks = 16;  // at most this many K chunks (of 32) per accumulator segment
+// At most this many K chunks (of 32) per accumulator segment: f16 weights add two truncating MMAs
+// per K step, f32 weights three, so their segments are shorter.
+constexpr int kSegMaxChunksF16 = 16;
+constexpr int kSegMaxChunksF32 = 8;
 
-// Chunks per segment: K split into the fewest segments of at most kSegMaxChunks, as equal as possible.
+// Chunks per segment: K split into the fewest segments of at most the cap, as equal as possible.
+template <bool F32W>
 __device__ __forceinline__ int seg_chunks(int k_chunks) {
-    const int n = (k_chunks + kSegMaxChunks - 1) / kSegMaxChunks;
+    constexpr int cap = F32W ? kSegMaxChunksF32 : kSegMaxChunksF16;
+    const int n = (k_chunks + cap - 1) / cap;
     return (k_chunks + n - 1) / n;
 }
 constexpr int kMaxBn = 160;  // 2 · bn accumulator columns + A stages of 64 columns ≤ 512 (3 stages at 160)
@@ -345,7 +350,7 @@ __global__ void __maxnreg__(128)
     const bool split = args.a_tma == 1;
     const int conv_threads = split ? 256 : 128;
     const int K = args.k_chunks;
-    const int seg_len = seg_chunks(K);
+    const int seg_len = seg_chunks<F32W>(K);
     const int nseg = (K + seg_len - 1) / seg_len;
     // Persistent CTA: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (N tile fastest, so the CTAs
     // in flight share A rows through L2). Every ring keeps its position and phase across tiles,
