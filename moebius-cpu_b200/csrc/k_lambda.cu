@@ -74,12 +74,14 @@ __global__ void __launch_bounds__(kColmaxThreads) lambda_colmax_kernel(const flo
 // Block: k·G threads (G = column groups of 8 in this CTA's slab); thread (kk, g)
 // accumulates λ[kk][j0 + 8g .. +8] over the chunk's rows. The rows are staged in shared memory
 // `stage` at a time (the whole chunk where it fits), so the loads of a stage are all in flight
-// together.
+// together. VEC: 128-bit staging loads (k, vd and both row strides multiples of 4, 16-byte aligned).
+template <bool VEC>
 __global__ void lambda_partial_kernel(const float* __restrict__ keys, int64_t ks, const float* __restrict__ vals,
                                       int64_t vs, int64_t rows, int k, int vd, int chunks, int stage,
                                       const float* __restrict__ pmax, float* __restrict__ plam,
                                       float* __restrict__ psum) {
-    extern __shared__ float smem[];
+    extern __shared__ float4 smem_v[];  // float4: the staging tiles take 128-bit stores
+    float* smem = reinterpret_cast<float*>(smem_v);
     const int chunk = blockIdx.x, item = blockIdx.y, j0 = blockIdx.z * kLamCols;
     const int ncols = vd - j0 < kLamCols ? vd - j0 : kLamCols;
     const int groups = (ncols + 7) / 8;
@@ -105,15 +107,35 @@ __global__ void lambda_partial_kernel(const float* __restrict__ keys, int64_t ks
     __syncthreads();
     for (int64_t rt = r0; rt < r1; rt += stage) {
         const int nr = (int)(r1 - rt < stage ? r1 - rt : stage);
+        if constexpr (VEC) {
+            const int k4 = k >> 2;
 #pragma unroll 4
-        for (int i = tid; i < nr * k; i += nthr) {
-            const int rr = i / k, c = i - rr * k;
-            e_t[rr * k + c] = expf(__ldg(kb + (rt + rr) * ks + c) - colmax[c]);
-        }
+            for (int i = tid; i < nr * k4; i += nthr) {
+                const int rr = i / k4, c = 4 * (i - rr * k4);
+                const float4 kv = __ldg(reinterpret_cast<const float4*>(kb + (rt + rr) * ks + c));
+                *reinterpret_cast<float4*>(e_t + rr * k + c) =
+                    make_float4(expf(kv.x - colmax[c]), expf(kv.y - colmax[c + 1]), expf(kv.z - colmax[c + 2]),
+                                expf(kv.w - colmax[c + 3]));
+            }
+            constexpr int kCols4 = kLamCols / 4;
 #pragma unroll 4
-        for (int i = tid; i < nr * kLamCols; i += nthr) {
-            const int rr = i / kLamCols, c = i - rr * kLamCols;
-            v_t[rr * kLamCols + c] = c < ncols ? __ldg(vb + (rt + rr) * vs + j0 + c) : 0.0f;
+            for (int i = tid; i < nr * kCols4; i += nthr) {
+                const int rr = i / kCols4, c = 4 * (i - rr * kCols4);
+                *reinterpret_cast<float4*>(v_t + rr * kLamCols + c) =
+                    c < ncols ? __ldg(reinterpret_cast<const float4*>(vb + (rt + rr) * vs + j0 + c))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        } else {
+#pragma unroll 4
+            for (int i = tid; i < nr * k; i += nthr) {
+                const int rr = i / k, c = i - rr * k;
+                e_t[rr * k + c] = expf(__ldg(kb + (rt + rr) * ks + c) - colmax[c]);
+            }
+#pragma unroll 4
+            for (int i = tid; i < nr * kLamCols; i += nthr) {
+                const int rr = i / kLamCols, c = i - rr * kLamCols;
+                v_t[rr * kLamCols + c] = c < ncols ? __ldg(vb + (rt + rr) * vs + j0 + c) : 0.0f;
+            }
         }
         __syncthreads();
         if (active) {
@@ -467,14 +489,20 @@ void launch_lambda_content(mbx_ctx* ctx, const float* keys, int64_t ks, const fl
     auto stage_bytes = [&](int r) { return (int)(k + (int64_t)r * k + (int64_t)r * kLamCols) * 4; };
     while (stage > 32 && stage_bytes(stage) > limit) stage /= 2;
     const int smem = stage_bytes(stage);
-    static bool configured = false;
-    if (!configured) {
-        set_smem(lambda_partial_kernel, 227 * 1024);
-        configured = true;
-    }
     MBX_REQUIRE(smem <= 227 * 1024, "lambda: k too large for the staging tile");
-    lambda_partial_kernel<<<dim3((unsigned)chunks, (unsigned)items, (unsigned)slabs), threads, smem, ctx->stream>>>(
-        keys, ks, vals, vs, rows, (int)k, (int)vd, (int)chunks, stage, pmax, plam, psum);
+    const bool vec = k % 4 == 0 && vd % 4 == 0 && ks % 4 == 0 && vs % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(keys) & 15) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15) == 0;
+    auto launch = [&](auto kern, bool& configured) {
+        if (!configured) {
+            set_smem(kern, 227 * 1024);
+            configured = true;
+        }
+        kern<<<dim3((unsigned)chunks, (unsigned)items, (unsigned)slabs), threads, smem, ctx->stream>>>(
+            keys, ks, vals, vs, rows, (int)k, (int)vd, (int)chunks, stage, pmax, plam, psum);
+    };
+    static bool configured_vec = false, configured_scalar = false;
+    if (vec) launch(lambda_partial_kernel<true>, configured_vec);
+    else launch(lambda_partial_kernel<false>, configured_scalar);
     after_launch(ctx, "lambda_partial");
     lambda_finalize_kernel<<<grid_for(ctx, items * k * vd, 256), 256, 0, ctx->stream>>>(plam, psum, items, (int)k,
                                                                                         (int)vd, (int)chunks, lam);
