@@ -48,6 +48,9 @@ def test_invalid_arguments_return_status_and_message():
     assert lib.mbx_silu_inplace(None, None, 4) == mbx.abi.ERR_INVALID_ARGUMENT
     assert b"context" in lib.mbx_last_error()
     assert lib.mbx_ctx_create(0, None) == mbx.abi.ERR_INVALID_ARGUMENT
+    assert lib.mbx_depthwise3x3_fused(None, None, 1, 4, 4, 8, None, None, 1, None, None, 1, None) == \
+        mbx.abi.ERR_INVALID_ARGUMENT
+    assert b"context" in lib.mbx_last_error()
 
 
 def test_context_needs_a_b200():
