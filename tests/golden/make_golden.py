@@ -1,6 +1,6 @@
 """Writes the committed golden fixtures under tests/golden/.
 
-    python tests/golden/make_golden.py [--reference-root PATH]
+    python tests/golden/make_golden.py --reference-root PATH   (or MOEBIUS_REFERENCE_ROOT=PATH)
 
 1. ``kernels_ref.safetensors``: the reference's own kernel fixture
    (moebius-cpu ``tests/fixtures/kernels.safetensors``, produced by its
@@ -205,8 +205,11 @@ def converted_manifest(reference_root):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-root", default="/root/reference")
+    ap.add_argument("--reference-root", default=os.environ.get("MOEBIUS_REFERENCE_ROOT"),
+                    help="a moebius-cpu checkout (default: $MOEBIUS_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference_root:
+        ap.error("give --reference-root or set MOEBIUS_REFERENCE_ROOT to a moebius-cpu checkout")
     src = os.path.join(args.reference_root, "tests", "fixtures", "kernels.safetensors")
     ref = load_file(src)
     save_file({k: np.ascontiguousarray(v) for k, v in ref.items()}, os.path.join(HERE, "kernels_ref.safetensors"),
