@@ -515,7 +515,9 @@ def run_ours(args):
             "conv": conv, "memory_sweep": sweep, "vae_decoder": vae_line,
             "hbm_peak_gbs": hbm, "hbm_peak_kind": peak_kind,
         }
-        if not args.skip_cpu:
+        # The CPU baseline is timed at N = 1 only: under torchrun the other ranks would be
+        # polling a collective meanwhile, taking host cores from the timed CPU run.
+        if not args.skip_cpu and world == 1:
             line["cpu_baseline"] = cpu_inpaint_baseline(args.small)
         print(json.dumps(line), flush=True)
     eng.close()

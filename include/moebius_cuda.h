@@ -85,6 +85,14 @@ void *mbx_ctx_stream(mbx_ctx *ctx);
 int32_t mbx_ctx_synchronize(mbx_ctx *ctx);
 /* Number of this library's kernel launches on this context so far. */
 uint64_t mbx_ctx_launch_count(const mbx_ctx *ctx);
+/* Self-test of the device-side error path (no reference counterpart: the
+ * reference runs on the CPU and has no device waits). Enqueues one kernel whose
+ * single thread waits on a barrier that nothing arrives at, giving up after
+ * `cycles` clock cycles (1 <= cycles <= 2^32, about 2 s at most) as every
+ * bounded wait in this library does; no copy is issued. The next
+ * mbx_ctx_synchronize() then returns MBX_ERR_TIMEOUT and clears the record, and
+ * the context stays usable. */
+int32_t mbx_selftest_wait_timeout(mbx_ctx *ctx, int64_t cycles);
 
 /* ---------------------------------------------------------------- memory
  * A stream-ordered best-fit caching pool: the device analogue of the

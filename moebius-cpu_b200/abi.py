@@ -14,6 +14,7 @@ REPO = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "lib", "libmoebius_cuda.so")
 HEADER = os.path.join(REPO, "include", "moebius_cuda.h")
 ENGINE_HEADER = os.path.join(REPO, "include", "moebius_cuda_engine.h")
+COMPAT_HEADER = os.path.join(REPO, "include", "moebius_cpu.h")
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
@@ -81,6 +82,7 @@ SIGNATURES = {
     "mbx_ctx_stream": (_vp, [_vp]),
     "mbx_ctx_synchronize": (_i32, [_vp]),
     "mbx_ctx_launch_count": (_u64, [_vp]),
+    "mbx_selftest_wait_timeout": (_i32, [_vp, _i64]),
     "mbx_alloc": (_i32, [_vp, _sz, _pvp]),
     "mbx_free": (_i32, [_vp, _vp]),
     "mbx_pool_release_below": (_i32, [_vp, _sz]),
@@ -154,6 +156,16 @@ SIGNATURES = {
     "mbx_ddim_alphas_cumprod": (_i32, [_pf32]),
 }
 
+# include/moebius_cpu.h: the reference's own C API names (a drop-in for moebius-cpu hosts).
+COMPAT_SIGNATURES = {
+    "moebius_abi_version": (ctypes.c_uint32, []),
+    "moebius_last_error": (ctypes.c_char_p, []),
+    "moebius_engine_create": (_i32, [ctypes.c_char_p, _u32, _pvp]),
+    "moebius_engine_destroy": (None, [_vp]),
+    "moebius_inpaint": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, ctypes.POINTER(InpaintParams),
+                               PROGRESS_FN, _vp, ctypes.POINTER(Rect)]),
+}
+
 _lib = None
 
 
@@ -169,6 +181,11 @@ def header_symbols() -> list[str]:
     return sorted(set(re.findall(r"\b(mbx_[a-z0-9_]+)\s*\(", text)) - {"mbx_progress_fn"})
 
 
+def compat_header_symbols() -> list[str]:
+    """Function names declared in include/moebius_cpu.h."""
+    return sorted(set(re.findall(r"\b(moebius_[a-z0-9_]+)\s*\(", open(COMPAT_HEADER).read())))
+
+
 def lib() -> ctypes.CDLL:
     """The loaded library with argtypes set. Raises if it was not built."""
     global _lib
@@ -177,7 +194,7 @@ def lib() -> ctypes.CDLL:
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C moebius-cpu_b200/csrc` "
                                "(or __graft_entry__.build()); there is no CPU fallback")
         handle = ctypes.CDLL(LIB_PATH)
-        for name, (res, args) in SIGNATURES.items():
+        for name, (res, args) in {**SIGNATURES, **COMPAT_SIGNATURES}.items():
             fn = getattr(handle, name)
             fn.restype = res
             fn.argtypes = args

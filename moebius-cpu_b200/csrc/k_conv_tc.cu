@@ -48,7 +48,8 @@
 // pass through shared memory.
 // The last segment is folded straight into the epilogue: + bias (+ residual)
 // → global. Every mbarrier wait is bounded; on timeout the CTA records the
-// error in the context's device error word, skips its stores and exits.
+// error in the context's device error word, skips its stores, waits (bounded)
+// until the bulk copies it issued have landed, and exits.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -132,23 +133,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ void record_timeout(int* err, int kernel, int site) {
+    if (atomicCAS(err, 0, kErrWaitTimeout) == 0) {
+        err[1] = kernel;
+        err[2] = site;
+    }
+}
+
 // Bounded wait for phase `parity` of `bar`. Returns false when the CTA is
-// aborting (another role gave up) or after kWaitLimit cycles, in which case
+// aborting (another role gave up) or after `limit` cycles, in which case
 // the error is recorded and the abort flag raised.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int site, volatile int* abort_flag,
-                                       bool honour_abort) {
+                                       bool honour_abort, long long limit = kWaitLimit, int kernel = kKConvTc) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (honour_abort && *abort_flag) return false;
-        if (clock64() - t0 > kWaitLimit) {
-            if (atomicCAS(err, 0, kErrWaitTimeout) == 0) {
-                err[1] = kKConvTc;
-                err[2] = site;
-            }
+        if (clock64() - t0 > limit) {
+            record_timeout(err, kernel, site);
             *abort_flag = 1;
             return false;
+        }
+    }
+}
+
+// Abort path: waits, until the clock64 value `deadline`, for phase `parity` of `bar`, a phase
+// armed by a bulk copy of this CTA; it completes once the copy has landed (and every other
+// arrival the phase counts has been made).
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, long long deadline, int* err, int site) {
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() > deadline) {
+            record_timeout(err, kKConvTc, site);
+            return;
         }
     }
 }
@@ -342,6 +359,11 @@ __global__ void __maxnreg__(128)
     const uint32_t misc = final_bar + 8u;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (misc - base));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
+    volatile int* s_wfills = reinterpret_cast<volatile int*>(gbase + (misc + 8 - base));
+    // Fill counts for the abort path: arrivals this converter thread made on the stage full
+    // barriers, weight tiles and A boxes the TMA issuers armed (a CTA's chunk count stays below
+    // 2^31, checked at launch).
+    int conv_fills = 0, w_fills = 0, a_fills = 0;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Converters: warps 10-13, plus warps 0-3 for 1×1 convs with TMA-fed A rows (the loader warps are
@@ -349,6 +371,7 @@ __global__ void __maxnreg__(128)
     // eight, each thread converts half of its row's 32 channels.
     const bool split = args.a_tma == 1;
     const int conv_threads = split ? 256 : 128;
+    const bool is_converter = warp >= 10 || (split && warp < 4);
     const int K = args.k_chunks;
     const int seg_len = seg_chunks<F32W>(K);
     const int nseg = (K + seg_len - 1) / seg_len;
@@ -479,7 +502,7 @@ __global__ void __maxnreg__(128)
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
-    } else if (warp >= 10 || (split && warp < 4)) {
+    } else if (is_converter) {
         // ------------------------------------------------------------ converters
         // One tile row per thread (its TMEM lane): staging row → [SiLU](x·scale + shift) at a
         // spatially valid tap (padding stays zero; channel padding beyond c_in meets zero
@@ -562,6 +585,7 @@ __global__ void __maxnreg__(128)
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(a_full_bar(a));
+                ++conv_fills;
                 if (++q == nstg) {
                     q = 0;
                     qphase ^= 1;
@@ -688,6 +712,7 @@ __global__ void __maxnreg__(128)
                         tma_load_4d(stg, &tmap_a, cchunk * BK, x0 + kx - args.pad_l, y0 + ky - args.pad_t, item,
                                     sfull_bar(q));
                     }
+                    ++a_fills;
                     if (++q == nstg) {
                         q = 0;
                         qphase ^= 1;
@@ -713,12 +738,14 @@ __global__ void __maxnreg__(128)
                     mbar_arrive_expect_tx(b_full_bar(s), bstage_bytes);
                     tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, b_full_bar(s));
                     if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, b_full_bar(s));
+                    ++w_fills;
                     if (++s == bstages) {
                         s = 0;
                         sphase ^= 1;
                     }
                 }
             }
+            *s_wfills = w_fills;
         }
         __syncwarp();
     } else if (warp >= 6 && warp < 10) {
@@ -801,10 +828,44 @@ __global__ void __maxnreg__(128)
     }
     tc_fence_before();
     __syncthreads();
+    if (*abort_flag) {  // uniform: nothing raises the flag after the barrier above
+        // Abort path: no bulk copy may still be writing this CTA's shared memory when it exits,
+        // so the TMA issuers wait for the last phase of every slot they armed. A weight stage's
+        // phase also counts one arrival per converter thread: converters that stopped early make
+        // theirs for the fills the weight issuer armed. The weight issuer arms fill i only after
+        // fill i - stages was consumed, so it is at most `stages` fills ahead of any converter,
+        // and each such arrival lands in the phase of its own fill.
+        const long long deadline = clock64() + kWaitLimit;
+        if (is_converter) {
+            const int armed = *s_wfills;
+            for (int i = conv_fills; i < armed; ++i) mbar_arrive(b_full_bar(i % bstages));
+        }
+        if (warp == 5 && lane == 0)
+            for (int i = max(0, w_fills - bstages); i < w_fills; ++i)
+                drain_wait(b_full_bar(i % bstages), (uint32_t)((i / bstages) & 1), deadline, args.err, 10);
+        if (warp == 5 && lane == 1 && args.a_tma)
+            for (int i = max(0, a_fills - nstg); i < a_fills; ++i)
+                drain_wait(sfull_bar(i % nstg), (uint32_t)((i / nstg) & 1), deadline, args.err, 11);
+        __syncthreads();
+    }
     if (warp == 4) {
         tc_fence_after();
         tmem_dealloc(tmem, (uint32_t)args.tmem_cols);
     }
+}
+
+// Self-test of the bounded-wait error path: one thread initialises a barrier that nothing will
+// ever arrive at and waits on it as the conv roles wait, with the caller's limit; no copy is
+// issued. The wait gives up, records the timeout in the context's error word, and the kernel
+// returns.
+__global__ void wait_probe_kernel(int* err, long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+    (void)mbar_wait(b, 0, err, 12, &abort_flag, false, limit, kKWaitProbe);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -854,18 +915,18 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtenso
     auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
     const int stage = (F32W ? 2 : 1) * a.bn * 128;
     const int smem = a.stages * stage + a.stg_slots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
-    static bool configured = false;
-    if (!configured) {
-        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
-                   "conv smem attribute");
+    // The register check depends on the build only, so once per process suffices; the
+    // shared-memory limit is a per-device attribute.
+    static std::once_flag checked;
+    std::call_once(checked, [&] {
         cudaFuncAttributes fa;
         check_cuda(cudaFuncGetAttributes(&fa, kernel), "conv attributes");
         if (fa.maxThreadsPerBlock < kThreads)
             fail(MBX_ERR_INTERNAL, "conv kernel built with " + std::to_string(fa.numRegs) +
                                        " registers per thread cannot launch " + std::to_string(kThreads) +
                                        " threads");
-        configured = true;
-    }
+    });
+    ensure_smem_limit(reinterpret_cast<const void*>(kernel), kMaxSmem, "conv smem attribute");
     (void)m_tiles;
     // Persistent: one CTA per SM (the shared-memory footprint allows one), tiles strided over them.
     const int64_t blocks = std::min<int64_t>(a.tiles, (int64_t)ctx->sm_count);
@@ -873,6 +934,11 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtenso
 }
 
 }  // namespace
+
+void launch_wait_probe(mbx_ctx* ctx, int64_t cycles) {
+    wait_probe_kernel<<<1, 1, 0, ctx->stream>>>(ctx->dev_err, (long long)cycles);
+    after_launch(ctx, "wait probe");
+}
 
 void encode_tensor_map_f32(CUtensorMap* map, const float* base, int rank, const uint64_t* dims,
                            const uint64_t* strides, const uint32_t* box, bool swizzle128) {
@@ -961,6 +1027,9 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     const int64_t m_tiles = (a.m_total + BM - 1) / BM;
     MBX_REQUIRE(m_tiles * a.n_tiles < (int64_t(1) << 40), "conv: too many tiles");
     a.tiles = m_tiles * a.n_tiles;
+    // The abort path counts a CTA's K chunks in 32-bit integers.
+    MBX_REQUIRE((a.tiles + ctx->sm_count - 1) / ctx->sm_count * a.k_chunks < (int64_t(1) << 31),
+                "conv: too many K chunks per CTA");
     const bool vec4 = (s.c_in & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                       (!pro_scale || ((reinterpret_cast<uintptr_t>(pro_scale) & 15) == 0 &&
                                       (reinterpret_cast<uintptr_t>(pro_shift) & 15) == 0));

@@ -215,11 +215,10 @@ __global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_co
                 : "memory");
     }
     // Bounded wait for the boxes; on timeout (any thread's) the error is recorded and the CTA
-    // writes nothing.
+    // writes nothing. The boxes may still be in flight then: thread 0 keeps waiting for them,
+    // bounded again, so the CTA (and its shared memory) does not retire under a pending copy.
     {
-        const long long t0 = clock64();
-        int timed_out = 0;
-        while (true) {
+        auto landed = [&]() {
             uint32_t ok;
             asm volatile(
                 "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, "
@@ -227,14 +226,23 @@ __global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_co
                 : "=r"(ok)
                 : "r"(b)
                 : "memory");
-            if (ok) break;
+            return ok != 0;
+        };
+        const long long t0 = clock64();
+        int timed_out = 0;
+        while (!landed()) {
             if (clock64() - t0 > kDwWaitLimit) {
                 timed_out = 1;
                 break;
             }
         }
         if (__syncthreads_or(timed_out)) {
-            if (threadIdx.x == 0 && atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
+            if (threadIdx.x == 0) {
+                if (atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
+                const long long t1 = clock64();
+                while (!landed() && clock64() - t1 <= kDwWaitLimit) {
+                }
+            }
             return;
         }
     }
@@ -349,12 +357,7 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
             const dim3 grid((unsigned)cblocks, (unsigned)(tiles_x * tiles_y), (unsigned)n);
             auto launch = [&](auto kern, int sets) {
                 const int smem = sets * (int)kSetBytes;
-                static bool configured[2][3] = {};
-                if (!configured[pro][epilogue]) {
-                    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                               "depthwise smem attribute");
-                    configured[pro][epilogue] = true;
-                }
+                ensure_smem_limit(reinterpret_cast<const void*>(kern), smem, "depthwise smem attribute");
                 kern<<<grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
                                                                 pro_scale, pro_shift, pro_silu ? 1 : 0, out,
                                                                 (int)tiles_x, ctx->dev_err);

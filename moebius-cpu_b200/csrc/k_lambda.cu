@@ -458,8 +458,7 @@ void dispatch_vs(int vs, F&& f) {
 
 template <typename K>
 void set_smem(K kernel, int bytes) {
-    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
-               "lambda smem attribute");
+    ensure_smem_limit(reinterpret_cast<const void*>(kernel), bytes, "lambda smem attribute");
 }
 
 }  // namespace
@@ -492,17 +491,13 @@ void launch_lambda_content(mbx_ctx* ctx, const float* keys, int64_t ks, const fl
     MBX_REQUIRE(smem <= 227 * 1024, "lambda: k too large for the staging tile");
     const bool vec = k % 4 == 0 && vd % 4 == 0 && ks % 4 == 0 && vs % 4 == 0 &&
                      (reinterpret_cast<uintptr_t>(keys) & 15) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15) == 0;
-    auto launch = [&](auto kern, bool& configured) {
-        if (!configured) {
-            set_smem(kern, 227 * 1024);
-            configured = true;
-        }
+    auto launch = [&](auto kern) {
+        set_smem(kern, 227 * 1024);
         kern<<<dim3((unsigned)chunks, (unsigned)items, (unsigned)slabs), threads, smem, ctx->stream>>>(
             keys, ks, vals, vs, rows, (int)k, (int)vd, (int)chunks, stage, pmax, plam, psum);
     };
-    static bool configured_vec = false, configured_scalar = false;
-    if (vec) launch(lambda_partial_kernel<true>, configured_vec);
-    else launch(lambda_partial_kernel<false>, configured_scalar);
+    if (vec) launch(lambda_partial_kernel<true>);
+    else launch(lambda_partial_kernel<false>);
     after_launch(ctx, "lambda_partial");
     lambda_finalize_kernel<<<grid_for(ctx, items * k * vd, 256), 256, 0, ctx->stream>>>(plam, psum, items, (int)k,
                                                                                         (int)vd, (int)chunks, lam);
@@ -520,11 +515,7 @@ void launch_self_position(mbx_ctx* ctx, const float* q, const float* lam, const 
         const int smem = (kHalo * kHalo * halo_stride(VS) + (int)k * VS) * 4;
         MBX_REQUIRE(smem <= 227 * 1024, "self lambda: head width too large");
         auto kern = self_position_kernel<VS>;
-        static bool configured = false;
-        if (!configured) {
-            set_smem(kern, 227 * 1024);
-            configured = true;
-        }
+        set_smem(kern, 227 * 1024);
         kern<<<dim3((unsigned)(tiles_x * tiles_y), (unsigned)(k / VS), (unsigned)n), 512, smem, ctx->stream>>>(
             q, lam, a, (int)a_stride, v, v_stride, (int)h, (int)w, (int)k, tiles_x, out);
     });
@@ -541,11 +532,7 @@ void launch_cross_position(mbx_ctx* ctx, const float* q, const float* e_table, c
         const int smem = ((int)k * VS + kTokens * VS) * 4;
         MBX_REQUIRE(smem <= 227 * 1024, "cross lambda: head width too large");
         auto kern = cross_position_kernel<VS>;
-        static bool configured = false;
-        if (!configured) {
-            set_smem(kern, 227 * 1024);
-            configured = true;
-        }
+        set_smem(kern, 227 * 1024);
         kern<<<dim3((unsigned)((hw + 63) / 64), (unsigned)(k / VS), (unsigned)n), 512, smem, ctx->stream>>>(
             q, e_table, lam, vtab, (int)period, hw, (int)k, out);
     });

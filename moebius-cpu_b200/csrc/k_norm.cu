@@ -290,9 +290,7 @@ void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int
     const size_t smem = size_t(2) * rows * cs * sizeof(float);
     dim3 grid((unsigned)chunks, (unsigned)n, (unsigned)(groups / gps));
     auto run = [&](auto kernel) {
-        if (smem > 48 * 1024)
-            check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                       "gn smem attribute");
+        if (smem > 48 * 1024) ensure_smem_limit(reinterpret_cast<const void*>(kernel), (int)smem, "gn smem attribute");
         kernel<<<grid, kGnThreads, smem, ctx->stream>>>(x, hw, (int)c, (int)groups, (int)cs, add, part);
     };
     if (vec)

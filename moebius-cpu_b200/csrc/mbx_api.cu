@@ -152,6 +152,18 @@ void Pool::release_below(size_t min_bytes) {
 
 void record_error(int32_t code, const char* msg) { set_error(code, msg); }
 
+void ensure_smem_limit(const void* kernel, int bytes, const char* what) {
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, int> set;  // (device, kernel) -> limit set
+    std::lock_guard<std::mutex> lock(mu);
+    int& have = set[{device, kernel}];
+    if (have >= bytes) return;
+    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+    have = bytes;
+}
+
 
 }  // namespace mbx
 
@@ -233,6 +245,15 @@ int32_t mbx_ctx_synchronize(mbx_ctx* ctx) {
             mbx::fail(MBX_ERR_TIMEOUT, "device wait timed out (kernel " + std::to_string(rec[1]) + ", site " +
                                            std::to_string(rec[2]) + ")");
         }
+    });
+}
+
+int32_t mbx_selftest_wait_timeout(mbx_ctx* ctx, int64_t cycles) {
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(cycles >= 1 && cycles <= (int64_t(1) << 32), "cycles must be in [1, 2^32]");
+        use_device(ctx);
+        mbx::launch_wait_probe(ctx, cycles);
     });
 }
 

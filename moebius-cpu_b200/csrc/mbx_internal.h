@@ -39,7 +39,7 @@ inline void check_cuda(cudaError_t e, const char* what) {
 // Device-side error record written by kernels whose bounded waits gave up:
 // [0] = code (0 = none), [1] = kernel id, [2] = detail (barrier / stage).
 enum DeviceErr : int { kErrNone = 0, kErrWaitTimeout = 1 };
-enum KernelId : int { kKConvTc = 1, kKGnSlab = 2, kKDepthwise = 3 };
+enum KernelId : int { kKConvTc = 1, kKGnSlab = 2, kKDepthwise = 3, kKWaitProbe = 4 };
 
 // Stream-ordered best-fit caching allocator (device analogue of the
 // reference's Scratch pool). All blocks are used on the context stream, so a
@@ -92,6 +92,13 @@ namespace mbx {
 // catch their own exceptions).
 void record_error(int32_t code, const char* msg);
 
+// Raises `kernel`'s dynamic shared-memory limit to at least `bytes` on the
+// calling thread's current device. The attribute belongs to the device that is
+// current when it is set, so a process driving several GPUs needs it once per
+// device: it is set on the first request per (device, kernel) and again only
+// for a larger request. Safe to call from several host threads.
+void ensure_smem_limit(const void* kernel, int bytes, const char* what);
+
 // Kernel launchers (each returns after enqueueing on ctx->stream).
 void launch_silu_inplace(mbx_ctx* ctx, float* x, int64_t len);
 void launch_add(mbx_ctx* ctx, const float* a, const float* b, float* out, int64_t len);
@@ -122,6 +129,9 @@ struct ConvShape {
     int64_t ho, wo;
     int stride, pad_t, pad_l, up;
 };
+// One thread waits, with the given limit in clock cycles, on a barrier nothing arrives at
+// (the bounded-wait self-test behind mbx_selftest_wait_timeout).
+void launch_wait_probe(mbx_ctx* ctx, int64_t cycles);
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
                     float* out, int act = 0);

@@ -165,8 +165,8 @@ def test_single_block_config(mbx, ctx, oracle):
 @pytest.mark.parametrize("hw,ci,co", [(64, 128, 128), (64, 256, 512), (64, 512, 256), (128, 128, 256)])
 @pytest.mark.parametrize("dtype", ["f32", "f16"])
 def test_conv_sweep_matches_oracle(mbx, ctx, oracle, k, hw, ci, co, dtype):
-    """BASELINE config 3 shapes (B = 1; the largest sizes are covered by the bench's
-    property checks): w ~N(0, 1/√fan_in), fused bias + residual epilogue."""
+    """BASELINE config 3 shapes at B = 1 (B = 8 at 256×256 below): w ~N(0, 1/√fan_in), fused
+    bias + residual epilogue."""
     rng = np.random.default_rng(hw + ci + co + k)
     x = rng.standard_normal((1, hw, hw, ci)).astype(np.float32)
     shape = (co, ci) if k == 1 else (co, 3, 3, ci)
@@ -184,14 +184,47 @@ def test_conv_sweep_matches_oracle(mbx, ctx, oracle, k, hw, ci, co, dtype):
     assert scaled_err(got, want) <= 2e-5
 
 
+@pytest.mark.parametrize("k,ci,co,dtype", [
+    (3, 512, 512, "f16"),  # the benchmark's roofline shape
+    (3, 512, 512, "f32"),
+    (3, 256, 256, "f16"),
+    (3, 128, 512, "f32"),
+    (1, 512, 512, "f16"),
+    (1, 256, 128, "f32"),
+])
+def test_conv_sweep_b8_256_matches_oracle(mbx, ctx, oracle, k, ci, co, dtype):
+    """BASELINE config 3 at its largest size, [8, 256, 256, c_in]: the 3×3 convs take the TMA
+    path that loads A as 128-pixel pieces of 256-pixel rows (a 4-D box, zero fill as the
+    padding), the 1×1 convs the 2-D A box; whole outputs against the oracle (its Winograd path
+    for the 3×3), fused bias + residual epilogue."""
+    rng = np.random.default_rng(8 * ci + co + k)
+    shape = (8, 256, 256, ci)
+    x = rng.standard_normal(shape, dtype=np.float32)
+    wshape = (co, ci) if k == 1 else (co, 3, 3, ci)
+    wt = rng.normal(0.0, 1.0 / np.sqrt(ci * k * k), wshape).astype(np.float32)
+    bias = rng.normal(0.0, 0.01, co).astype(np.float32)
+    res = rng.standard_normal((8, 256, 256, co), dtype=np.float32)
+    wref = wt if dtype == "f32" else wt.astype(np.float16).astype(np.float32)
+    p = mbx.Param(ctx, wt, dtype)
+    if k == 1:
+        got = mbx.conv1x1(up(ctx, x), p, up(ctx, bias), up(ctx, res)).numpy()
+        want = oracle.conv1x1(x, wref, bias, res)
+    else:
+        got = mbx.conv3x3(up(ctx, x), p, up(ctx, bias), residual=up(ctx, res)).numpy()
+        want = oracle.add(oracle.conv3x3(x, wref, bias), res)
+    p.close()
+    assert max_rel_err(got, want) <= (GATE_F32 if dtype == "f32" else GATE_F16)
+    assert scaled_err(got, want) <= 2e-5
+
+
 @pytest.mark.parametrize("shape,stride,pad,upx,co", [
     ((2, 64, 64, 320), 2, (1, 1, 1, 1), False, 320),     # UNet Downsample2D, level 0
     ((1, 128, 128, 128), 2, (0, 0, 1, 1), False, 128),   # VAE encoder Downsample2D
     ((2, 16, 16, 1280), 1, (1, 1, 1, 1), True, 1280),    # UNet Upsample2D, level 2
     ((1, 64, 64, 4), 1, (1, 1, 1, 1), False, 512),       # VAE decoder conv_in (4 channels)
     ((1, 64, 64, 128), 1, (1, 1, 1, 1), False, 3),       # VAE conv_out (3 channels)
-    # Upsampled inputs through the TMA boxes of each tile geometry: 128 / wo output rows per tile
-    # (wo 32, 64, 128) and 128-pixel pieces of a row (wo 256, 512).
+    # Upsampled inputs at each tile geometry: 128 / wo output rows per tile (wo 32, 64, 128) and
+    # 128-pixel pieces of a row (wo 256, 512). Upsampled convs gather A with cp.async (no TMA box).
     ((2, 16, 16, 64), 1, (1, 1, 1, 1), True, 96),
     ((1, 32, 32, 64), 1, (1, 1, 1, 1), True, 160),
     ((2, 64, 64, 96), 1, (1, 1, 1, 1), True, 64),
@@ -222,4 +255,25 @@ def test_conv_errors(mbx, ctx):
 
 def test_device_error_word_is_clear(mbx, ctx):
     """No bounded wait gave up during the tests above (mbx_ctx_synchronize reports MBX_ERR_TIMEOUT otherwise)."""
+    ctx.synchronize()
+
+
+def test_bounded_wait_gives_up_and_the_context_recovers(mbx, ctx, ref_fixture):
+    """A device wait that runs out, in the form that faults nothing: one thread waits on a
+    barrier that nothing arrives at (no copy issued) with a limit of 2e7 cycles (about 10 ms).
+    mbx_ctx_synchronize reports MBX_ERR_TIMEOUT with the kernel and site, clears the record,
+    and the same context then runs a conv that matches the reference fixture."""
+    lib = mbx.abi.lib()
+    ctx.synchronize()
+    mbx.check(lib.mbx_selftest_wait_timeout(ctx.handle, 20_000_000))
+    assert lib.mbx_ctx_synchronize(ctx.handle) == mbx.abi.ERR_TIMEOUT
+    msg = lib.mbx_last_error()
+    assert b"timed out" in msg and b"kernel 4" in msg and b"site 12" in msg, msg
+    ctx.synchronize()  # the record was cleared
+    assert lib.mbx_selftest_wait_timeout(ctx.handle, 0) == mbx.abi.ERR_INVALID_ARGUMENT
+    f = ref_fixture
+    w = mbx.Param(ctx, f["c1.w"])
+    got = mbx.conv1x1(up(ctx, f["c1.x"]), w, up(ctx, f["c1.b"])).numpy()
+    w.close()
+    assert scaled_err(got, f["c1.y"]) <= REF_TOL
     ctx.synchronize()

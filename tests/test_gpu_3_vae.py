@@ -1,23 +1,28 @@
-"""GPU parity of the VAE pieces against the CPU oracle:
+"""GPU parity of the VAE against the CPU oracle:
 the tensor-core GEMM with a device B operand, the flushed row softmax, the
-mid-block attention (src/vae/mod.rs:240-293) and the whole decoder
+mid-block attention (src/vae/mod.rs:240-293), and the whole decoder
 (src/vae/decoder.rs:74-99) with seeded random-init weights, f32 (3×TF32) and
-f16 (2×TF32) weight storage. Gates: max relative error ≤ 1e-3 (f32) / 5e-3
-(f16) per kernel, and 8-bit output PSNR ≥ 45 dB for the decoder."""
+f16 (2×TF32) weight storage. The engine's decoder (eng_vae.cpp, the one the
+benchmark times) runs config 4 as stated: a 64×64 latent decoded to 512×512
+at batch 1 and 8. The kernel-composition tests build the attention and a
+small decoder in Python from the kernel ABI (tests/vae_compose.py). Gates:
+max relative error ≤ 1e-3 (f32) / 5e-3 (f16) per kernel, 8-bit output PSNR ≥
+45 dB for the decoder."""
 import ctypes
-import importlib
+import os
 
 import numpy as np
 import pytest
 
-from conftest import max_rel_err, scaled_err
+from conftest import load_package, max_rel_err, scaled_err
 
 pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")
 def vae():
-    return importlib.import_module("moebius-cpu_b200.vae")
+    import vae_compose
+    return vae_compose
 
 
 @pytest.fixture(scope="module")
@@ -80,8 +85,8 @@ def test_mid_attention(mbx, ctx, oracle, vae, vae_ref, wdtype):
 
 
 @pytest.mark.parametrize("wdtype", ["f32", "f16"])
-def test_decoder_matches_oracle(mbx, ctx, vae, vae_ref, wdtype):
-    """Full decoder on a 16×16 latent (128×128 image), batch 2."""
+def test_composed_decoder_matches_oracle(mbx, ctx, vae, vae_ref, wdtype):
+    """The decoder composed from the kernel ABI on a 16×16 latent (128×128 image), batch 2."""
     w = vae.random_decoder_weights(11, f16=(wdtype == "f16"))
     lat = (np.random.default_rng(13).standard_normal((2, 16, 16, 4)) * vae.SCALING_FACTOR).astype(np.float32)
     dec = vae.Decoder(ctx, w, wdtype)
@@ -101,3 +106,41 @@ def test_decoder_items_are_independent(mbx, ctx, vae):
     one = dec.decode(ctx.upload(lat[1:2])).numpy()
     dec.close()
     assert scaled_err(both[1:2], one) <= 1e-6
+
+
+@pytest.fixture(scope="module", params=["f16", "f32"])
+def vae_engine(request, tmp_path_factory, ctx):
+    """An engine with the full-size VAE (block_out 128/256/512/512) in the given weight
+    precision; its UNet is a scaled one (the decoder does not use it)."""
+    mbx = load_package()
+    syn = mbx.synthetic
+    d = str(tmp_path_factory.mktemp(f"vae_{request.param}"))
+    syn.write_weights_dir(d, seed=3, f16=request.param == "f16", unet_widths=(64, 128, 256), latent=16,
+                          vae_widths=syn.VAE_WIDTHS)
+    wv, _ = syn.read_safetensors(os.path.join(d, "vae.safetensors"))
+    eng = mbx.engine.Engine(d, 0)
+    eng.set_stream(ctx.stream)
+    yield eng, wv, request.param
+    eng.close()
+
+
+def test_engine_decoder_config4_matches_oracle(ctx, vae_engine, vae_ref):
+    """BASELINE config 4 through the engine decoder: latent [B, 64, 64, 4] ~ N(0, 1) → [B, 512, 512, 3].
+    f16 weights (the benchmark's) at B = 8 with N(0,1)-distributed unscaled latents (the
+    decoder's input after its 1/0.13025 scaling); f32 weights at B = 1 with N(0, 1) taken
+    as the scaled latent itself."""
+    eng, wv, wdtype = vae_engine
+    b = 8 if wdtype == "f16" else 1
+    rng = np.random.default_rng(41 + b)
+    lat = rng.standard_normal((b, 64, 64, 4)).astype(np.float32)
+    if wdtype == "f16":
+        lat *= np.float32(0.13025)
+    out = ctx.empty((b, 512, 512, 3))
+    latd = ctx.upload(lat)
+    eng.vae_decode(latd.ptr, b, 64, 64, out.ptr)
+    got = out.numpy()
+    want = vae_ref.decode(wv, lat)
+    assert got.shape == want.shape == (b, 512, 512, 3)
+    assert max_rel_err(got, want) <= (1e-3 if wdtype == "f32" else 5e-3)
+    for i in range(b):
+        assert psnr8(got[i], want[i]) >= 45.0, f"item {i}"

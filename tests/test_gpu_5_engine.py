@@ -5,7 +5,8 @@ presets, every paste mode, mask dilation and images of any size, with
 caller-supplied noise, on seeded random-init weights in the converter's
 format. Scaled-down networks of the same structure (widths 64/128/256,
 latent 16; VAE widths 32/64/128/128) keep the oracle fast; the full-size
-network runs one UNet step and a 2-step inpaint. Gates (BASELINE
+network runs one UNet step, a 2-step inpaint and the benchmark's batch of
+8 Exact inpaints (19 DDIM steps). Gates (BASELINE
 north_star): max relative error ≤ 1e-3 (f32 weights, 3xTF32) / 5e-3 (f16
 weights, 2xTF32) per network output, 8-bit PSNR ≥ 45 dB end to end."""
 import ctypes
@@ -36,12 +37,18 @@ def _weights(tmp_path_factory, name, unet=TINY_UNET, vae=TINY_VAE, f16=True, see
     return d, wu, wv
 
 
+# fixture name -> (weights directory, engine)
+_WEIGHT_DIRS = {}
+
+
 @pytest.fixture(scope="module", params=["f16", "f32"])
 def tiny(request, tmp_path_factory, mbx, ctx):
     d, wu, wv = _weights(tmp_path_factory, f"tiny_{request.param}", f16=request.param == "f16")
     eng = mbx.engine.Engine(d, 0)
     eng.set_stream(ctx.stream)
+    _WEIGHT_DIRS[f"tiny_{request.param}"] = (d, eng)
     yield eng, wu, wv, request.param
+    _WEIGHT_DIRS.pop(f"tiny_{request.param}", None)
     eng.close()
 
 
@@ -298,3 +305,71 @@ def test_full_size_inpaint_matches_oracle(mbx, full):
     eng.inpaint_batch(got, masks, mbx.engine.params(steps=3), noise=(nv, ni, no))
     want = pipeline_ref.inpaint(wu, wv, img[0], masks[0], nv, ni[0], no[0], steps=3)
     assert psnr8(got[0], want) >= 45.0
+
+
+def test_full_size_exact_batch_of_8_matches_oracle(mbx, full):
+    """The benchmark's configuration: 8 full-size 512² Exact inpaints in one batch (20 steps at
+    strength 0.99 = 19 DDIM steps, CFG 2.5, the UNet replayed from the graph captured at batch
+    16), f16 weights, random-ellipse masks covering 10-40 %. Items 0 and 5 against the oracle
+    pipeline with the same noise (src/pipeline.rs:217-373, src/preset.rs:59-72); the
+    device-buffer call the benchmark times gives the same bytes as the host-buffer call."""
+    from oracle import pipeline_ref, unet_ref
+    eng, wu, wv = full
+    syn = mbx.synthetic
+    rng = np.random.default_rng(1234)
+    n = 8
+    img = rng.integers(0, 256, (n, 512, 512, 3), dtype=np.uint8)
+    masks = syn.ellipse_masks(rng, n, 512)
+    nv = rng.standard_normal((2 * n, 64, 64, 4), dtype=np.float32)
+    ni = rng.standard_normal((n, 64, 64, 4), dtype=np.float32)
+    no = rng.standard_normal((n, 4), dtype=np.float32)
+    got = img.copy()
+    eng.inpaint_batch(got, masks, noise=(nv, ni, no))
+    # The device-buffer path (what the benchmark's `value` times).
+    ctx = mbx.Context(0)
+    try:
+        dpx, dm = ctx.upload(img, np.uint8), ctx.upload(masks, np.uint8)
+        dnv, dni, dno = ctx.upload(nv), ctx.upload(ni), ctx.upload(no)
+        ctx.synchronize()
+        eng.inpaint_batch_device(dpx.ptr, dm.ptr, n, 512, 3, mbx.engine.params(), (dnv.ptr, dni.ptr, dno.ptr))
+        got_dev = dpx.numpy()
+    finally:
+        ctx.close()
+    assert np.array_equal(got_dev, got), "device-buffer and host-buffer calls agree"
+    ehs = unet_ref.conditioning(wu)
+    for i in (0, 5):
+        want = pipeline_ref.inpaint(wu, wv, img[i], masks[i], nv[2 * i:2 * i + 2], ni[i], no[i], ehs=ehs)
+        assert psnr8(got[i], want) >= 45.0, f"item {i}"
+        assert not np.array_equal(got[i], img[i])
+
+
+def test_moebius_cpu_dropin_runs_the_engine(mbx, tiny):
+    """The reference-named C API (include/moebius_cpu.h) on a real weights directory: an inpaint
+    through moebius_inpaint gives the same bytes and rectangle as mbx_inpaint with the same seed."""
+    import ctypes
+    eng = tiny[0]
+    d = _WEIGHT_DIRS[f"tiny_{tiny[3]}"][0]
+    lib = mbx.abi.lib()
+    h = ctypes.c_void_p()
+    mbx.check(lib.moebius_engine_create(d.encode(), 7, ctypes.byref(h)))
+    try:
+        rng = np.random.default_rng(24)
+        img, masks, *_ = _inputs(rng, 1, 128, ch=4)
+        p = mbx.engine.params(steps=3, seed=11)
+        want = img[0].copy()
+        rect_want = eng.inpaint(want, masks[0], p)
+        got = img[0].copy()
+        rect = mbx.abi.Rect()
+        st = lib.moebius_inpaint(h, got.ctypes.data_as(ctypes.c_void_p), 128, 128, 128 * 4, 4,
+                                 masks[0].ctypes.data_as(ctypes.c_void_p), 128, ctypes.byref(p),
+                                 mbx.abi.PROGRESS_FN(), None, ctypes.byref(rect))
+        assert st == 0, lib.moebius_last_error()
+        assert np.array_equal(got, want)
+        assert (rect.x, rect.y, rect.width, rect.height) == rect_want
+        # Reference status codes: a bad channel count is MOEBIUS_ERR_INVALID_ARGUMENT.
+        st = lib.moebius_inpaint(h, got.ctypes.data_as(ctypes.c_void_p), 128, 128, 128 * 4, 2,
+                                 masks[0].ctypes.data_as(ctypes.c_void_p), 128, None, mbx.abi.PROGRESS_FN(), None,
+                                 None)
+        assert st == 1
+    finally:
+        lib.moebius_engine_destroy(h)

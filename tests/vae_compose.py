@@ -1,7 +1,8 @@
-"""The moebius-cpu VAE decoder on the moebius-cuda kernels.
-
-A caller of the engine layer, kept here to run BASELINE config 4 (the full
-decoder) on the GPU. Structure and names follow the reference's
+"""TEST HELPER: the moebius-cpu VAE decoder composed in Python from the
+kernel ABI (include/moebius_cuda.h) entry points, to test how those kernels
+compose (GroupNorm prologues, the tensor-core GEMMs and the flushed softmax of
+the mid attention) independently of the engine's C++ decoder (eng_vae.cpp),
+which the engine tests check against the oracle. Structure and names follow the reference's
 src/vae/decoder.rs and src/vae/mod.rs (diffusers AutoencoderKL, SDXL-VAE:
 block_out (128, 256, 512, 512), 3 resnets per up level, one single-head
 attention in the mid block, GroupNorm(32) eps 1e-6):
@@ -22,9 +23,12 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import Context, DeviceTensor, Param
-from . import conv1x1, conv3x3, group_norm, group_norm_affine
-from .abi import check, lib
+from conftest import load_package
+
+_mbx = load_package()
+Context, DeviceTensor, Param = _mbx.Context, _mbx.DeviceTensor, _mbx.Param
+conv1x1, conv3x3, group_norm, group_norm_affine = _mbx.conv1x1, _mbx.conv3x3, _mbx.group_norm, _mbx.group_norm_affine
+check, lib = _mbx.abi.check, _mbx.abi.lib
 
 VAE_BLOCK_OUT = (128, 256, 512, 512)
 LATENT_CHANNELS = 4
