@@ -58,6 +58,7 @@ INPAINT_TFLOP = 16.76
 SWEEP_SHAPE = (8, 512, 512, 512)
 BYTES_PER_ELT = {"group_norm_silu": 8, "bias_temb_add": 8, "residual_add": 12, "depthwise3x3": 8}
 CONV_SHAPE = (8, 256, 256, 512, 512, 9)  # n, h, w, c_in, c_out, taps: the conv sweep's largest 3×3 case
+SWEEP_OVERRIDE = None  # --sweep-shape: another memory-sweep shape (profiling cases)
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -294,9 +295,10 @@ def bench_conv(mbx, ctx, torch, dev, small):
     return out
 
 
-def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm):
-    """BASELINE configs[1] at its largest shape: the four memory-bound ops, algorithmic GB/s."""
-    shape = (1, 256, 256, 512) if small else SWEEP_SHAPE
+def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm, shape=None):
+    """BASELINE configs[1] at its largest shape (or `shape`): the four memory-bound ops, algorithmic
+    GB/s at the reference's byte rule (input + output bytes, examples/kernel_bench.rs:93,106)."""
+    shape = shape or ((1, 256, 256, 512) if small else SWEEP_SHAPE)
     n, h, w, c = shape
     gen = torch.Generator(device=dev).manual_seed(1234)
     x = torch.randn(shape, device=dev, generator=gen)
@@ -330,11 +332,61 @@ def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm):
     elems = int(np.prod(shape))
     op_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in ev.items()}
     total_ms = sum(op_ms.values())
-    return {"workload": f"BASELINE configs[1], largest shape {list(shape)} (inputs larger than L2)",
+    return {"workload": f"BASELINE configs[1], shape {list(shape)} (inputs larger than L2)",
             "gbs": round(sum(BYTES_PER_ELT.values()) * elems / (total_ms / 1e3) / 1e9, 1),
             "ops_ms": {k: round(v, 4) for k, v in op_ms.items()},
             "ops_frac_of_hbm": {k: round(BYTES_PER_ELT[k] * elems / (v / 1e3) / 1e9 / hbm, 4)
                                 for k, v in op_ms.items()}}
+
+
+def bench_unet_memory_kernels(mbx, ctx, torch, dev, hbm, batch=16):
+    """The UNet's own memory-bound shapes at the headline batch (8 inpaints × the CFG pair), bytes
+    counted as the reference counts them (input + output): the level-0 MixFFN depthwise with the
+    GLU·SiLU epilogue [16,64,64,1600] → 800 channels (4 B per input + 4 B per output element), the
+    level-0 LayerNorm over 16·4096 tokens of 320 channels (8 B/elt), and the DWConv2d depthwise with
+    its GroupNorm + SiLU prologue and ReLU [16,64,64,320] (8 B/elt)."""
+    gen = torch.Generator(device=dev).manual_seed(99)
+    W = lambda t: mbx.DeviceTensor.wrap(ctx, t.data_ptr(), tuple(t.shape))  # noqa: E731
+    x = torch.randn(batch, 64, 64, 1600, device=dev, generator=gen)
+    glu_w = torch.randn(3, 3, 1600, device=dev, generator=gen) / 3
+    glu_b = 0.01 * torch.randn(1600, device=dev, generator=gen)
+    glu_y = torch.empty(batch, 64, 64, 800, device=dev)
+    t = torch.randn(batch * 4096, 320, device=dev, generator=gen)
+    ln_g = 1 + 0.02 * torch.randn(320, device=dev, generator=gen)
+    ln_b = 0.02 * torch.randn(320, device=dev, generator=gen)
+    ln_y = torch.empty_like(t)
+    r = torch.randn(batch, 64, 64, 320, device=dev, generator=gen)
+    r_w = torch.randn(3, 3, 320, device=dev, generator=gen) / 3
+    r_b = 0.01 * torch.randn(320, device=dev, generator=gen)
+    sc = 1 + 0.1 * torch.randn(batch, 320, device=dev, generator=gen)
+    sh = 0.1 * torch.randn(batch, 320, device=dev, generator=gen)
+    r_y = torch.empty_like(r)
+    X, GW, GB, GY = W(x), W(glu_w), W(glu_b), W(glu_y)
+    T, LG, LB, LY = W(t), W(ln_g), W(ln_b), W(ln_y)
+    R, RW, RB, SC, SH, RY = W(r), W(r_w), W(r_b), W(sc), W(sh), W(r_y)
+    ops = [("depthwise3x3_glu_silu", lambda: mbx.depthwise3x3(X, GW, GB, "glu_silu", out=GY),
+            (x.numel() + glu_y.numel()) * 4),
+           ("layer_norm", lambda: mbx.layer_norm(T, LG, LB, 1e-5, out=LY), 8 * t.numel()),
+           ("depthwise3x3_gn_prologue_relu",
+            lambda: mbx.depthwise3x3(R, RW, RB, "relu", out=RY, prologue=(SC, SH, True)), 8 * r.numel())]
+    for _ in range(3):
+        for _, f, _ in ops:
+            f()
+    torch.cuda.synchronize()
+    out = {"workload": f"UNet level-0 shapes at batch {batch} (inputs larger than L2)"}
+    for name, f, nbytes in ops:
+        evs = []
+        for _ in range(5):
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            f()
+            e_ev.record()
+            evs.append((s_ev, e_ev))
+        torch.cuda.synchronize()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+        out[name] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                     "frac_of_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm, 4)}
+    return out
 
 
 def bench_vae_decoder(eng, torch, dev, latent):
@@ -481,14 +533,15 @@ def run_ours(args):
         components["note"] = (f"ms per call at the step's batch: one UNet step at batch {2 * n} (eager, no graph), "
                               f"VAE encode of {2 * n} images, decode of {n}")
     hbm, peak_kind = peaks()
-    conv = sweep = vae_line = None
+    conv = sweep = vae_line = unet_mem = None
     if rank == 0:
         ctxm = mbx.Context(local)
         ctxm.set_stream(stream.cuda_stream)
         if not args.skip_conv:
             conv = bench_conv(mbx, ctxm, torch, dev, args.small)
         if not args.skip_sweep:
-            sweep = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm)
+            sweep = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm, SWEEP_OVERRIDE)
+            unet_mem = bench_unet_memory_kernels(mbx, ctxm, torch, dev, hbm)
         if not args.skip_vae:
             vae_line = bench_vae_decoder(eng, torch, dev, side // 8)
         ctxm.close()
@@ -512,7 +565,7 @@ def run_ours(args):
             "implied_tflops": round(value * INPAINT_TFLOP, 1),
             "roofline": roof, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
             "result_changed_pixel_frac": round(changed, 4), "components_ms": components,
-            "conv": conv, "memory_sweep": sweep, "vae_decoder": vae_line,
+            "conv": conv, "memory_sweep": sweep, "unet_memory_kernels": unet_mem, "vae_decoder": vae_line,
             "hbm_peak_gbs": hbm, "hbm_peak_kind": peak_kind,
         }
         # The CPU baseline is timed at N = 1 only: under torchrun the other ranks would be
@@ -586,7 +639,8 @@ def run_secondary_only(args, mbx, torch, dev, eng, stream, world, rank, dist):
         if not args.skip_conv:
             out["conv"] = bench_conv(mbx, ctxm, torch, dev, args.small)
         if not args.skip_sweep:
-            out["memory_sweep"] = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm)
+            out["memory_sweep"] = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm, SWEEP_OVERRIDE)
+            out["unet_memory_kernels"] = bench_unet_memory_kernels(mbx, ctxm, torch, dev, hbm)
         if not args.skip_vae:
             out["vae_decoder"] = bench_vae_decoder(eng, torch, dev, (128 if args.small else SIDE) // 8)
         ctxm.close()
@@ -666,10 +720,15 @@ def main():
                     help="time one pipeline component alone (profiling case)")
     ap.add_argument("--conv-shape", default=None,
                     help="n,h,w,c_in,c_out[,taps] of the conv measurement (taps 9: 3x3, 1: 1x1)")
+    ap.add_argument("--sweep-shape", default=None, help="n,h,w,c of the memory-sweep measurement")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a scaled-down network (64/128/256, 128x128 images) and small sweeps")
     args = ap.parse_args()
-    global CONV_SHAPE
+    global CONV_SHAPE, SWEEP_OVERRIDE
+    if args.sweep_shape:
+        SWEEP_OVERRIDE = tuple(int(v) for v in args.sweep_shape.split(","))
+        if len(SWEEP_OVERRIDE) != 4:
+            ap.error("--sweep-shape takes n,h,w,c")
     if args.conv_shape:
         vals = tuple(int(v) for v in args.conv_shape.split(","))
         if len(vals) not in (5, 6) or (len(vals) == 6 and vals[5] not in (1, 9)):
