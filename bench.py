@@ -339,6 +339,53 @@ def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm, shape=None):
                                 for k, v in op_ms.items()}}
 
 
+def bench_gn_fused(mbx, ctx, torch, dev, hbm, shape):
+    """GroupNorm(32) + SiLU when its statistics come from the producing conv's epilogue
+    (mbx_conv_group_norm_affine), on the memory sweep's shape: the producer is a 1×1 conv c → c (f16
+    weights). The GroupNorm's own cost is then the statistics' extra cost inside the conv (conv with
+    statistics, fold and finalize, minus the plain conv) plus the apply pass (8 B/elt)."""
+    n, h, w, c = shape
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    x = torch.randn(shape, device=dev, generator=gen)
+    y, z = torch.empty_like(x), torch.empty_like(x)
+    gamma = 1.0 + 0.02 * torch.randn(c, device=dev, generator=gen)
+    beta = 0.02 * torch.randn(c, device=dev, generator=gen)
+    W = lambda t: mbx.DeviceTensor.wrap(ctx, t.data_ptr(), tuple(t.shape))  # noqa: E731
+    X, Y, Z, G, B = W(x), W(y), W(z), W(gamma), W(beta)
+    wt = (torch.randn(c, c, generator=torch.Generator().manual_seed(5)) / c ** 0.5).numpy()
+    p = mbx.Param(ctx, wt, "f16")
+    state = {}
+
+    def stats():
+        _, state["sc"], state["sh"] = mbx.conv_group_norm_affine(X, p, 32, 1e-6, G, B, out=Y)
+
+    ops = [("conv_plain", lambda: mbx.conv1x1(X, p, out=Y)), ("conv_with_statistics", stats),
+           ("apply_silu", lambda: mbx.group_norm_apply(Y, state["sc"], state["sh"], silu=True, out=Z))]
+    for _ in range(3):
+        for _, f in ops:
+            f()
+    torch.cuda.synchronize()
+    ev = {name: [] for name, _ in ops}
+    for _ in range(5):
+        for name, f in ops:
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            f()
+            e_ev.record()
+            ev[name].append((s_ev, e_ev))
+    torch.cuda.synchronize()
+    p.close()
+    ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in ev.items()}
+    elems = x.numel()
+    gn_ms = max(ms["conv_with_statistics"] - ms["conv_plain"], 0.0) + ms["apply_silu"]
+    return {"workload": f"{list(shape)}: 1x1 conv {c}->{c} (f16 weights) producing the GroupNorm input",
+            "ms": {k: round(v, 4) for k, v in ms.items()},
+            "statistics_extra_ms": round(ms["conv_with_statistics"] - ms["conv_plain"], 4),
+            "group_norm_silu_ms": round(gn_ms, 4),
+            "group_norm_silu_frac_of_hbm": round(8 * elems / (gn_ms / 1e3) / 1e9 / hbm, 4),
+            "apply_frac_of_hbm": round(8 * elems / (ms["apply_silu"] / 1e3) / 1e9 / hbm, 4)}
+
+
 def bench_unet_memory_kernels(mbx, ctx, torch, dev, hbm, batch=16):
     """The UNet's own memory-bound shapes at the headline batch (8 inpaints × the CFG pair), bytes
     counted as the reference counts them (input + output): the level-0 MixFFN depthwise with the
@@ -533,7 +580,7 @@ def run_ours(args):
         components["note"] = (f"ms per call at the step's batch: one UNet step at batch {2 * n} (eager, no graph), "
                               f"VAE encode of {2 * n} images, decode of {n}")
     hbm, peak_kind = peaks()
-    conv = sweep = vae_line = unet_mem = None
+    conv = sweep = vae_line = unet_mem = gn_fused = None
     if rank == 0:
         ctxm = mbx.Context(local)
         ctxm.set_stream(stream.cuda_stream)
@@ -542,6 +589,7 @@ def run_ours(args):
         if not args.skip_sweep:
             sweep = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm, SWEEP_OVERRIDE)
             unet_mem = bench_unet_memory_kernels(mbx, ctxm, torch, dev, hbm)
+            gn_fused = bench_gn_fused(mbx, ctxm, torch, dev, hbm, (1, 256, 256, 512) if args.small else SWEEP_SHAPE)
         if not args.skip_vae:
             vae_line = bench_vae_decoder(eng, torch, dev, side // 8)
         ctxm.close()
@@ -565,7 +613,8 @@ def run_ours(args):
             "implied_tflops": round(value * INPAINT_TFLOP, 1),
             "roofline": roof, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
             "result_changed_pixel_frac": round(changed, 4), "components_ms": components,
-            "conv": conv, "memory_sweep": sweep, "unet_memory_kernels": unet_mem, "vae_decoder": vae_line,
+            "conv": conv, "memory_sweep": sweep, "group_norm_fused": gn_fused, "unet_memory_kernels": unet_mem,
+            "vae_decoder": vae_line,
             "hbm_peak_gbs": hbm, "hbm_peak_kind": peak_kind,
         }
         # The CPU baseline is timed at N = 1 only: under torchrun the other ranks would be
@@ -641,6 +690,7 @@ def run_secondary_only(args, mbx, torch, dev, eng, stream, world, rank, dist):
         if not args.skip_sweep:
             out["memory_sweep"] = bench_memory_sweep(mbx, ctxm, torch, dev, args.small, hbm, SWEEP_OVERRIDE)
             out["unet_memory_kernels"] = bench_unet_memory_kernels(mbx, ctxm, torch, dev, hbm)
+            out["group_norm_fused"] = bench_gn_fused(mbx, ctxm, torch, dev, hbm, SWEEP_OVERRIDE or SWEEP_SHAPE)
         if not args.skip_vae:
             out["vae_decoder"] = bench_vae_decoder(eng, torch, dev, (128 if args.small else SIDE) // 8)
         ctxm.close()

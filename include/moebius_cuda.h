@@ -222,6 +222,22 @@ int32_t mbx_conv3x3(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t 
                     const mbx_param *weight, const float *bias, int64_t stride, const int64_t pad[4],
                     int32_t upsample2x, const float *pro_scale, const float *pro_shift, int32_t pro_silu,
                     const float *residual, float *out);
+/* A 1x1 or 3x3 convolution (taps from the weight) whose epilogue also gathers the GroupNorm
+ * statistics of its output, ending with that output's GroupNorm affine: out as mbx_conv1x1_fused /
+ * mbx_conv3x3 give it, then scale_out / shift_out [n, c_out] as mbx_group_norm_affine(out, groups,
+ * eps, gamma, beta, add) gives them, without reading out again. The statistics are per-channel f32
+ * sums over 256-pixel chunks folded per group in f64, as in the separate pass. For a 1x1 weight,
+ * stride must be 1 and upsample2x 0 (pad is ignored and may be NULL). Output maps that are not a
+ * multiple of 256 pixels, or c_out not a multiple of 4, take the separate statistics pass.
+ * Reference: Conv1x1::forward / Conv3x3::forward (src/engine/conv.rs:38-102) followed by
+ * GroupNorm::affine (src/engine/norm.rs:57-129), as src/unet/blocks.rs:84-112 and
+ * src/vae/mod.rs:190-211 call them. */
+int32_t mbx_conv_group_norm_affine(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                                   const mbx_param *weight, const float *bias, int64_t stride, const int64_t pad[4],
+                                   int32_t upsample2x, const float *pro_scale, const float *pro_shift,
+                                   int32_t pro_silu, const float *residual, int32_t act, float *out, int64_t groups,
+                                   float eps, const float *gamma, const float *beta, const float *add,
+                                   float *scale_out, float *shift_out);
 
 /* c[m x n] (+)= A . B with arbitrary element strides (A: rows m, cols k;
  * B: rows k, cols n); c dense row-major. f32 FMA accumulation.

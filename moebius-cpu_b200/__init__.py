@@ -37,7 +37,8 @@ from .abi import MbxError, check, lib
 
 __all__ = ["Context", "DeviceTensor", "Param", "MbxError", "abi", "group_norm", "group_norm_affine",
            "group_norm_apply", "layer_norm", "depthwise3x3", "conv1x1", "conv3x3", "conv3x3_output_hw",
-           "silu_inplace", "add_inplace", "concat_channels", "bias_temb_add", "matmul", "EPILOGUES"]
+           "silu_inplace", "add_inplace", "concat_channels", "bias_temb_add", "matmul", "conv_group_norm_affine",
+           "EPILOGUES"]
 
 EPILOGUES = {"none": abi.EPILOGUE_NONE, "relu": abi.EPILOGUE_RELU, "glu_silu": abi.EPILOGUE_GLU_SILU}
 
@@ -315,6 +316,26 @@ def conv3x3(x: DeviceTensor, weight: Param, bias: Optional[DeviceTensor] = None,
     check(lib().mbx_conv3x3(x.ctx.handle, x.vp, n, h, w, c, weight.handle, _vp(bias), stride, p, int(upsample2x),
                             _vp(ps), _vp(pz), silu, _vp(residual), out.vp))
     return out
+
+
+def conv_group_norm_affine(x: DeviceTensor, weight: Param, groups: int, eps: float, gamma: DeviceTensor,
+                          beta: DeviceTensor, bias: Optional[DeviceTensor] = None, add: Optional[DeviceTensor] = None,
+                          stride: int = 1, pad=(1, 1, 1, 1), upsample2x: bool = False, prologue=None,
+                          residual: Optional[DeviceTensor] = None, act: int = abi.ACT_NONE,
+                          out: Optional[DeviceTensor] = None):
+    """A 1x1 or 3x3 conv (by the weight's taps) plus the GroupNorm affine of its output from statistics
+    gathered in the conv's epilogue (mbx_conv_group_norm_affine): returns (out, scale [n, c_out],
+    shift [n, c_out])."""
+    n, h, w, c = _nhwc(x)
+    ho, wo = conv3x3_output_hw(h, w, stride, pad, upsample2x) if weight.taps == 9 else (h, w)
+    out = out or x.ctx.empty((n, ho, wo, weight.c_out))
+    scale, shift = x.ctx.empty((n, weight.c_out)), x.ctx.empty((n, weight.c_out))
+    p = (ctypes.c_int64 * 4)(*pad)
+    ps, pz, silu = (None, None, 0) if prologue is None else (prologue[0], prologue[1], int(prologue[2]))
+    check(lib().mbx_conv_group_norm_affine(x.ctx.handle, x.vp, n, h, w, c, weight.handle, _vp(bias), stride, p,
+                                           int(upsample2x), _vp(ps), _vp(pz), silu, _vp(residual), int(act), out.vp,
+                                           groups, eps, gamma.vp, beta.vp, _vp(add), scale.vp, shift.vp))
+    return out, scale, shift
 
 
 def matmul(a: DeviceTensor, b: DeviceTensor, c: Optional[DeviceTensor] = None,

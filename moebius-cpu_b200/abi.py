@@ -111,6 +111,8 @@ SIGNATURES = {
     "mbx_conv3x3_output_hw": (_i32, [_i64, _i64, _i64, _pi64, _i32, _pi64, _pi64]),
     "mbx_conv3x3": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _pi64, _i32, _vp, _vp, _i32, _vp,
                            _vp]),
+    "mbx_conv_group_norm_affine": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _pi64, _i32, _vp, _vp,
+                                          _i32, _vp, _i32, _vp, _i64, _f32, _vp, _vp, _vp, _vp, _vp]),
     "mbx_matmul": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32]),
     "mbx_softmax_rows": (_i32, [_vp, _vp, _i64, _i64, _f32, _f32]),
     "mbx_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _vp]),

@@ -79,6 +79,7 @@ public:
     const mbx_param* get() const { return p_; }
     int64_t c_out() const { return p_ ? p_->c_out : 0; }
     int64_t c_in() const { return p_ ? p_->c_in : 0; }
+    int64_t taps() const { return p_ ? p_->taps : 0; }
 
 private:
     mbx_ctx* ctx_ = nullptr;
@@ -155,6 +156,17 @@ Tensor conv3x3(const Tensor& x, const Conv& cv, const float* pro_scale = nullptr
                bool pro_silu = false, const float* residual = nullptr);
 // GroupNorm affine (per-item scale/shift [n, c]); `add` [n, c] or null.
 void gn_affine(const Tensor& x, const GroupNormP& g, const float* add, Tensor& scale, Tensor& shift);
+
+// The GroupNorm that will consume a conv's output: the conv gathers its statistics in its epilogue
+// (mbx_conv_group_norm_affine) and fills scale / shift, so the output is not read again for them.
+struct NextNorm {
+    const GroupNormP* g = nullptr;
+    const float* add = nullptr;  // [n, c] or null (the resnets' time embedding)
+    Tensor* scale = nullptr;
+    Tensor* shift = nullptr;
+};
+Tensor conv_gn(const Tensor& x, const Conv& cv, const NextNorm& next, const float* residual = nullptr,
+               const float* pro_scale = nullptr, const float* pro_shift = nullptr, bool pro_silu = false);
 
 uint16_t f32_to_f16(float v);
 float f16_to_f32(uint16_t h);

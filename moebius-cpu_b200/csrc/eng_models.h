@@ -34,7 +34,9 @@ struct DwConv2d {
     static DwConv2d load(const Loader& l, int64_t c_in, int64_t c_out);
     // gn_scale / gn_shift [n, c_in]: the block's input is SiLU(x*gn_scale + gn_shift), applied on
     // the fly (a GroupNorm + SiLU in front of the block).
-    Tensor forward(const Tensor& x, const float* gn_scale = nullptr, const float* gn_shift = nullptr) const;
+    // next: the GroupNorm that consumes the output; its affine comes from the pointwise conv's epilogue.
+    Tensor forward(const Tensor& x, const float* gn_scale = nullptr, const float* gn_shift = nullptr,
+                   const NextNorm* next = nullptr) const;
 };
 
 struct DwResnet {

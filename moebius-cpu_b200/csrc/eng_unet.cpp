@@ -106,14 +106,15 @@ DwConv2d DwConv2d::load(const Loader& l, int64_t c_in, int64_t c_out) {
 // or a = SiLU(x*gn_scale + gn_shift). Without the skip, a is built inside the depthwise kernel's window
 // and never stored; with it, a is stored once for the 1×1 conv's residual read (rebuilding it in the
 // conv's epilogue cost that kernel more than the saved pass).
-Tensor DwConv2d::forward(const Tensor& x, const float* gn_scale, const float* gn_shift) const {
+Tensor DwConv2d::forward(const Tensor& x, const float* gn_scale, const float* gn_shift, const NextNorm* next) const {
     const bool skip = c_in == c_out;
     if (gn_scale && skip) {
         Tensor a(x.ctx(), x.n, x.h, x.w, x.c);
         ck(mbx_group_norm_apply(x.ctx(), x.data(), x.n, x.h * x.w, x.c, gn_scale, gn_shift, 1, nullptr, a.data()));
-        return forward(a);
+        return forward(a, nullptr, nullptr, next);
     }
     Tensor mid = depthwise(x, dw_w, dw_b, MBX_EPILOGUE_RELU, gn_scale, gn_shift);
+    if (next) return conv_gn(mid, pw, *next, skip ? x.data() : nullptr);
     return conv1x1(mid, pw, skip ? x.data() : nullptr);
 }
 
@@ -138,9 +139,11 @@ Tensor DwResnet::forward(const Tensor& x, const float* temb_proj) const {
     // Each GroupNorm + SiLU is applied by the DWConv2d that follows it (statistics pass here).
     Tensor scale, shift;
     gn_affine(x, norm1, nullptr, scale, shift);
-    Tensor b = conv1.forward(x, scale.data(), shift.data());
-    gn_affine(b, norm2, temb_proj, scale, shift);
-    Tensor out = conv2.forward(b, scale.data(), shift.data());
+    // norm2's statistics (of b + temb) come from conv1's pointwise epilogue.
+    Tensor scale2, shift2;
+    const NextNorm next{&norm2, temb_proj, &scale2, &shift2};
+    Tensor b = conv1.forward(x, scale.data(), shift.data(), &next);
+    Tensor out = conv2.forward(b, scale2.data(), shift2.data());
     b = Tensor();
     scale = Tensor();
     shift = Tensor();

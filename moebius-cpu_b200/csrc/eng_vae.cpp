@@ -45,8 +45,11 @@ Tensor norm_silu(const Tensor& x, const GroupNormP& g) {
 
 // h = conv1(SiLU(GN1(x))); h = conv2(SiLU(GN2(h))); h + (shortcut(x) | x)  (src/vae/mod.rs:190-211).
 Tensor VaeResnet::forward(const Tensor& x) const {
-    Tensor h = conv3x3(norm_silu(x, norm1), conv1);
-    Tensor a = norm_silu(h, norm2);
+    // norm2's statistics come from conv1's epilogue; only its apply pass reads h.
+    Tensor s2, t2;
+    Tensor h = conv_gn(norm_silu(x, norm1), conv1, NextNorm{&norm2, nullptr, &s2, &t2});
+    Tensor a(h.ctx(), h.n, h.h, h.w, h.c);
+    ck(mbx_group_norm_apply(h.ctx(), h.data(), h.n, h.h * h.w, h.c, s2.data(), t2.data(), 1, nullptr, a.data()));
     h = Tensor();
     if (!has_shortcut) return conv3x3(a, conv2, nullptr, nullptr, false, x.data());
     Tensor o = conv3x3(a, conv2);

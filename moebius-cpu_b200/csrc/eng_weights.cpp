@@ -425,6 +425,20 @@ Tensor conv3x3(const Tensor& x, const Conv& cv, const float* pro_scale, const fl
     return out;
 }
 
+Tensor conv_gn(const Tensor& x, const Conv& cv, const NextNorm& next, const float* residual, const float* pro_scale,
+               const float* pro_shift, bool pro_silu) {
+    int64_t ho = x.h, wo = x.w;
+    if (cv.w.taps() == 9) ck(mbx_conv3x3_output_hw(x.h, x.w, cv.stride, cv.pad, cv.up ? 1 : 0, &ho, &wo));
+    Tensor out(x.ctx(), x.n, ho, wo, cv.c_out);
+    *next.scale = Tensor(x.ctx(), x.n, 1, 1, cv.c_out);
+    *next.shift = Tensor(x.ctx(), x.n, 1, 1, cv.c_out);
+    ck(mbx_conv_group_norm_affine(x.ctx(), x.data(), x.n, x.h, x.w, x.c, cv.w.get(), cv.b.f(), cv.stride, cv.pad,
+                                  cv.up ? 1 : 0, pro_scale, pro_shift, pro_silu ? 1 : 0, residual, MBX_ACT_NONE,
+                                  out.data(), next.g->groups, next.g->eps, next.g->gamma.f(), next.g->beta.f(),
+                                  next.add, next.scale->data(), next.shift->data()));
+    return out;
+}
+
 void gn_affine(const Tensor& x, const GroupNormP& g, const float* add, Tensor& scale, Tensor& shift) {
     scale = Tensor(x.ctx(), x.n, 1, 1, x.c);
     shift = Tensor(x.ctx(), x.n, 1, 1, x.c);

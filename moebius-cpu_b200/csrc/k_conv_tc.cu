@@ -104,6 +104,11 @@ struct ConvArgs {
     const float* pro_shift;
     int pro_silu;
     int act;  // epilogue activation after bias and residual: 0 none, 1 SiLU
+    // GroupNorm statistics of the output (null = off): per M tile and drain warp, the f32 sums of
+    // y and y² over the warp's 32 rows per channel, y = out + gn_add[item] ([n][c_out] or null);
+    // layout [m_tiles][4][2][c_out].
+    float* gn_part;
+    const float* gn_add;
     int* err;
 };
 
@@ -362,7 +367,8 @@ __global__ void __maxnreg__(128)
     volatile int* s_wfills = reinterpret_cast<volatile int*>(gbase + (misc + 8 - base));
     // Fill counts for the abort path: arrivals this converter thread made on the stage full
     // barriers, weight tiles and A boxes the TMA issuers armed (a CTA's chunk count stays below
-    // 2^31, checked at launch).
+    // 2^31, checked at launch). Each role derives its count from its loop position when it leaves
+    // the loop, so no counter stays live in the hot loops.
     int conv_fills = 0, w_fills = 0, a_fills = 0;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -379,6 +385,9 @@ __global__ void __maxnreg__(128)
     // in flight share A rows through L2). Every ring keeps its position and phase across tiles,
     // so the next tile's loads and MMAs overlap this tile's epilogue.
     const int64_t tiles = args.tiles;
+    // Fill counts of a role that walked all of this CTA's tiles, or stopped at chunk kc of tile t.
+    auto all_fills = [&]() { return (int)((tiles - blockIdx.x + gridDim.x - 1) / gridDim.x) * K; };
+    auto fills_at = [&](int64_t t, int kc) { return (int)((t - blockIdx.x) / gridDim.x) * K + kc; };
     auto tile_m0 = [&](int64_t t) { return (t / args.n_tiles) * (int64_t)BM; };
     auto tile_n0 = [&](int64_t t) { return (int)(t % args.n_tiles) * bn; };
     // TMEM columns: accumulators [0, 2·bn), A stage a at 2·bn + 64·a (32 columns of TF32
@@ -530,6 +539,7 @@ __global__ void __maxnreg__(128)
                 if (!mbar_wait(sfull_bar(q), (uint32_t)qphase, args.err, 9, abort_flag, true) ||
                     !mbar_wait(a_empty_bar(a), (uint32_t)(aphase ^ 1), args.err, 1, abort_flag, true)) {
                     live = false;
+                    conv_fills = fills_at(t, kc);
                     break;
                 }
                 const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
@@ -585,7 +595,6 @@ __global__ void __maxnreg__(128)
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(a_full_bar(a));
-                ++conv_fills;
                 if (++q == nstg) {
                     q = 0;
                     qphase ^= 1;
@@ -600,6 +609,7 @@ __global__ void __maxnreg__(128)
                 }
             }
         }
+        if (live) conv_fills = all_fills();
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
@@ -701,6 +711,7 @@ __global__ void __maxnreg__(128)
                 for (int kc = 0; kc < K; ++kc) {
                     if (!mbar_wait(sempty_bar(q), (uint32_t)(qphase ^ 1), args.err, 8, abort_flag, true)) {
                         live = false;
+                        a_fills = fills_at(t, kc);
                         break;
                     }
                     const uint32_t stg = stg_base + (uint32_t)q * A_BYTES;
@@ -712,7 +723,6 @@ __global__ void __maxnreg__(128)
                         tma_load_4d(stg, &tmap_a, cchunk * BK, x0 + kx - args.pad_l, y0 + ky - args.pad_t, item,
                                     sfull_bar(q));
                     }
-                    ++a_fills;
                     if (++q == nstg) {
                         q = 0;
                         qphase ^= 1;
@@ -723,6 +733,7 @@ __global__ void __maxnreg__(128)
                     }
                 }
             }
+            if (live) a_fills = all_fills();
         }
         if (lane == 0) {
             int s = 0, sphase = 0;
@@ -732,19 +743,20 @@ __global__ void __maxnreg__(128)
                 for (int kc = 0; kc < K; ++kc) {
                     if (!mbar_wait(b_empty_bar(s), (uint32_t)(sphase ^ 1), args.err, 4, abort_flag, true)) {
                         live = false;
+                        w_fills = fills_at(t, kc);
                         break;
                     }
                     const uint32_t b_hi = base + (uint32_t)s * bstage_bytes;
                     mbar_arrive_expect_tx(b_full_bar(s), bstage_bytes);
                     tma_load_2d(b_hi, &tmap_hi, kc * BK, n0, b_full_bar(s));
                     if constexpr (F32W) tma_load_2d(b_hi + b_bytes, &tmap_lo, kc * BK, n0, b_full_bar(s));
-                    ++w_fills;
                     if (++s == bstages) {
                         s = 0;
                         sphase ^= 1;
                     }
                 }
             }
+            if (live) w_fills = all_fills();
             *s_wfills = w_fills;
         }
         __syncwarp();
@@ -755,6 +767,9 @@ __global__ void __maxnreg__(128)
         const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
         const uint32_t srow = sum_base + (uint32_t)row * sum_stride;
         const bool vec_out = (args.c_out & 3) == 0;
+        // Transposed (coalesced) stores for float4 outputs; a SiLU epilogue keeps one row per thread
+        // (inside the UNet its transposed form ran 22 % slower) unless statistics are gathered.
+        const bool transpose = vec_out && (!args.act || args.gn_part);
         int gseg = 0;
         bool live = true;
         for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
@@ -781,16 +796,95 @@ __global__ void __maxnreg__(128)
                             acc[4 * v + 3] = r4.w + acc[4 * v + 3];
                         }
                     }
-                    if (!last) {
+                    if (!last || transpose) {
 #pragma unroll
                         for (int v = 0; v < 8; ++v)
                             st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1],
                                          acc[4 * v + 2], acc[4 * v + 3]);
+                        if (!last) continue;
+                        // Transposed stores: the warp's 32 × 32 block goes through this row's slot
+                        // of the (segment) sum buffer, so each store instruction writes four
+                        // whole 128-byte row pieces instead of 32 scattered 16-byte ones. Lane l
+                        // takes the float4 column group l % 8 of rows 4i + l / 8. The row stride
+                        // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
+                        __syncwarp();
+                        const int nb = n0 + cc;
+                        if (nb < args.c_out) {
+                            const int j = lane & 7;
+                            const int col = nb + 4 * j;
+                            const bool col_ok = col < args.c_out;  // c_out % 4 == 0: the whole float4
+                            const float4 b4 = args.bias && col_ok
+                                                  ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                            const int64_t m_base = tile_m0(t) + qd * 32;
+                            // GroupNorm statistics: the tile's rows all belong to one item.
+                            float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs, gad = gs;
+                            if (args.gn_add && col_ok)
+                                gad = __ldg(reinterpret_cast<const float4*>(args.gn_add +
+                                                                            (tile_m0(t) / hw_out) * args.c_out + col));
+                            // All eight shared loads, then all eight residual loads, then the stores: a
+                            // residual load placed after a store would wait out its whole latency.
+                            float4 a4[8], r4[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
+                                                     (uint32_t)(cc + 4 * j) * 4u);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int64_t mr = m_base + 4 * i + (lane >> 3);
+                                r4[i] = args.residual && col_ok && mr < args.m_total
+                                            ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int64_t mr = m_base + 4 * i + (lane >> 3);
+                                if (mr >= args.m_total || !col_ok) continue;
+                                float4 pre = b4;
+                                if (args.residual)
+                                    pre = make_float4(r4[i].x + pre.x, r4[i].y + pre.y, r4[i].z + pre.z, r4[i].w + pre.w);
+                                const float4 a = a4[i];
+                                float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
+                                if (args.act)
+                                    o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                                *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
+                                if (args.gn_part) {
+                                    const float4 y = make_float4(o4.x + gad.x, o4.y + gad.y, o4.z + gad.z, o4.w + gad.w);
+                                    gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
+                                    gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
+                                                     fmaf(y.w, y.w, gq.w));
+                                }
+                            }
+                            if (args.gn_part) {
+                                // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
+                                // order, so results do not depend on timing), then lanes 0-7 write the
+                                // warp's sums for their four channels.
+#pragma unroll
+                                for (int o = 8; o <= 16; o <<= 1) {
+                                    gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
+                                    gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
+                                    gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
+                                    gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
+                                    gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
+                                    gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
+                                    gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
+                                    gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
+                                }
+                                if (lane < 8 && col_ok) {
+                                    float* dst = args.gn_part + ((tile_m0(t) / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
+                                    *reinterpret_cast<float4*>(dst) = gs;
+                                    *reinterpret_cast<float4*>(dst + args.c_out) = gq;
+                                }
+                            }
+                        }
+                        __syncwarp();  // the slots are read before any lane overwrites them
                         continue;
                     }
                     if (m >= args.m_total) continue;
                     const int nb = n0 + cc;
                     if (nb >= args.c_out) continue;
+                    // One row per thread: float4 stores (SiLU epilogues), or scalar stores for output
+                    // widths that are not a multiple of 4 (the VAE's 3-channel conv_out).
                     float* dst = args.out + m * args.c_out + nb;
                     const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
                     if (vec_out && nb + 32 <= args.c_out) {
@@ -935,6 +1029,12 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtenso
 
 }  // namespace
 
+bool conv_gn_fusable(const ConvShape& s, int64_t c_out) { return c_out % 4 == 0 && (s.ho * s.wo) % 256 == 0; }
+
+int64_t conv_gn_part_floats(const ConvShape& s, int64_t c_out) {
+    return (s.n * s.ho * s.wo + BM - 1) / BM * 4 * 2 * c_out;
+}
+
 void launch_wait_probe(mbx_ctx* ctx, int64_t cycles) {
     wait_probe_kernel<<<1, 1, 0, ctx->stream>>>(ctx->dev_err, (long long)cycles);
     after_launch(ctx, "wait probe");
@@ -985,7 +1085,7 @@ void encode_param_tmaps(mbx_param* p) {
 
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
-                    float* out, int act) {
+                    float* out, int act, float* gn_part, const float* gn_add) {
     ConvArgs a{};
     a.x = x;
     a.m_total = s.n * s.ho * s.wo;
@@ -1022,6 +1122,10 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.pro_shift = pro_shift;
     a.pro_silu = pro_silu ? 1 : 0;
     a.act = act;
+    a.gn_part = gn_part;
+    a.gn_add = gn_add;
+    MBX_REQUIRE(!gn_part || conv_gn_fusable(s, p->c_out),
+                "conv: GroupNorm statistics in the epilogue need c_out % 4 == 0 and output maps of 256k pixels");
     a.err = ctx->dev_err;
     MBX_REQUIRE(a.m_total < (int64_t(1) << 40), "conv: too many output pixels");
     const int64_t m_tiles = (a.m_total + BM - 1) / BM;

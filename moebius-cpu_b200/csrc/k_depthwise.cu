@@ -11,6 +11,8 @@
 // and DRAM traffic is about one read of the input (+3% y-halo) plus one write. Taps are accumulated bias-first in
 // (ky, kx) order with fma(tap, x, acc) as in acc_block (:112-143); padding
 // taps contribute nothing.
+#include <algorithm>
+
 #include "mbx_device.cuh"
 #include "mbx_internal.h"
 
@@ -165,168 +167,229 @@ __global__ void __launch_bounds__(kDwThreads, 4) dw3x3_kernel(const float* __res
 
 
 // ---------------------------------------------------------------- TMA-tiled variant
-// A CTA owns a 16 × 16 output tile of 32 channels (both channel sets for GLU): one TMA box
-// {32, 18, 18, 1} per set brings the tile with its halo, read once from global memory (the box's
-// zero fill past the map is never used: padding taps are skipped as above). Each thread then
-// walks 8 output rows of one 4-channel vector at one x, sliding a 3-row window through shared
-// memory; its taps and bias sit in registers.
+// A tile is 16 × 16 output pixels of 32 channels (both channel sets for GLU): one TMA box
+// {32, 18, 18, 1} per set brings it with its halo, read once from global memory (the box's zero
+// fill past the map is never used: padding taps are skipped as above). Persistent CTAs walk tiles
+// tt = blockIdx.x, blockIdx.x + gridDim.x, ... (channel block fastest, then tile, then item)
+// through a two-stage ring: tile i + 1's boxes land while tile i is computed, so the memory pipe
+// stays busy (one CTA per SM with the GLU's two sets, two otherwise). Each thread walks 8 output
+// rows of one 4-channel vector at one x, sliding a 3-row window through shared memory; its taps
+// and bias sit in registers, reloaded when the tile's channel block changes.
 constexpr int kTT = 16;                                           // tile side (output pixels)
 constexpr int kTC = 32;                                           // channels per tile
 constexpr int kTH = kTT + 2;                                      // halo tile side
-constexpr int kTileThreads = 256;                                 // 8 vectors × 16 columns × 2 row groups
+constexpr int kTileThreads = 256;  // 8 vectors × 16 columns × 2 row groups (× 2 channel sets for GLU)
+template <int EPI>
+constexpr int tile_threads() { return EPI == MBX_EPILOGUE_GLU_SILU ? 2 * kTileThreads : kTileThreads; }
 constexpr uint32_t kSetBytes = (uint32_t)kTH * kTH * kTC * 4;    // 41472
+constexpr int kStages = 2;
 constexpr long long kDwWaitLimit = 4ll << 30;                     // clock cycles (about 2 s)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+__device__ __forceinline__ bool dw_landed(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+struct DwTiles {
+    int cblocks, tiles_x, tiles_xy;
+    int64_t total;
+    __device__ __forceinline__ void at(int64_t tt, int& cb, int& y0, int& x0, int& item) const {
+        cb = (int)(tt % cblocks);
+        const int64_t rest = tt / cblocks;
+        const int tile = (int)(rest % tiles_xy);
+        item = (int)(rest / tiles_xy);
+        const int ty = tile / tiles_x;
+        y0 = ty * kTT;
+        x0 = (tile - ty * tiles_x) * kTT;
+    }
+};
+
 // PRO: GroupNorm prologue, the input read as [SiLU](x*pro_scale[item,c] + pro_shift[item,c]).
 template <int EPI, bool PRO>
-__global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
+__global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
                                                                  int w, int c, const float* __restrict__ weight,
                                                                  const float* __restrict__ bias,
                                                                  const float* __restrict__ pro_scale,
                                                                  const float* __restrict__ pro_shift, int pro_silu,
-                                                                 float* __restrict__ out, int tiles_x, int* err) {
+                                                                 float* __restrict__ out, DwTiles tiles, int* err) {
     constexpr bool kGlu = EPI == MBX_EPILOGUE_GLU_SILU;
     constexpr int kSets = kGlu ? 2 : 1;
-    extern __shared__ __align__(1024) float tile[];  // [set][kTH][kTH][kTC]
-    __shared__ uint64_t bar;
+    constexpr uint32_t kStageBytes = (uint32_t)kSets * kSetBytes;
+    extern __shared__ __align__(1024) float ring[];  // [stage][set][kTH][kTH][kTC]
+    __shared__ __align__(8) uint64_t bars[kStages];
     const int c_out = kGlu ? c / 2 : c;
-    const int c0 = blockIdx.x * kTC;
-    const int ty = blockIdx.y / tiles_x, tx = blockIdx.y - (blockIdx.y / tiles_x) * tiles_x;
-    const int y0 = ty * kTT, x0 = tx * kTT, item = blockIdx.z;
-    const uint32_t b = smem_addr(&bar);
-    if (threadIdx.x == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(b),
-                     "r"((uint32_t)kSets * kSetBytes)
+    const uint32_t bar0 = smem_addr(&bars[0]);
+    auto bar = [&](int s) { return bar0 + 8u * (uint32_t)s; };
+    auto stage_ptr = [&](int s) { return ring + (size_t)s * (kStageBytes / 4); };
+    // Thread 0: arms stage s for tile tt and issues its boxes.
+    auto issue = [&](int s, int64_t tt) {
+        int cb, y0, x0, item;
+        tiles.at(tt, cb, y0, x0, item);
+        asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar(s)),
+                     "r"(kStageBytes)
                      : "memory");
 #pragma unroll
         for (int set = 0; set < kSets; ++set)
             asm volatile(
                 "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-                "%3, %4, %5}], [%6];" ::"r"(smem_addr(tile + set * kTH * kTH * kTC)),
-                "l"(reinterpret_cast<uint64_t>(&map)), "r"(c0 + set * c_out), "r"(x0 - 1), "r"(y0 - 1), "r"(item),
-                "r"(b)
+                "%3, %4, %5}], [%6];" ::"r"(smem_addr(stage_ptr(s) + set * kTH * kTH * kTC)),
+                "l"(reinterpret_cast<uint64_t>(&map)), "r"(cb * kTC + set * c_out), "r"(x0 - 1), "r"(y0 - 1),
+                "r"(item), "r"(bar(s))
                 : "memory");
-    }
-    // Bounded wait for the boxes; on timeout (any thread's) the error is recorded and the CTA
-    // writes nothing. The boxes may still be in flight then: thread 0 keeps waiting for them,
-    // bounded again, so the CTA (and its shared memory) does not retire under a pending copy.
-    {
-        auto landed = [&]() {
-            uint32_t ok;
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, "
-                "p;\n\t}"
-                : "=r"(ok)
-                : "r"(b)
-                : "memory");
-            return ok != 0;
-        };
-        const long long t0 = clock64();
-        int timed_out = 0;
-        while (!landed()) {
-            if (clock64() - t0 > kDwWaitLimit) {
-                timed_out = 1;
-                break;
-            }
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar(s)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < kStages; ++s) {
+            const int64_t tt = blockIdx.x + (int64_t)s * gridDim.x;
+            if (tt < tiles.total) issue(s, tt);
         }
-        if (__syncthreads_or(timed_out)) {
-            if (threadIdx.x == 0) {
-                if (atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
-                const long long t1 = clock64();
-                while (!landed() && clock64() - t1 <= kDwWaitLimit) {
+    }
+    __syncthreads();
+    // Thread mapping: channel quad j, column xl, row group rg (8 rows each). With GLU the two
+    // channel sets go to a lane pair (lane, lane ^ 16), so each thread holds one set's taps and
+    // window (fewer registers, twice the warps); the value lane takes the gate by shuffle.
+    constexpr int kThreads = tile_threads<EPI>();
+    const int lane = threadIdx.x & 31;
+    const int j = threadIdx.x & 7;
+    const int xl = kGlu ? 2 * ((threadIdx.x >> 5) & 7) + ((lane >> 3) & 1) : (threadIdx.x >> 3) & 15;
+    const int rg = kGlu ? threadIdx.x >> 8 : threadIdx.x >> 7;
+    const int my_set = kGlu ? lane >> 4 : 0;
+    Vec<4> wt[9], bs;
+    int cb_loaded = -1;
+    int it = 0;
+    for (int64_t tt = blockIdx.x; tt < tiles.total; tt += gridDim.x, ++it) {
+        const int s = it & 1;
+        const uint32_t parity = (uint32_t)((it >> 1) & 1);
+        // Bounded wait for the boxes; on timeout (any thread's) the error is recorded and the CTA
+        // writes nothing more. Thread 0 then keeps waiting, bounded again, for the boxes it issued
+        // (this tile's and the next one's), so the CTA does not retire under a pending copy.
+        {
+            const long long t0 = clock64();
+            int timed_out = 0;
+            while (!dw_landed(bar(s), parity)) {
+                if (clock64() - t0 > kDwWaitLimit) {
+                    timed_out = 1;
+                    break;
                 }
             }
-            return;
-        }
-    }
-    if constexpr (PRO) {
-        // GroupNorm prologue on the landed window, in place, at in-image pixels of real channels (the
-        // padding taps are skipped below and channels past c are never stored, so their zero fill
-        // stays). Same arithmetic as the GroupNorm apply kernel: fmaf(x, scale, shift), then SiLU.
-        const int q4 = threadIdx.x & 7;
-#pragma unroll
-        for (int set = 0; set < kSets; ++set) {
-            const int cc = c0 + set * c_out + 4 * q4;
-            if (cc >= c) continue;
-            const float4 sc = __ldg(reinterpret_cast<const float4*>(pro_scale + (int64_t)item * c + cc));
-            const float4 sh = __ldg(reinterpret_cast<const float4*>(pro_shift + (int64_t)item * c + cc));
-            float* base = tile + set * kTH * kTH * kTC + 4 * q4;
-            for (int px = threadIdx.x >> 3; px < kTH * kTH; px += kTileThreads / 8) {
-                const int row = px / kTH, col = px - row * kTH;
-                const int gy = y0 - 1 + row, gx = x0 - 1 + col;
-                if (gy < 0 || gy >= h || gx < 0 || gx >= w) continue;
-                float4* e = reinterpret_cast<float4*>(base + px * kTC);
-                float4 t = *e;
-                t = make_float4(fmaf(t.x, sc.x, sh.x), fmaf(t.y, sc.y, sh.y), fmaf(t.z, sc.z, sh.z),
-                                fmaf(t.w, sc.w, sh.w));
-                if (pro_silu) t = make_float4(dev_silu(t.x), dev_silu(t.y), dev_silu(t.z), dev_silu(t.w));
-                *e = t;
+            if (__syncthreads_or(timed_out)) {
+                if (threadIdx.x == 0) {
+                    if (atomicCAS(err, 0, kErrWaitTimeout) == 0) err[1] = kKDepthwise;
+                    const long long t1 = clock64();
+                    while (!dw_landed(bar(s), parity) && clock64() - t1 <= kDwWaitLimit) {
+                    }
+                    if (tt + gridDim.x < tiles.total) {
+                        const uint32_t p1 = (uint32_t)(((it + 1) >> 1) & 1);
+                        while (!dw_landed(bar(s ^ 1), p1) && clock64() - t1 <= 2 * kDwWaitLimit) {
+                        }
+                    }
+                }
+                return;
             }
         }
+        int cb, y0, x0, item;
+        tiles.at(tt, cb, y0, x0, item);
+        const int c0 = cb * kTC;
+        float* tile = stage_ptr(s);
+        if constexpr (PRO) {
+            // GroupNorm prologue on the landed window, in place, at in-image pixels of real channels
+            // (the padding taps are skipped below and channels past c are never stored, so their
+            // zero fill stays). Same arithmetic as the GroupNorm apply kernel: fmaf(x, scale, shift),
+            // then SiLU.
+            const int q4 = threadIdx.x & 7;
+#pragma unroll
+            for (int set = 0; set < kSets; ++set) {
+                const int cc = c0 + set * c_out + 4 * q4;
+                if (cc >= c) continue;
+                const float4 sc = __ldg(reinterpret_cast<const float4*>(pro_scale + (int64_t)item * c + cc));
+                const float4 sh = __ldg(reinterpret_cast<const float4*>(pro_shift + (int64_t)item * c + cc));
+                float* base = tile + set * kTH * kTH * kTC + 4 * q4;
+                for (int px = threadIdx.x >> 3; px < kTH * kTH; px += kThreads / 8) {
+                    const int row = px / kTH, col = px - row * kTH;
+                    const int gy = y0 - 1 + row, gx = x0 - 1 + col;
+                    if (gy < 0 || gy >= h || gx < 0 || gx >= w) continue;
+                    float4* e = reinterpret_cast<float4*>(base + px * kTC);
+                    float4 t = *e;
+                    t = make_float4(fmaf(t.x, sc.x, sh.x), fmaf(t.y, sc.y, sh.y), fmaf(t.z, sc.z, sh.z),
+                                    fmaf(t.w, sc.w, sh.w));
+                    if (pro_silu) t = make_float4(dev_silu(t.x), dev_silu(t.y), dev_silu(t.z), dev_silu(t.w));
+                    *e = t;
+                }
+            }
+            __syncthreads();
+        }
+        const int ch = c0 + 4 * j, ox = x0 + xl;
+        const bool valid = ch < c_out && ox < w;
+        // The taps of this thread's channel quad (its set) stay in registers while the channel
+        // block stays the same; quads past c_out get zeros (their results are never stored).
+        if (cb != cb_loaded) {
+            const bool real = ch < c_out;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) wt[k] = real ? vload<4>(weight + k * c + my_set * c_out + ch) : vzero<4>();
+            bs = real ? vload<4>(bias + my_set * c_out + ch) : vzero<4>();
+            cb_loaded = cb;
+        }
+        if (valid || kGlu) {  // GLU lanes compute unconditionally: the gate shuffle needs the whole warp
+            const bool left = ox > 0, right = ox + 1 < w;
+            const float* set_tile = tile + my_set * kTH * kTH * kTC;
+            auto at = [&](int row, int col) -> Vec<4> {
+                const float4 f = *reinterpret_cast<const float4*>(set_tile + ((row * kTH + col) * kTC + 4 * j));
+                Vec<4> r;
+                r.v[0] = f.x;
+                r.v[1] = f.y;
+                r.v[2] = f.z;
+                r.v[3] = f.w;
+                return r;
+            };
+            const int r_begin = rg * (kTT / 2), r_end = min(r_begin + kTT / 2, h - y0);
+            Vec<4> win[3][3];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+                for (int k = 0; k < 3; ++k) win[rr][k] = at(r_begin + rr, xl + k);
+            // Fully unrolled, so the window's rotation below is register renaming, not moves.
+#pragma unroll
+            for (int rr = 0; rr < kTT / 2; ++rr) {
+                const int r = r_begin + rr;
+                if (r >= r_end) break;  // uniform across a GLU lane pair and across the warp
+                const int oy = y0 + r;
+#pragma unroll
+                for (int k = 0; k < 3; ++k) win[2][k] = at(r + 2, xl + k);
+                const bool top = oy > 0, bottom = oy + 1 < h;
+                Vec<4> res = taps<4>(win, wt, bs, top, bottom, left, right);
+                if constexpr (EPI == MBX_EPILOGUE_RELU) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
+                } else if constexpr (kGlu) {
+                    // value · SiLU(gate): the gate lane's result comes across the pair.
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float gate = __shfl_xor_sync(0xffffffffu, res.v[k], 16);
+                        res.v[k] = res.v[k] * dev_silu(gate);
+                    }
+                }
+                if (valid && my_set == 0) vstore<4>(out + (((int64_t)item * h + oy) * w + ox) * c_out + ch, res);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    win[0][k] = win[1][k];
+                    win[1][k] = win[2][k];
+                }
+            }
+        }
+        // Every thread's reads (and the prologue's writes) of this stage are ordered before the
+        // next boxes land in it (an async-proxy write), then thread 0 re-arms the stage.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
-    }
-    const int j = threadIdx.x & 7, xl = (threadIdx.x >> 3) & 15, rg = threadIdx.x >> 7;
-    const int ch = c0 + 4 * j, ox = x0 + xl;
-    if (ch >= c_out || ox >= w) return;
-    // All taps of this thread's channel quad (both GLU sets) stay in registers for the whole tile.
-    Vec<4> wt[kSets][9], bs[kSets];
-#pragma unroll
-    for (int set = 0; set < kSets; ++set) {
-#pragma unroll
-        for (int k = 0; k < 9; ++k) wt[set][k] = vload<4>(weight + k * c + set * c_out + ch);
-        bs[set] = vload<4>(bias + set * c_out + ch);
-    }
-    const bool left = ox > 0, right = ox + 1 < w;
-    auto at = [&](int set, int row, int col) -> Vec<4> {
-        const float4 f = *reinterpret_cast<const float4*>(tile + (((set * kTH + row) * kTH + col) * kTC + 4 * j));
-        Vec<4> r;
-        r.v[0] = f.x;
-        r.v[1] = f.y;
-        r.v[2] = f.z;
-        r.v[3] = f.w;
-        return r;
-    };
-    const int r_begin = rg * (kTT / 2), r_end = min(r_begin + kTT / 2, h - y0);
-    Vec<4> win[kSets][3][3];
-#pragma unroll
-    for (int set = 0; set < kSets; ++set)
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-            for (int k = 0; k < 3; ++k) win[set][rr][k] = at(set, r_begin + rr, xl + k);
-    for (int r = r_begin; r < r_end; ++r) {
-        const int oy = y0 + r;
-#pragma unroll
-        for (int set = 0; set < kSets; ++set)
-#pragma unroll
-            for (int k = 0; k < 3; ++k) win[set][2][k] = at(set, r + 2, xl + k);
-        const bool top = oy > 0, bottom = oy + 1 < h;
-        Vec<4> acc[kSets];
-#pragma unroll
-        for (int set = 0; set < kSets; ++set) acc[set] = taps<4>(win[set], wt[set], bs[set], top, bottom, left, right);
-        Vec<4> res = acc[0];
-        if constexpr (EPI == MBX_EPILOGUE_RELU) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
-        } else if constexpr (kGlu) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
-        }
-        vstore<4>(out + (((int64_t)item * h + oy) * w + ox) * c_out + ch, res);
-#pragma unroll
-        for (int set = 0; set < kSets; ++set)
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                win[set][0][k] = win[set][1][k];
-                win[set][1][k] = win[set][2][k];
-            }
+        if (threadIdx.x == 0 && tt + (int64_t)kStages * gridDim.x < tiles.total)
+            issue(s, tt + (int64_t)kStages * gridDim.x);
     }
 }
 
@@ -354,13 +417,18 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
             const uint64_t strides[3] = {(uint64_t)c * 4, (uint64_t)(w * c) * 4, (uint64_t)(h * w * c) * 4};
             const uint32_t box[4] = {(uint32_t)kTC, (uint32_t)kTH, (uint32_t)kTH, 1};
             encode_tensor_map_f32(&map, x, 4, dims, strides, box, false);
-            const dim3 grid((unsigned)cblocks, (unsigned)(tiles_x * tiles_y), (unsigned)n);
+            DwTiles tiles{(int)cblocks, (int)tiles_x, (int)(tiles_x * tiles_y), cblocks * tiles_x * tiles_y * n};
             auto launch = [&](auto kern, int sets) {
-                const int smem = sets * (int)kSetBytes;
+                const int smem = kStages * sets * (int)kSetBytes;
                 ensure_smem_limit(reinterpret_cast<const void*>(kern), smem, "depthwise smem attribute");
-                kern<<<grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
-                                                                pro_scale, pro_shift, pro_silu ? 1 : 0, out,
-                                                                (int)tiles_x, ctx->dev_err);
+                const int threads = sets == 2 ? 2 * kTileThreads : kTileThreads;
+                int per_sm = 0;
+                check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
+                           "depthwise occupancy");
+                const int64_t grid = std::min<int64_t>(tiles.total, (int64_t)ctx->sm_count * std::max(per_sm, 1));
+                kern<<<(unsigned)grid, threads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
+                                                                          pro_scale, pro_shift, pro_silu ? 1 : 0, out,
+                                                                          tiles, ctx->dev_err);
             };
             if (pro) {
                 if (epilogue == MBX_EPILOGUE_NONE) launch(dw3x3_tma_kernel<MBX_EPILOGUE_NONE, true>, 1);

@@ -143,6 +143,34 @@ __global__ void __launch_bounds__(1024) gn_finalize_kernel(const double* __restr
     }
 }
 
+// Epilogue statistics → GroupNorm partials. Chunk k of item b (pixels 256k … 256k + 255) is the
+// two 128-row M tiles 2·(b·chunks + k) and the next of the producing conv; each tile holds the sums of
+// its four drain warps. Per channel the eight f32 sums are added in a fixed order, then the group's
+// channels are folded in f64 (src/engine/norm.rs:78-80), as gn_partials_kernel does.
+__global__ void gn_fold_tiles_kernel(const float* __restrict__ tp, int64_t total, int c, int groups,
+                                     double* __restrict__ part) {
+    const int cg = c / groups;
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int g = (int)(idx % groups);
+        const int64_t t0 = 2 * (idx / groups);
+        double ss = 0.0, qq = 0.0;
+        for (int ch = g * cg; ch < (g + 1) * cg; ++ch) {
+            float sum = 0.0f, sq = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float* src = tp + (t0 * 4 + k) * 2 * (int64_t)c + ch;
+                sum += __ldg(src);
+                sq += __ldg(src + c);
+            }
+            ss += (double)sum;
+            qq += (double)sq;
+        }
+        part[idx * 2] = ss;
+        part[idx * 2 + 1] = qq;
+    }
+}
+
 // grid.y = item; each thread keeps one channel vector's scale/shift in registers.
 template <int V, bool SILU, bool RES>
 __global__ void __launch_bounds__(256) gn_apply_kernel(const float* __restrict__ x, int64_t hw, int c,
@@ -298,6 +326,15 @@ void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int
     else
         add ? run(gn_partials_kernel<1, true>) : run(gn_partials_kernel<1, false>);
     after_launch(ctx, "group_norm partials");
+}
+
+void launch_gn_fold_tiles(mbx_ctx* ctx, const float* tile_part, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                          double* part) {
+    MBX_REQUIRE(hw % kGnChunk == 0, "GroupNorm fold: maps of a multiple of 256 pixels");
+    const int64_t total = n * gn_chunks(hw) * groups;
+    gn_fold_tiles_kernel<<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(tile_part, total, (int)c, (int)groups,
+                                                                              part);
+    after_launch(ctx, "group_norm fold");
 }
 
 void launch_gn_finalize(mbx_ctx* ctx, const double* part, int64_t n, int64_t hw, int64_t c, int64_t groups,

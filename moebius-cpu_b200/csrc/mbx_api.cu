@@ -665,6 +665,61 @@ int32_t mbx_conv3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t 
     });
 }
 
+int32_t mbx_conv_group_norm_affine(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int64_t w, int64_t c_in,
+                                   const mbx_param* weight, const float* bias, int64_t stride, const int64_t pad[4],
+                                   int32_t upsample2x, const float* pro_scale, const float* pro_shift,
+                                   int32_t pro_silu, const float* residual, int32_t act, float* out, int64_t groups,
+                                   float eps, const float* gamma, const float* beta, const float* add,
+                                   float* scale_out, float* shift_out) {
+    int64_t ho = h, wo = w;
+    if (weight && weight->taps == 9) {
+        const int32_t st = mbx_conv3x3_output_hw(h, w, stride, pad, upsample2x, &ho, &wo);
+        if (st != MBX_OK) return st;
+    }
+    return guard([&] {
+        require_ctx(ctx);
+        MBX_REQUIRE(weight != nullptr, "null weight");
+        MBX_REQUIRE(weight->c_in == c_in, "conv input channels");
+        MBX_REQUIRE(weight->taps == 9 || (stride == 1 && !upsample2x), "a 1x1 conv takes stride 1 and no upsample");
+        MBX_REQUIRE(n >= 0 && h >= 1 && w >= 1, "bad shape");
+        MBX_REQUIRE((pro_scale == nullptr) == (pro_shift == nullptr), "prologue needs both scale and shift");
+        MBX_REQUIRE(act == MBX_ACT_NONE || act == MBX_ACT_SILU, "unknown activation");
+        check_gn(n, ho, wo, weight->c_out, groups);
+        if (n == 0) return;
+        require_ptr(x, "x");
+        require_ptr(out, "out");
+        require_ptr(gamma, "gamma");
+        require_ptr(beta, "beta");
+        require_ptr(scale_out, "scale_out");
+        require_ptr(shift_out, "shift_out");
+        MBX_REQUIRE(out != x, "conv: out must not alias x");
+        if (weight->taps == 9)
+            MBX_REQUIRE((h << (upsample2x ? 1 : 0)) < (1 << 14) && (w << (upsample2x ? 1 : 0)) < (1 << 14),
+                        "conv3x3: image side must be below 16384 (after the optional upsample)");
+        use_device(ctx);
+        const int64_t c_out = weight->c_out;
+        const mbx::ConvShape s = weight->taps == 9
+                                     ? mbx::ConvShape{n, h, w, c_in, ho, wo, int(stride), int(pad[0]), int(pad[1]),
+                                                      upsample2x ? 1 : 0}
+                                     : mbx::ConvShape{n, h, w, c_in, h, w, 1, 0, 0, 0};
+        if (mbx::conv_gn_fusable(s, c_out)) {
+            // Statistics gathered by the conv's epilogue, folded, then the usual finalize.
+            mbx::PoolBuf tiles(ctx, size_t(mbx::conv_gn_part_floats(s, c_out)) * sizeof(float));
+            mbx::launch_conv_tc(ctx, x, s, weight, bias, pro_scale, pro_shift, pro_silu != 0, residual, out, act,
+                                tiles.as<float>(), add);
+            const int64_t hw = ho * wo;
+            mbx::PoolBuf part(ctx, size_t(n) * mbx::gn_chunks(hw) * groups * 2 * sizeof(double));
+            mbx::launch_gn_fold_tiles(ctx, tiles.as<float>(), n, hw, c_out, groups, part.as<double>());
+            mbx::launch_gn_finalize(ctx, part.as<double>(), n, hw, c_out, groups, eps, gamma, beta, add, scale_out,
+                                    shift_out);
+        } else {
+            // Output maps that are not a multiple of 256 pixels (or c_out % 4 != 0): a separate pass.
+            mbx::launch_conv_tc(ctx, x, s, weight, bias, pro_scale, pro_shift, pro_silu != 0, residual, out, act);
+            gn_affine_impl(ctx, out, n, ho, wo, c_out, groups, eps, gamma, beta, add, scale_out, shift_out);
+        }
+    });
+}
+
 int32_t mbx_softmax_rows(mbx_ctx* ctx, float* x, int64_t rows, int64_t n, float scale, float flush) {
     return guard([&] {
         require_ctx(ctx);

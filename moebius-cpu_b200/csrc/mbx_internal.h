@@ -134,7 +134,16 @@ struct ConvShape {
 void launch_wait_probe(mbx_ctx* ctx, int64_t cycles);
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
-                    float* out, int act = 0);
+                    float* out, int act = 0, float* gn_part = nullptr, const float* gn_add = nullptr);
+// GroupNorm statistics gathered in the conv epilogue (gn_part of launch_conv_tc): possible when the
+// output has c_out % 4 == 0 channels and maps of a multiple of 256 pixels (a 256-pixel statistics
+// chunk is then two whole 128-row M tiles of one item); the scratch holds conv_gn_part_floats floats.
+bool conv_gn_fusable(const ConvShape& s, int64_t c_out);
+int64_t conv_gn_part_floats(const ConvShape& s, int64_t c_out);
+// Folds the epilogue's per-(M tile, drain warp) sums into the per-(item, chunk, group) f64 partials
+// that launch_gn_finalize takes (f32 per channel and chunk, then f64 over the group's channels).
+void launch_gn_fold_tiles(mbx_ctx* ctx, const float* tile_part, int64_t n, int64_t hw, int64_t c, int64_t groups,
+                          double* part);
 // A tiled TMA map over f32 data: dims innermost first, strides in bytes for dims 1.., box in
 // elements; reads outside the map fill with zeros.
 void encode_tensor_map_f32(CUtensorMap* map, const float* base, int rank, const uint64_t* dims,

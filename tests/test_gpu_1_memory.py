@@ -122,7 +122,10 @@ def test_depthwise_tails(mbx, ctx, extra_fixture):
                                       ((1, 40, 3, 26), "glu_silu"),
                                       # TMA-tiled kernel: ragged 16 × 16 tiles and a partial channel box
                                       ((1, 37, 45, 72), "glu_silu"), ((2, 20, 50, 96), "relu"),
-                                      ((1, 18, 18, 36), "none")])
+                                      ((1, 18, 18, 36), "none"),
+                                      # several tiles per persistent CTA: the two-stage ring wraps and
+                                      # the channel block (and so the taps) changes between tiles
+                                      ((4, 128, 128, 96), "none"), ((3, 48, 80, 200), "relu")])
 def test_depthwise_matches_oracle(mbx, ctx, oracle, shape, ep):
     rng = np.random.default_rng(shape[-1] + len(ep))
     c = shape[-1]

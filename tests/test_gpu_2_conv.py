@@ -277,3 +277,60 @@ def test_bounded_wait_gives_up_and_the_context_recovers(mbx, ctx, ref_fixture):
     w.close()
     assert scaled_err(got, f["c1.y"]) <= REF_TOL
     ctx.synchronize()
+
+
+@pytest.mark.parametrize("shape,k,co,dtype,with_add,with_res,act,upx", [
+    ((16, 64, 64, 320), 1, 320, "f16", True, True, 0, False),   # UNet DwConv2d pointwise → norm2 (+ temb)
+    ((2, 32, 32, 640), 1, 640, "f16", True, False, 0, False),
+    ((2, 64, 64, 128), 3, 256, "f32", False, False, 0, False),  # VAE resnet conv1 → norm2
+    ((1, 64, 64, 64), 3, 128, "f16", False, True, 0, True),     # upsampled 3×3: output 128 × 128
+    ((1, 32, 32, 96), 1, 160, "f16", False, False, 1, False),   # SiLU epilogue, 160-wide N tiles
+    ((2, 10, 12, 64), 1, 96, "f16", True, False, 0, False),     # 120-pixel maps: the separate statistics pass
+])
+def test_conv_group_norm_affine(mbx, ctx, oracle, shape, k, co, dtype, with_add, with_res, act, upx):
+    """mbx_conv_group_norm_affine: the conv's output is the plain conv's bit for bit, and the
+    GroupNorm affine built from the epilogue's statistics equals the separate statistics pass on
+    that output at the GroupNorm tolerance, and the oracle's conv + GroupNorm::affine at the gates
+    (src/engine/conv.rs:38-102, src/engine/norm.rs:57-129)."""
+    rng = np.random.default_rng(sum(shape) + co + k)
+    n, h, w, ci = shape
+    groups = 32
+    x = rng.standard_normal(shape).astype(np.float32)
+    wshape = (co, ci) if k == 1 else (co, 3, 3, ci)
+    wt = rng.normal(0.0, 1.0 / np.sqrt(ci * k * k), wshape).astype(np.float32)
+    bias = rng.normal(0.0, 0.01, co).astype(np.float32)
+    ho, wo = (2 * h, 2 * w) if upx else (h, w)
+    res = rng.standard_normal((n, ho, wo, co)).astype(np.float32) if with_res else None
+    add = rng.normal(0.0, 0.5, (n, co)).astype(np.float32) if with_add else None
+    gamma = rng.normal(1.0, 0.1, co).astype(np.float32)
+    beta = rng.normal(0.0, 0.1, co).astype(np.float32)
+    p = mbx.Param(ctx, wt, dtype)
+    xd, bd = up(ctx, x), up(ctx, bias)
+    rd = up(ctx, res) if with_res else None
+    ad = up(ctx, add) if with_add else None
+    gd, betad = up(ctx, gamma), up(ctx, beta)
+    out, sc, sh = mbx.conv_group_norm_affine(xd, p, groups, 1e-5, gd, betad, bias=bd, add=ad, upsample2x=upx,
+                                             residual=rd, act=act)
+    if k == 1:
+        plain = ctx.empty((n, ho, wo, co))
+        mbx.check(mbx.abi.lib().mbx_conv1x1_fused(ctx.handle, xd.vp, n, h, w, ci, p.handle, bd.vp, None, None, 0,
+                                                 rd.vp if rd else None, act, plain.vp))
+    else:
+        plain = mbx.conv3x3(xd, p, bd, upsample2x=upx, residual=rd)
+    got = out.numpy()
+    assert np.array_equal(got, plain.numpy())
+    sc2, sh2 = mbx.group_norm_affine(plain, groups, 1e-5, gd, betad, add=ad)
+    assert scaled_err(sc.numpy(), sc2.numpy()) <= REF_TOL
+    assert scaled_err(sh.numpy(), sh2.numpy()) <= REF_TOL
+    wref = wt if dtype == "f32" else wt.astype(np.float16).astype(np.float32)
+    want = oracle.conv1x1(x, wref, bias, res) if k == 1 else oracle.conv3x3(x, wref, bias, upsample2x=upx)
+    if k == 3 and with_res:
+        want = oracle.add(want, res)
+    if act:
+        want = oracle.silu(want)
+    wsc, wsh = oracle.group_norm_affine(want, groups, 1e-5, gamma, beta, add=add)
+    gate = GATE_F32 if dtype == "f32" else GATE_F16
+    assert max_rel_err(got, want) <= gate
+    assert max_rel_err(sc.numpy(), wsc) <= gate
+    assert max_rel_err(sh.numpy(), wsh) <= gate
+    p.close()
