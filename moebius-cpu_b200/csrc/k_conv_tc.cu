@@ -323,7 +323,9 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
                  : "memory");
 }
 
-template <bool F32W, bool VEC4, bool FLAT>
+// GN: the epilogue also gathers GroupNorm statistics (args.gn_part); a separate instantiation, so the
+// other convs' epilogue code is unchanged.
+template <bool F32W, bool VEC4, bool FLAT, bool GN>
 __global__ void __maxnreg__(128)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
                    const __grid_constant__ CUtensorMap tmap_a, const ConvArgs args) {
@@ -563,12 +565,34 @@ __global__ void __maxnreg__(128)
                         const int cb = cchunk * BK + 4 * j0;
                         const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
                         const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
+                        if constexpr (VEC4) {
+                            // c_in % 4 == 0 and 16-byte aligned scale / shift: whole float4 groups.
 #pragma unroll
-                        for (int e = 0; e < 4 * NV; ++e) {
-                            if (cb + e < args.c_in) {
-                                float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
-                                if (args.pro_silu) y = dev_silu(y);
-                                v[e] = y;
+                            for (int jj = 0; jj < NV; ++jj) {
+                                if (cb + 4 * jj >= args.c_in) continue;
+                                const float4 s4 = __ldg(reinterpret_cast<const float4*>(sc) + jj);
+                                const float4 h4 = __ldg(reinterpret_cast<const float4*>(sh) + jj);
+                                float y0 = fmaf(v[4 * jj], s4.x, h4.x), y1 = fmaf(v[4 * jj + 1], s4.y, h4.y);
+                                float y2 = fmaf(v[4 * jj + 2], s4.z, h4.z), y3 = fmaf(v[4 * jj + 3], s4.w, h4.w);
+                                if (args.pro_silu) {
+                                    y0 = dev_silu(y0);
+                                    y1 = dev_silu(y1);
+                                    y2 = dev_silu(y2);
+                                    y3 = dev_silu(y3);
+                                }
+                                v[4 * jj] = y0;
+                                v[4 * jj + 1] = y1;
+                                v[4 * jj + 2] = y2;
+                                v[4 * jj + 3] = y3;
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4 * NV; ++e) {
+                                if (cb + e < args.c_in) {
+                                    float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
+                                    if (args.pro_silu) y = dev_silu(y);
+                                    v[e] = y;
+                                }
                             }
                         }
                     }
@@ -769,7 +793,7 @@ __global__ void __maxnreg__(128)
         const bool vec_out = (args.c_out & 3) == 0;
         // Transposed (coalesced) stores for float4 outputs; a SiLU epilogue keeps one row per thread
         // (inside the UNet its transposed form ran 22 % slower) unless statistics are gathered.
-        const bool transpose = vec_out && (!args.act || args.gn_part);
+        const bool transpose = vec_out && (!args.act || GN);
         int gseg = 0;
         bool live = true;
         for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
@@ -819,7 +843,7 @@ __global__ void __maxnreg__(128)
                             const int64_t m_base = tile_m0(t) + qd * 32;
                             // GroupNorm statistics: the tile's rows all belong to one item.
                             float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs, gad = gs;
-                            if (args.gn_add && col_ok)
+                            if (GN && args.gn_add && col_ok)
                                 gad = __ldg(reinterpret_cast<const float4*>(args.gn_add +
                                                                             (tile_m0(t) / hw_out) * args.c_out + col));
                             // All eight shared loads, then all eight residual loads, then the stores: a
@@ -848,14 +872,14 @@ __global__ void __maxnreg__(128)
                                 if (args.act)
                                     o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
                                 *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
-                                if (args.gn_part) {
+                                if constexpr (GN) {
                                     const float4 y = make_float4(o4.x + gad.x, o4.y + gad.y, o4.z + gad.z, o4.w + gad.w);
                                     gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
                                     gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
                                                      fmaf(y.w, y.w, gq.w));
                                 }
                             }
-                            if (args.gn_part) {
+                            if constexpr (GN) {
                                 // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
                                 // order, so results do not depend on timing), then lanes 0-7 write the
                                 // warp's sums for their four channels.
@@ -1004,9 +1028,9 @@ int stage_count(bool f32w, int bn) {
     return std::min(8, (kMaxSmem - 2048 - kMinStgSlots * (int)A_BYTES - sum_bytes(bn)) / stage);
 }
 
-template <bool F32W, bool VEC4, bool FLAT>
+template <bool F32W, bool VEC4, bool FLAT, bool GN>
 void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtensorMap& tmap_a, int64_t m_tiles) {
-    auto kernel = conv_tc_kernel<F32W, VEC4, FLAT>;
+    auto kernel = conv_tc_kernel<F32W, VEC4, FLAT, GN>;
     const int stage = (F32W ? 2 : 1) * a.bn * 128;
     const int smem = a.stages * stage + a.stg_slots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
     // The register check depends on the build only, so once per process suffices; the
@@ -1166,21 +1190,28 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
             encode_a_map(&tmap_a, x, 4, dims, strides, box);
         }
     }
-    if (a.flat) {
-        if (f32w)
-            vec4 ? run_conv<true, true, true>(ctx, p, a, tmap_a, m_tiles)
-                 : run_conv<true, false, true>(ctx, p, a, tmap_a, m_tiles);
-        else
-            vec4 ? run_conv<false, true, true>(ctx, p, a, tmap_a, m_tiles)
-                 : run_conv<false, false, true>(ctx, p, a, tmap_a, m_tiles);
-    } else {
-        if (f32w)
-            vec4 ? run_conv<true, true, false>(ctx, p, a, tmap_a, m_tiles)
-                 : run_conv<true, false, false>(ctx, p, a, tmap_a, m_tiles);
-        else
-            vec4 ? run_conv<false, true, false>(ctx, p, a, tmap_a, m_tiles)
-                 : run_conv<false, false, false>(ctx, p, a, tmap_a, m_tiles);
-    }
+    auto dispatch = [&](auto gn) {
+        constexpr bool G = decltype(gn)::value;
+        if (a.flat) {
+            if (f32w)
+                vec4 ? run_conv<true, true, true, G>(ctx, p, a, tmap_a, m_tiles)
+                     : run_conv<true, false, true, G>(ctx, p, a, tmap_a, m_tiles);
+            else
+                vec4 ? run_conv<false, true, true, G>(ctx, p, a, tmap_a, m_tiles)
+                     : run_conv<false, false, true, G>(ctx, p, a, tmap_a, m_tiles);
+        } else {
+            if (f32w)
+                vec4 ? run_conv<true, true, false, G>(ctx, p, a, tmap_a, m_tiles)
+                     : run_conv<true, false, false, G>(ctx, p, a, tmap_a, m_tiles);
+            else
+                vec4 ? run_conv<false, true, false, G>(ctx, p, a, tmap_a, m_tiles)
+                     : run_conv<false, false, false, G>(ctx, p, a, tmap_a, m_tiles);
+        }
+    };
+    if (gn_part)
+        dispatch(std::true_type{});
+    else
+        dispatch(std::false_type{});
     after_launch(ctx, "conv (tcgen05)");
 }
 

@@ -178,9 +178,7 @@ __global__ void __launch_bounds__(kDwThreads, 4) dw3x3_kernel(const float* __res
 constexpr int kTT = 16;                                           // tile side (output pixels)
 constexpr int kTC = 32;                                           // channels per tile
 constexpr int kTH = kTT + 2;                                      // halo tile side
-constexpr int kTileThreads = 256;  // 8 vectors × 16 columns × 2 row groups (× 2 channel sets for GLU)
-template <int EPI>
-constexpr int tile_threads() { return EPI == MBX_EPILOGUE_GLU_SILU ? 2 * kTileThreads : kTileThreads; }
+constexpr int kTileThreads = 256;                                 // 8 vectors × 16 columns × 2 row groups
 constexpr uint32_t kSetBytes = (uint32_t)kTH * kTH * kTC * 4;    // 41472
 constexpr int kStages = 2;
 constexpr long long kDwWaitLimit = 4ll << 30;                     // clock cycles (about 2 s)
@@ -213,7 +211,7 @@ struct DwTiles {
 
 // PRO: GroupNorm prologue, the input read as [SiLU](x*pro_scale[item,c] + pro_shift[item,c]).
 template <int EPI, bool PRO>
-__global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
+__global__ void __launch_bounds__(kTileThreads) dw3x3_tma_kernel(const __grid_constant__ CUtensorMap map, int h,
                                                                  int w, int c, const float* __restrict__ weight,
                                                                  const float* __restrict__ bias,
                                                                  const float* __restrict__ pro_scale,
@@ -253,16 +251,11 @@ __global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __
         }
     }
     __syncthreads();
-    // Thread mapping: channel quad j, column xl, row group rg (8 rows each). With GLU the two
-    // channel sets go to a lane pair (lane, lane ^ 16), so each thread holds one set's taps and
-    // window (fewer registers, twice the warps); the value lane takes the gate by shuffle.
-    constexpr int kThreads = tile_threads<EPI>();
-    const int lane = threadIdx.x & 31;
-    const int j = threadIdx.x & 7;
-    const int xl = kGlu ? 2 * ((threadIdx.x >> 5) & 7) + ((lane >> 3) & 1) : (threadIdx.x >> 3) & 15;
-    const int rg = kGlu ? threadIdx.x >> 8 : threadIdx.x >> 7;
-    const int my_set = kGlu ? lane >> 4 : 0;
-    Vec<4> wt[9], bs;
+    // Thread mapping: channel quad j, column xl, row group rg (8 rows each); a thread holds both
+    // GLU sets (splitting them over a lane pair, to halve the registers and double the warps, was
+    // slower: the gate shuffles and the doubled SiLU work cost more than the extra warps gained).
+    const int j = threadIdx.x & 7, xl = (threadIdx.x >> 3) & 15, rg = threadIdx.x >> 7;
+    Vec<4> wt[kSets][9], bs[kSets];
     int cb_loaded = -1;
     int it = 0;
     for (int64_t tt = blockIdx.x; tt < tiles.total; tt += gridDim.x, ++it) {
@@ -312,7 +305,7 @@ __global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __
                 const float4 sc = __ldg(reinterpret_cast<const float4*>(pro_scale + (int64_t)item * c + cc));
                 const float4 sh = __ldg(reinterpret_cast<const float4*>(pro_shift + (int64_t)item * c + cc));
                 float* base = tile + set * kTH * kTH * kTC + 4 * q4;
-                for (int px = threadIdx.x >> 3; px < kTH * kTH; px += kThreads / 8) {
+                for (int px = threadIdx.x >> 3; px < kTH * kTH; px += kTileThreads / 8) {
                     const int row = px / kTH, col = px - row * kTH;
                     const int gy = y0 - 1 + row, gx = x0 - 1 + col;
                     if (gy < 0 || gy >= h || gx < 0 || gx >= w) continue;
@@ -327,21 +320,22 @@ __global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __
             __syncthreads();
         }
         const int ch = c0 + 4 * j, ox = x0 + xl;
-        const bool valid = ch < c_out && ox < w;
-        // The taps of this thread's channel quad (its set) stay in registers while the channel
-        // block stays the same; quads past c_out get zeros (their results are never stored).
-        if (cb != cb_loaded) {
-            const bool real = ch < c_out;
+        if (ch < c_out && ox < w) {
+            // All taps of this thread's channel quad (both GLU sets) stay in registers while the
+            // channel block stays the same.
+            if (cb != cb_loaded) {
 #pragma unroll
-            for (int k = 0; k < 9; ++k) wt[k] = real ? vload<4>(weight + k * c + my_set * c_out + ch) : vzero<4>();
-            bs = real ? vload<4>(bias + my_set * c_out + ch) : vzero<4>();
-            cb_loaded = cb;
-        }
-        if (valid || kGlu) {  // GLU lanes compute unconditionally: the gate shuffle needs the whole warp
+                for (int set = 0; set < kSets; ++set) {
+#pragma unroll
+                    for (int k = 0; k < 9; ++k) wt[set][k] = vload<4>(weight + k * c + set * c_out + ch);
+                    bs[set] = vload<4>(bias + set * c_out + ch);
+                }
+                cb_loaded = cb;
+            }
             const bool left = ox > 0, right = ox + 1 < w;
-            const float* set_tile = tile + my_set * kTH * kTH * kTC;
-            auto at = [&](int row, int col) -> Vec<4> {
-                const float4 f = *reinterpret_cast<const float4*>(set_tile + ((row * kTH + col) * kTC + 4 * j));
+            auto at = [&](int set, int row, int col) -> Vec<4> {
+                const float4 f =
+                    *reinterpret_cast<const float4*>(tile + (((set * kTH + row) * kTH + col) * kTC + 4 * j));
                 Vec<4> r;
                 r.v[0] = f.x;
                 r.v[1] = f.y;
@@ -350,38 +344,44 @@ __global__ void __launch_bounds__(tile_threads<EPI>()) dw3x3_tma_kernel(const __
                 return r;
             };
             const int r_begin = rg * (kTT / 2), r_end = min(r_begin + kTT / 2, h - y0);
-            Vec<4> win[3][3];
+            Vec<4> win[kSets][3][3];
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr)
+            for (int set = 0; set < kSets; ++set)
 #pragma unroll
-                for (int k = 0; k < 3; ++k) win[rr][k] = at(r_begin + rr, xl + k);
+                for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) win[set][rr][k] = at(set, r_begin + rr, xl + k);
             // Fully unrolled, so the window's rotation below is register renaming, not moves.
 #pragma unroll
             for (int rr = 0; rr < kTT / 2; ++rr) {
                 const int r = r_begin + rr;
-                if (r >= r_end) break;  // uniform across a GLU lane pair and across the warp
+                if (r >= r_end) break;
                 const int oy = y0 + r;
 #pragma unroll
-                for (int k = 0; k < 3; ++k) win[2][k] = at(r + 2, xl + k);
+                for (int set = 0; set < kSets; ++set)
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) win[set][2][k] = at(set, r + 2, xl + k);
                 const bool top = oy > 0, bottom = oy + 1 < h;
-                Vec<4> res = taps<4>(win, wt, bs, top, bottom, left, right);
+                Vec<4> acc[kSets];
+#pragma unroll
+                for (int set = 0; set < kSets; ++set)
+                    acc[set] = taps<4>(win[set], wt[set], bs[set], top, bottom, left, right);
+                Vec<4> res = acc[0];
                 if constexpr (EPI == MBX_EPILOGUE_RELU) {
 #pragma unroll
                     for (int k = 0; k < 4; ++k) res.v[k] = fmaxf(res.v[k], 0.0f);
                 } else if constexpr (kGlu) {
-                    // value · SiLU(gate): the gate lane's result comes across the pair.
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float gate = __shfl_xor_sync(0xffffffffu, res.v[k], 16);
-                        res.v[k] = res.v[k] * dev_silu(gate);
+                    for (int k = 0; k < 4; ++k) res.v[k] = acc[0].v[k] * dev_silu(acc[kSets - 1].v[k]);
+                }
+                vstore<4>(out + (((int64_t)item * h + oy) * w + ox) * c_out + ch, res);
+#pragma unroll
+                for (int set = 0; set < kSets; ++set)
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) {
+                        win[set][0][k] = win[set][1][k];
+                        win[set][1][k] = win[set][2][k];
                     }
-                }
-                if (valid && my_set == 0) vstore<4>(out + (((int64_t)item * h + oy) * w + ox) * c_out + ch, res);
-#pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    win[0][k] = win[1][k];
-                    win[1][k] = win[2][k];
-                }
             }
         }
         // Every thread's reads (and the prologue's writes) of this stage are ordered before the
@@ -421,12 +421,11 @@ void launch_depthwise3x3(mbx_ctx* ctx, const float* x, int64_t n, int64_t h, int
             auto launch = [&](auto kern, int sets) {
                 const int smem = kStages * sets * (int)kSetBytes;
                 ensure_smem_limit(reinterpret_cast<const void*>(kern), smem, "depthwise smem attribute");
-                const int threads = sets == 2 ? 2 * kTileThreads : kTileThreads;
                 int per_sm = 0;
-                check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
+                check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTileThreads, smem),
                            "depthwise occupancy");
                 const int64_t grid = std::min<int64_t>(tiles.total, (int64_t)ctx->sm_count * std::max(per_sm, 1));
-                kern<<<(unsigned)grid, threads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
+                kern<<<(unsigned)grid, kTileThreads, smem, ctx->stream>>>(map, (int)h, (int)w, (int)c, weight, bias,
                                                                           pro_scale, pro_shift, pro_silu ? 1 : 0, out,
                                                                           tiles, ctx->dev_err);
             };

@@ -144,30 +144,35 @@ __global__ void __launch_bounds__(1024) gn_finalize_kernel(const double* __restr
 }
 
 // Epilogue statistics → GroupNorm partials. Chunk k of item b (pixels 256k … 256k + 255) is the
-// two 128-row M tiles 2·(b·chunks + k) and the next of the producing conv; each tile holds the sums of
-// its four drain warps. Per channel the eight f32 sums are added in a fixed order, then the group's
-// channels are folded in f64 (src/engine/norm.rs:78-80), as gn_partials_kernel does.
-__global__ void gn_fold_tiles_kernel(const float* __restrict__ tp, int64_t total, int c, int groups,
-                                     double* __restrict__ part) {
+// two 128-row M tiles 2·(b·chunks + k) and the next of the producing conv, whose eight per-warp sum
+// rows [2][c] lie next to each other. One CTA per chunk: per channel the eight f32 sums in a fixed
+// order (coalesced across threads), then each group's channels folded in f64
+// (src/engine/norm.rs:78-80), as gn_partials_kernel does.
+__global__ void __launch_bounds__(256) gn_fold_tiles_kernel(const float* __restrict__ tp, int c, int groups,
+                                                             double* __restrict__ part) {
+    extern __shared__ float chunk_sums[];  // [2][c]
+    const int64_t gc = blockIdx.x;
+    const float* base = tp + gc * 16 * (int64_t)c;
+    for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+        float sum = 0.0f, sq = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            sum += __ldg(base + (int64_t)k * 2 * c + ch);
+            sq += __ldg(base + (int64_t)k * 2 * c + c + ch);
+        }
+        chunk_sums[ch] = sum;
+        chunk_sums[c + ch] = sq;
+    }
+    __syncthreads();
     const int cg = c / groups;
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int g = (int)(idx % groups);
-        const int64_t t0 = 2 * (idx / groups);
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
         double ss = 0.0, qq = 0.0;
         for (int ch = g * cg; ch < (g + 1) * cg; ++ch) {
-            float sum = 0.0f, sq = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float* src = tp + (t0 * 4 + k) * 2 * (int64_t)c + ch;
-                sum += __ldg(src);
-                sq += __ldg(src + c);
-            }
-            ss += (double)sum;
-            qq += (double)sq;
+            ss += (double)chunk_sums[ch];
+            qq += (double)chunk_sums[c + ch];
         }
-        part[idx * 2] = ss;
-        part[idx * 2 + 1] = qq;
+        part[(gc * groups + g) * 2] = ss;
+        part[(gc * groups + g) * 2 + 1] = qq;
     }
 }
 
@@ -331,9 +336,13 @@ void launch_gn_partials(mbx_ctx* ctx, const float* x, int64_t n, int64_t hw, int
 void launch_gn_fold_tiles(mbx_ctx* ctx, const float* tile_part, int64_t n, int64_t hw, int64_t c, int64_t groups,
                           double* part) {
     MBX_REQUIRE(hw % kGnChunk == 0, "GroupNorm fold: maps of a multiple of 256 pixels");
-    const int64_t total = n * gn_chunks(hw) * groups;
-    gn_fold_tiles_kernel<<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(tile_part, total, (int)c, (int)groups,
-                                                                              part);
+    const int64_t chunks = n * gn_chunks(hw);
+    MBX_REQUIRE(chunks < (int64_t(1) << 31), "GroupNorm fold: too many chunks");
+    const int smem = (int)(2 * c * sizeof(float));
+    if (smem > 48 * 1024)
+        ensure_smem_limit(reinterpret_cast<const void*>(gn_fold_tiles_kernel), smem, "gn fold smem attribute");
+    const int threads = (int)std::min<int64_t>(256, (c + 31) / 32 * 32);
+    gn_fold_tiles_kernel<<<(unsigned)chunks, threads, smem, ctx->stream>>>(tile_part, (int)c, (int)groups, part);
     after_launch(ctx, "group_norm fold");
 }
 
