@@ -266,9 +266,11 @@ __global__ void __launch_bounds__(512, 1)
         acc1[j] += last1.y;
     }
     const float* hbase = halo + (ty * kHalo + tx) * HS + 4 * jh;
-    auto tap = [&](int d, float ca, float cb) {
-        const int ky = d / kWin, kx = d - ky * kWin;
-        const float* hr = hbase + (ky * kHalo + kx) * HS;
+    // Tap d (0 ≤ d < 225) of a block of window rows starting at row `row0`: `dd` = d − 15·row0 is a
+    // compile-time constant inside the unrolled blocks below, so the window offset is an immediate.
+    auto tap = [&](const float* hrow0, int dd, float ca, float cb) {
+        const int ky = dd / kWin, kx = dd - ky * kWin;
+        const float* hr = hrow0 + (ky * kHalo + kx) * HS;
 #pragma unroll
         for (int i = 0; i < NG; ++i) {
             const float4 v4 = *reinterpret_cast<const float4*>(hr + 8 * i);
@@ -282,23 +284,71 @@ __global__ void __launch_bounds__(512, 1)
             acc1[4 * i + 3] = fmaf(cb, v4.w, acc1[4 * i + 3]);
         }
     };
-    // The coefficients stream from global memory four taps at a time; the next group's loads are
-    // issued before this group's FMAs so their latency hides behind them.
-    float4 ca4 = __ldg(reinterpret_cast<const float4*>(arow0));
-    float4 cb4 = __ldg(reinterpret_cast<const float4*>(arow1));
+    // Taps in (ky, kx) order, in blocks of 60 (4 window rows, 15 coefficient float4s): three full
+    // blocks, then 44 taps and tap 224 (from last0 / last1). Inside a block everything is unrolled;
+    // the coefficients stream from global memory a float4 (four taps) at a time, the next one
+    // loaded before the current four taps' FMAs.
+    constexpr int kBlock = 4 * kWin;
+    if constexpr (NG > 5) {
+        // 80-channel slices: 80 accumulators leave no registers for the unrolled blocks' window
+        // loads in flight (it spilled), so one float4 of coefficients (four taps) per iteration.
+        float4 ca4 = __ldg(reinterpret_cast<const float4*>(arow0));
+        float4 cb4 = __ldg(reinterpret_cast<const float4*>(arow1));
 #pragma unroll 1
-    for (int d = 0; d < kTaps - 1; d += 4) {
-        const float4 ca = ca4, cb = cb4;
-        if (d + 4 < kTaps - 1) {
-            ca4 = __ldg(reinterpret_cast<const float4*>(arow0 + d + 4));
-            cb4 = __ldg(reinterpret_cast<const float4*>(arow1 + d + 4));
+        for (int d = 0; d < kTaps - 1; d += 4) {
+            const float4 ca = ca4, cb = cb4;
+            if (d + 4 < kTaps - 1) {
+                ca4 = __ldg(reinterpret_cast<const float4*>(arow0 + d + 4));
+                cb4 = __ldg(reinterpret_cast<const float4*>(arow1 + d + 4));
+            }
+            tap(hbase, d, ca.x, cb.x);
+            tap(hbase, d + 1, ca.y, cb.y);
+            tap(hbase, d + 2, ca.z, cb.z);
+            tap(hbase, d + 3, ca.w, cb.w);
         }
-        tap(d, ca.x, cb.x);
-        tap(d + 1, ca.y, cb.y);
-        tap(d + 2, ca.z, cb.z);
-        tap(d + 3, ca.w, cb.w);
+        tap(hbase, kTaps - 1, last0.x, last1.x);
+    } else {
+#pragma unroll 1
+    for (int blk = 0; blk < 3; ++blk) {
+        const float* hrow0 = hbase + blk * 4 * kHalo * HS;
+        const float* c0p = arow0 + blk * kBlock;
+        const float* c1p = arow1 + blk * kBlock;
+        float4 ca4 = __ldg(reinterpret_cast<const float4*>(c0p));
+        float4 cb4 = __ldg(reinterpret_cast<const float4*>(c1p));
+#pragma unroll
+        for (int g = 0; g < kBlock / 4; ++g) {
+            const float4 ca = ca4, cb = cb4;
+            if (g + 1 < kBlock / 4) {
+                ca4 = __ldg(reinterpret_cast<const float4*>(c0p + 4 * (g + 1)));
+                cb4 = __ldg(reinterpret_cast<const float4*>(c1p + 4 * (g + 1)));
+            }
+            tap(hrow0, 4 * g, ca.x, cb.x);
+            tap(hrow0, 4 * g + 1, ca.y, cb.y);
+            tap(hrow0, 4 * g + 2, ca.z, cb.z);
+            tap(hrow0, 4 * g + 3, ca.w, cb.w);
+        }
     }
-    tap(kTaps - 1, last0.x, last1.x);
+    {
+        const float* hrow0 = hbase + 12 * kHalo * HS;
+        const float* c0p = arow0 + 3 * kBlock;
+        const float* c1p = arow1 + 3 * kBlock;
+        float4 ca4 = __ldg(reinterpret_cast<const float4*>(c0p));
+        float4 cb4 = __ldg(reinterpret_cast<const float4*>(c1p));
+#pragma unroll
+        for (int g = 0; g < 11; ++g) {
+            const float4 ca = ca4, cb = cb4;
+            if (g + 1 < 11) {
+                ca4 = __ldg(reinterpret_cast<const float4*>(c0p + 4 * (g + 1)));
+                cb4 = __ldg(reinterpret_cast<const float4*>(c1p + 4 * (g + 1)));
+            }
+            tap(hrow0, 4 * g, ca.x, cb.x);
+            tap(hrow0, 4 * g + 1, ca.y, cb.y);
+            tap(hrow0, 4 * g + 2, ca.z, cb.z);
+            tap(hrow0, 4 * g + 3, ca.w, cb.w);
+        }
+        tap(hrow0, 44, last0.x, last1.x);  // tap 224
+    }
+    }
     float* o0 = out + pix * c + h0 * k + j0 + 4 * jh;
     float* o1 = o0 + k;
 #pragma unroll
