@@ -148,6 +148,17 @@ def traffic_from_profiles(kernel_key: str):
     return None
 
 
+def traffic_ratios_from_profiles():
+    """DRAM bytes ÷ algorithmic bytes per memory-bound op, from the committed ncu summaries."""
+    pdir = os.path.join(REPO, "profiles")
+    out = {}
+    if os.path.isdir(pdir):
+        for name in sorted(os.listdir(pdir)):
+            for m in re.finditer(r"traffic_ratio_([a-z0-9_]+):\s*([0-9.]+)", open(os.path.join(pdir, name)).read()):
+                out[m.group(1)] = float(m.group(2))
+    return out
+
+
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -336,7 +347,9 @@ def bench_memory_sweep(mbx, ctx, torch, dev, small, hbm, shape=None):
             "gbs": round(sum(BYTES_PER_ELT.values()) * elems / (total_ms / 1e3) / 1e9, 1),
             "ops_ms": {k: round(v, 4) for k, v in op_ms.items()},
             "ops_frac_of_hbm": {k: round(BYTES_PER_ELT[k] * elems / (v / 1e3) / 1e9 / hbm, 4)
-                                for k, v in op_ms.items()}}
+                                for k, v in op_ms.items()},
+            "traffic_ratio_ncu": {k: v for k, v in traffic_ratios_from_profiles().items()},
+            "traffic_ratio_note": "DRAM bytes (ncu, profiles/*.md, [8,128,128,512]) / algorithmic bytes"}
 
 
 def bench_gn_fused(mbx, ctx, torch, dev, hbm, shape):
