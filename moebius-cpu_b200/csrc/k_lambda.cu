@@ -234,6 +234,8 @@ __global__ void __launch_bounds__(512, 1)
     // Content term Yc = Q·λc.
     const float* q0 = q + pix * c + h0 * k;
     const float* q1 = q0 + k;
+    // k is a multiple of 8: two steps per trip keep two groups of loads in flight.
+#pragma unroll 2
     for (int kk = 0; kk < k; kk += 4) {
         const float4 a4 = __ldg(reinterpret_cast<const float4*>(q0 + kk));
         const float4 b4 = __ldg(reinterpret_cast<const float4*>(q1 + kk));
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(512, 1)
     float bm0[kTokens], bm1[kTokens];
 #pragma unroll
     for (int m = 0; m < kTokens; ++m) bm0[m] = bm1[m] = 0.0f;
-    for (int kk = 0; kk < k; kk += 4) {
+    auto b_step = [&](int kk) {
         const float4 a4 = __ldg(reinterpret_cast<const float4*>(q0 + kk));
         const float4 b4 = __ldg(reinterpret_cast<const float4*>(q1 + kk));
 #pragma unroll
@@ -426,6 +428,14 @@ __global__ void __launch_bounds__(512, 1)
             bm1[m] = fmaf(b4.z, e4.z, bm1[m]);
             bm1[m] = fmaf(b4.w, e4.w, bm1[m]);
         }
+    };
+    if constexpr (NG <= 5) {
+        // k is a multiple of 8: two steps per trip keep two groups of table loads in flight (the
+        // 80-channel slices have no registers to spare for it).
+#pragma unroll 2
+        for (int kk = 0; kk < k; kk += 4) b_step(kk);
+    } else {
+        for (int kk = 0; kk < k; kk += 4) b_step(kk);
     }
     // acc0 / acc1: heads h0 / h0 + 1; element 4·i + e is value channel j0 + 8·i + 4·jh + e.
     float acc0[4 * NG], acc1[4 * NG];
