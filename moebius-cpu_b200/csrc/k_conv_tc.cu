@@ -827,83 +827,6 @@ __global__ void __maxnreg__(128)
                         for (int v = 0; v < 8; ++v)
                             st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1],
                                          acc[4 * v + 2], acc[4 * v + 3]);
-                        if (!last) continue;
-                        // Transposed stores: the warp's 32 × 32 block goes through this row's slot
-                        // of the (segment) sum buffer, so each store instruction writes four
-                        // whole 128-byte row pieces instead of 32 scattered 16-byte ones. Lane l
-                        // takes the float4 column group l % 8 of rows 4i + l / 8. The row stride
-                        // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
-                        __syncwarp();
-                        const int nb = n0 + cc;
-                        if (nb < args.c_out) {
-                            const int j = lane & 7;
-                            const int col = nb + 4 * j;
-                            const bool col_ok = col < args.c_out;  // c_out % 4 == 0: the whole float4
-                            const float4 b4 = args.bias && col_ok
-                                                  ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
-                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                            const int64_t m_base = tile_m0(t) + qd * 32;
-                            // GroupNorm statistics: the tile's rows all belong to one item.
-                            float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs, gad = gs;
-                            if (GN && args.gn_add && col_ok)
-                                gad = __ldg(reinterpret_cast<const float4*>(args.gn_add +
-                                                                            (tile_m0(t) / hw_out) * args.c_out + col));
-                            // All eight shared loads, then all eight residual loads, then the stores: a
-                            // residual load placed after a store would wait out its whole latency.
-                            float4 a4[8], r4[8];
-#pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
-                                                     (uint32_t)(cc + 4 * j) * 4u);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const int64_t mr = m_base + 4 * i + (lane >> 3);
-                                r4[i] = args.residual && col_ok && mr < args.m_total
-                                            ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const int64_t mr = m_base + 4 * i + (lane >> 3);
-                                if (mr >= args.m_total || !col_ok) continue;
-                                float4 pre = b4;
-                                if (args.residual)
-                                    pre = make_float4(r4[i].x + pre.x, r4[i].y + pre.y, r4[i].z + pre.z, r4[i].w + pre.w);
-                                const float4 a = a4[i];
-                                float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
-                                if (args.act)
-                                    o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
-                                *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
-                                if constexpr (GN) {
-                                    const float4 y = make_float4(o4.x + gad.x, o4.y + gad.y, o4.z + gad.z, o4.w + gad.w);
-                                    gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
-                                    gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
-                                                     fmaf(y.w, y.w, gq.w));
-                                }
-                            }
-                            if constexpr (GN) {
-                                // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
-                                // order, so results do not depend on timing), then lanes 0-7 write the
-                                // warp's sums for their four channels.
-#pragma unroll
-                                for (int o = 8; o <= 16; o <<= 1) {
-                                    gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
-                                    gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
-                                    gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
-                                    gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
-                                    gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
-                                    gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
-                                    gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
-                                    gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
-                                }
-                                if (lane < 8 && col_ok) {
-                                    float* dst = args.gn_part + ((tile_m0(t) / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
-                                    *reinterpret_cast<float4*>(dst) = gs;
-                                    *reinterpret_cast<float4*>(dst + args.c_out) = gq;
-                                }
-                            }
-                        }
-                        __syncwarp();  // the slots are read before any lane overwrites them
                         continue;
                     }
                     if (m >= args.m_total) continue;
@@ -941,8 +864,90 @@ __global__ void __maxnreg__(128)
                         }
                     }
                 }
+                // The accumulator has been read (into registers, or into the sum buffer for folds
+                // and transposed epilogues): the MMA warp may start the segment after next in it
+                // while the stores below run.
                 tc_fence_before();
-                mbar_arrive(acc_empty_bar(b));  // the accumulator has been read into registers
+                mbar_arrive(acc_empty_bar(b));
+                if (!last || !transpose) continue;
+                __syncwarp();  // the rows written above are read by other lanes below
+                for (int cc = 0; cc < bn; cc += 32) {
+                    // Transposed stores: the warp's 32 × 32 block goes through this row's slot
+                    // of the (segment) sum buffer, so each store instruction writes four
+                    // whole 128-byte row pieces instead of 32 scattered 16-byte ones. Lane l
+                    // takes the float4 column group l % 8 of rows 4i + l / 8. The row stride
+                    // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
+                    const int nb = n0 + cc;
+                    if (nb < args.c_out) {
+                        const int j = lane & 7;
+                        const int col = nb + 4 * j;
+                        const bool col_ok = col < args.c_out;  // c_out % 4 == 0: the whole float4
+                        const float4 b4 = args.bias && col_ok
+                                              ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const int64_t m_base = tile_m0(t) + qd * 32;
+                        // GroupNorm statistics: the tile's rows all belong to one item.
+                        float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs, gad = gs;
+                        if (GN && args.gn_add && col_ok)
+                            gad = __ldg(reinterpret_cast<const float4*>(args.gn_add +
+                                                                        (tile_m0(t) / hw_out) * args.c_out + col));
+                        // All eight shared loads, then all eight residual loads, then the stores: a
+                        // residual load placed after a store would wait out its whole latency.
+                        float4 a4[8], r4[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
+                                                 (uint32_t)(cc + 4 * j) * 4u);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int64_t mr = m_base + 4 * i + (lane >> 3);
+                            r4[i] = args.residual && col_ok && mr < args.m_total
+                                        ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int64_t mr = m_base + 4 * i + (lane >> 3);
+                            if (mr >= args.m_total || !col_ok) continue;
+                            float4 pre = b4;
+                            if (args.residual)
+                                pre = make_float4(r4[i].x + pre.x, r4[i].y + pre.y, r4[i].z + pre.z, r4[i].w + pre.w);
+                            const float4 a = a4[i];
+                            float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
+                            if (args.act)
+                                o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                            *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
+                            if constexpr (GN) {
+                                const float4 y = make_float4(o4.x + gad.x, o4.y + gad.y, o4.z + gad.z, o4.w + gad.w);
+                                gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
+                                gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
+                                                 fmaf(y.w, y.w, gq.w));
+                            }
+                        }
+                        if constexpr (GN) {
+                            // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
+                            // order, so results do not depend on timing), then lanes 0-7 write the
+                            // warp's sums for their four channels.
+#pragma unroll
+                            for (int o = 8; o <= 16; o <<= 1) {
+                                gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
+                                gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
+                                gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
+                                gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
+                                gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
+                                gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
+                                gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
+                                gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
+                            }
+                            if (lane < 8 && col_ok) {
+                                float* dst = args.gn_part + ((tile_m0(t) / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
+                                *reinterpret_cast<float4*>(dst) = gs;
+                                *reinterpret_cast<float4*>(dst + args.c_out) = gq;
+                            }
+                        }
+                    }
+                }
+                __syncwarp();  // the slots are read before any lane overwrites them
             }
         }
     }
