@@ -17,10 +17,10 @@
 //               raw staging ring (as many 16 KB slots as shared memory holds);
 //               zero padding (src-size 0), stride and the nearest-2× upsample
 //               are all address arithmetic here.
-//   warps 10-13 converters: apply the optional GroupNorm prologue
-//               [SiLU](x·scale + shift) at spatially valid taps, split each value
-//               v into hi = v (the tensor core reads it truncated to TF32) and
-//               lo = v − trunc_TF32(v) (exact), and tcgen05.st both into TMEM.
+//   warps 10-13 converters: split each value v into hi = v (the tensor core
+//               reads it truncated to TF32) and lo = v − trunc_TF32(v) (exact),
+//               and tcgen05.st both into TMEM. An optional GroupNorm prologue
+//               runs as its own pass before the kernel (launch_conv_tc).
 //   warp 4      MMA issuer (one thread) + TMEM allocation; K chunks go out in
 //               pairs, one barrier wait and one fence per 16 or 24 MMAs.
 //   warp 5      TMA issuer (one thread) for the pre-split weight tiles.
@@ -100,9 +100,6 @@ struct ConvArgs {
     const float* bias;
     const float* residual;
     float* out;
-    const float* pro_scale;
-    const float* pro_shift;
-    int pro_silu;
     int act;  // epilogue activation after bias and residual: 0 none, 1 SiLU
     // GroupNorm statistics of the output (null = off): per M tile and drain warp, the f32 sums of
     // y and y² over the warp's 32 rows per channel, y = out + gn_add[item] ([n][c_out] or null);
@@ -515,28 +512,16 @@ __global__ void __maxnreg__(128)
         asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit (abort path)
     } else if (is_converter) {
         // ------------------------------------------------------------ converters
-        // One tile row per thread (its TMEM lane): staging row → [SiLU](x·scale + shift) at a
-        // spatially valid tap (padding stays zero; channel padding beyond c_in meets zero
-        // weights) → TF32 high and low parts written to the A stage in TMEM. With eight
-        // converter warps, warps 10-13 take channels 0-15 and warps 0-3 16-31.
+        // One tile row per thread (its TMEM lane): staging row (zeros at padding taps; channel
+        // padding beyond c_in meets zero weights) → TF32 high and low parts written to the A stage
+        // in TMEM. With eight converter warps, warps 10-13 take channels 0-15 and warps 0-3 16-31.
         const int qd = warp & 3;
         const int half = warp < 4 ? 1 : 0;
         const int r = qd * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
-        const bool pro = args.pro_scale != nullptr;
         int q = 0, qphase = 0, a = 0, aphase = 0;
         bool live = true;
         for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
-            const int64_t m0 = tile_m0(t);
-            int pb = 0, geo = 0;
-            if constexpr (FLAT) {
-                // 1×1: the row's item selects the prologue's per-item scale / shift.
-                const int64_t m = m0 + r;
-                pb = m < args.m_total ? (int)(m / hw_out) : 0;
-            } else {
-                row_geo(m0, r, pb, geo);
-            }
-            int tap = 0, cchunk = 0;
             for (int kc = 0; kc < K; ++kc) {
                 if (!mbar_wait(sfull_bar(q), (uint32_t)qphase, args.err, 9, abort_flag, true) ||
                     !mbar_wait(a_empty_bar(a), (uint32_t)(aphase ^ 1), args.err, 1, abort_flag, true)) {
@@ -545,10 +530,8 @@ __global__ void __maxnreg__(128)
                     break;
                 }
                 const uint32_t stg = stg_base + (uint32_t)q * A_BYTES + (uint32_t)r * 128u;
-                bool ok = true;
-                if (pro) (void)tap_pixel(m0, r, pb, geo, tap / 3, tap - 3 * (tap / 3), ok);
-                // Loads 4·NV channels (16-byte units j0 …) of the row, applies the prologue, stores the
-                // high parts, releases the staging slot and stores the low parts at column c0.
+                // Loads 4·NV channels (16-byte units j0 …) of the row, stores the high parts, releases
+                // the staging slot and stores the low parts at column c0.
                 auto convert = [&](auto nv_tag, int j0, uint32_t c0) {
                     constexpr int NV = decltype(nv_tag)::value;
                     float v[4 * NV];
@@ -561,41 +544,6 @@ __global__ void __maxnreg__(128)
                         v[4 * jj + 3] = f.w;
                     }
                     if (!args.a_tma) mbar_arrive(sempty_bar(q));  // the staging row is in registers
-                    if (pro && ok) {
-                        const int cb = cchunk * BK + 4 * j0;
-                        const float* sc = args.pro_scale + (int64_t)pb * args.c_in + cb;
-                        const float* sh = args.pro_shift + (int64_t)pb * args.c_in + cb;
-                        if constexpr (VEC4) {
-                            // c_in % 4 == 0 and 16-byte aligned scale / shift: whole float4 groups.
-#pragma unroll
-                            for (int jj = 0; jj < NV; ++jj) {
-                                if (cb + 4 * jj >= args.c_in) continue;
-                                const float4 s4 = __ldg(reinterpret_cast<const float4*>(sc) + jj);
-                                const float4 h4 = __ldg(reinterpret_cast<const float4*>(sh) + jj);
-                                float y0 = fmaf(v[4 * jj], s4.x, h4.x), y1 = fmaf(v[4 * jj + 1], s4.y, h4.y);
-                                float y2 = fmaf(v[4 * jj + 2], s4.z, h4.z), y3 = fmaf(v[4 * jj + 3], s4.w, h4.w);
-                                if (args.pro_silu) {
-                                    y0 = dev_silu(y0);
-                                    y1 = dev_silu(y1);
-                                    y2 = dev_silu(y2);
-                                    y3 = dev_silu(y3);
-                                }
-                                v[4 * jj] = y0;
-                                v[4 * jj + 1] = y1;
-                                v[4 * jj + 2] = y2;
-                                v[4 * jj + 3] = y3;
-                            }
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 4 * NV; ++e) {
-                                if (cb + e < args.c_in) {
-                                    float y = fmaf(v[e], __ldg(sc + e), __ldg(sh + e));
-                                    if (args.pro_silu) y = dev_silu(y);
-                                    v[e] = y;
-                                }
-                            }
-                        }
-                    }
                     // High part: the value itself (the tensor core reads its TF32 truncation); low
                     // part: v − trunc_tf32(v), exact in f32 (again read truncated).
                     if constexpr (NV == 8) tmem_st32(lane_base + a_col(a) + c0, v);
@@ -626,10 +574,6 @@ __global__ void __maxnreg__(128)
                 if (++a == astages) {
                     a = 0;
                     aphase ^= 1;
-                }
-                if (++cchunk == args.cin_chunks) {
-                    cchunk = 0;
-                    ++tap;
                 }
             }
         }
@@ -1117,6 +1061,19 @@ void encode_param_tmaps(mbx_param* p) {
 void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_param* p, const float* bias,
                     const float* pro_scale, const float* pro_shift, bool pro_silu, const float* residual,
                     float* out, int act, float* gn_part, const float* gn_add) {
+    if (pro_scale) {
+        // The GroupNorm prologue as its own memory-bound pass into a pooled buffer. Applied per
+        // K chunk in the converters it is redone for every tap and every N tile that reads the
+        // pixel (36 times for a 3×3 conv to 512 channels), and its per-chunk scale / shift loads sit
+        // on the converters' critical path: 3×3 convs with it ran 3.3× slower, 1×1 convs 1.9×.
+        // Padding stays zero either way (the conv reads zeros outside the map).
+        PoolBuf normed(ctx, size_t(s.n * s.h * s.w * s.c_in) * sizeof(float));
+        launch_gn_apply(ctx, x, s.n, s.h * s.w, s.c_in, pro_scale, pro_shift, pro_silu, nullptr,
+                        normed.as<float>());
+        launch_conv_tc(ctx, normed.as<float>(), s, p, bias, nullptr, nullptr, false, residual, out, act, gn_part,
+                       gn_add);
+        return;
+    }
     ConvArgs a{};
     a.x = x;
     a.m_total = s.n * s.ho * s.wo;
@@ -1149,9 +1106,6 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     a.bias = bias;
     a.residual = residual;
     a.out = out;
-    a.pro_scale = pro_scale;
-    a.pro_shift = pro_shift;
-    a.pro_silu = pro_silu ? 1 : 0;
     a.act = act;
     a.gn_part = gn_part;
     a.gn_add = gn_add;
@@ -1165,9 +1119,7 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
     // The abort path counts a CTA's K chunks in 32-bit integers.
     MBX_REQUIRE((a.tiles + ctx->sm_count - 1) / ctx->sm_count * a.k_chunks < (int64_t(1) << 31),
                 "conv: too many K chunks per CTA");
-    const bool vec4 = (s.c_in & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-                      (!pro_scale || ((reinterpret_cast<uintptr_t>(pro_scale) & 15) == 0 &&
-                                      (reinterpret_cast<uintptr_t>(pro_shift) & 15) == 0));
+    const bool vec4 = (s.c_in & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const bool aligned_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                              (!residual || (reinterpret_cast<uintptr_t>(residual) & 15) == 0) &&
                              (!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
