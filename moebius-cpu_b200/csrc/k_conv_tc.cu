@@ -742,17 +742,36 @@ __global__ void __maxnreg__(128)
         const bool transpose = vec_out && (!args.act || GN);
         int gseg = 0;
         bool live = true;
+        // Transposed epilogue: lane l owns the float4 column group l % 8 of rows 4i + l / 8 of each
+        // 32 × 32 block. Its bias and GroupNorm-add operands for a block are loaded one block ahead
+        // (the first block's before the accumulator wait), so no block waits out their latency
+        // (loaded per block, that wait cost the short-K 1×1 convs up to 16 %).
+        const int tj = lane & 7;
+        struct BlockIn {
+            float4 bias, gadd;
+        };
+        auto load_block = [&](int64_t t, int n0, int cc, BlockIn& in) {
+            const int col = n0 + cc + 4 * tj;
+            const bool ok = n0 + cc < args.c_out && col < args.c_out;  // c_out % 4 == 0: whole float4s
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            in.bias = args.bias && ok ? __ldg(reinterpret_cast<const float4*>(args.bias + col)) : z;
+            in.gadd = GN && args.gn_add && ok
+                          ? __ldg(reinterpret_cast<const float4*>(args.gn_add + (tile_m0(t) / hw_out) * args.c_out + col))
+                          : z;
+        };
         for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
             const int64_t m = tile_m0(t) + row;
             const int n0 = tile_n0(t);
+            BlockIn cur;
             for (int seg = 0; seg < nseg; ++seg, ++gseg) {
                 const int b = gseg & 1;
+                const bool last = seg + 1 == nseg;
+                if (last && transpose) load_block(t, n0, 0, cur);
                 if (!mbar_wait(acc_full_bar(b), (gseg >> 1) & 1, args.err, 6, abort_flag, true)) {
                     live = false;
                     break;
                 }
                 tc_fence_after();
-                const bool last = seg + 1 == nseg;
                 for (int cc = 0; cc < bn; cc += 32) {
                     float acc[32];
                     tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
@@ -818,51 +837,47 @@ __global__ void __maxnreg__(128)
                 for (int cc = 0; cc < bn; cc += 32) {
                     // Transposed stores: the warp's 32 × 32 block goes through this row's slot
                     // of the (segment) sum buffer, so each store instruction writes four
-                    // whole 128-byte row pieces instead of 32 scattered 16-byte ones. Lane l
-                    // takes the float4 column group l % 8 of rows 4i + l / 8. The row stride
+                    // whole 128-byte row pieces instead of 32 scattered 16-byte ones. The row stride
                     // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
+                    BlockIn nxt;
+                    if (cc + 32 < bn) load_block(t, n0, cc + 32, nxt);
                     const int nb = n0 + cc;
                     if (nb < args.c_out) {
-                        const int j = lane & 7;
-                        const int col = nb + 4 * j;
-                        const bool col_ok = col < args.c_out;  // c_out % 4 == 0: the whole float4
-                        const float4 b4 = args.bias && col_ok
-                                              ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
-                        const int64_t m_base = tile_m0(t) + qd * 32;
-                        // GroupNorm statistics: the tile's rows all belong to one item.
-                        float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs, gad = gs;
-                        if (GN && args.gn_add && col_ok)
-                            gad = __ldg(reinterpret_cast<const float4*>(args.gn_add +
-                                                                        (tile_m0(t) / hw_out) * args.c_out + col));
+                        const int col = nb + 4 * tj;
+                        const bool col_ok = col < args.c_out;
+                        const int64_t m_base = tile_m0(t) + qd * 32 + (lane >> 3);
+                        float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs;
                         // All eight shared loads, then all eight residual loads, then the stores: a
                         // residual load placed after a store would wait out its whole latency.
                         float4 a4[8], r4[8];
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
                             a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
-                                                 (uint32_t)(cc + 4 * j) * 4u);
+                                                 (uint32_t)(cc + 4 * tj) * 4u);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const int64_t mr = m_base + 4 * i + (lane >> 3);
+                            const int64_t mr = m_base + 4 * i;
                             r4[i] = args.residual && col_ok && mr < args.m_total
                                         ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
                         }
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const int64_t mr = m_base + 4 * i + (lane >> 3);
+                            const int64_t mr = m_base + 4 * i;
                             if (mr >= args.m_total || !col_ok) continue;
-                            float4 pre = b4;
-                            if (args.residual)
-                                pre = make_float4(r4[i].x + pre.x, r4[i].y + pre.y, r4[i].z + pre.z, r4[i].w + pre.w);
                             const float4 a = a4[i];
+                            const float4 pre = make_float4(r4[i].x + cur.bias.x, r4[i].y + cur.bias.y,
+                                                           r4[i].z + cur.bias.z, r4[i].w + cur.bias.w);
                             float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
-                            if (args.act)
+                            // Only statistics-gathering convs reach this path with an activation (see
+                            // `transpose`). A runtime-only test let the compiler predicate the SiLU
+                            // instead of branching: 32 exp/divide pairs per block on every conv.
+                            if (GN && args.act)
                                 o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
                             *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
                             if constexpr (GN) {
-                                const float4 y = make_float4(o4.x + gad.x, o4.y + gad.y, o4.z + gad.z, o4.w + gad.w);
+                                const float4 g = cur.gadd;
+                                const float4 y = make_float4(o4.x + g.x, o4.y + g.y, o4.z + g.z, o4.w + g.w);
                                 gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
                                 gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
                                                  fmaf(y.w, y.w, gq.w));
@@ -890,6 +905,7 @@ __global__ void __maxnreg__(128)
                             }
                         }
                     }
+                    if (cc + 32 < bn) cur = nxt;
                 }
                 __syncwarp();  // the slots are read before any lane overwrites them
             }
