@@ -96,6 +96,11 @@ struct ConvArgs {
     // and tap from a 4-D map [n][h][w][c_in] (3×3, stride 1, no upsample; the box's zero fill
     // outside the map is the padding).
     int a_tma, a_bw;
+    // Epilogue by bulk tensor stores (single-segment tiles, float4 outputs, no activation, no
+    // statistics): the drain adds bias and residual while copying the accumulator into 32 × 32
+    // swizzled blocks in shared memory, and one lane per warp stores them with TMA; the residual
+    // blocks arrive by TMA beforehand (has_res).
+    int tma_out, has_res;
     int64_t tiles;  // m tiles × n tiles
     const float* bias;
     const float* residual;
@@ -200,6 +205,20 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
+
+// Bulk tensor store of a shared-memory box (global coordinates {x, y}); out-of-range elements are
+// not written. Completion is tracked per thread with the bulk-group counters.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// All this thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All this thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_slot), "r"(ncols)
@@ -325,7 +344,8 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
 template <bool F32W, bool VEC4, bool FLAT, bool GN>
 __global__ void __maxnreg__(128)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
-                   const __grid_constant__ CUtensorMap tmap_a, const ConvArgs args) {
+                   const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_out,
+                   const __grid_constant__ CUtensorMap tmap_res, const ConvArgs args) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -364,11 +384,16 @@ __global__ void __maxnreg__(128)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (misc - base));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (misc + 4 - base));
     volatile int* s_wfills = reinterpret_cast<volatile int*>(gbase + (misc + 8 - base));
+    // Residual-block barriers of the bulk-store epilogue, one per drain warp.
+    auto res_bar = [&](int qd) { return misc + 16u + 8u * qd; };
     // Fill counts for the abort path: arrivals this converter thread made on the stage full
     // barriers, weight tiles and A boxes the TMA issuers armed (a CTA's chunk count stays below
     // 2^31, checked at launch). Each role derives its count from its loop position when it leaves
     // the loop, so no counter stays live in the hot loops.
     int conv_fills = 0, w_fills = 0, a_fills = 0;
+    // Bulk-store epilogue, drain lane 0: a residual load in flight and the phase it completes.
+    int res_pending = 0;
+    uint32_t res_phase = 0;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Converters: warps 10-13, plus warps 0-3 for 1×1 convs with TMA-fed A rows (the loader warps are
@@ -407,6 +432,7 @@ __global__ void __maxnreg__(128)
             mbar_init(acc_empty_bar(b), 128);
         }
         mbar_init(final_bar, 1);
+        for (int qd = 0; qd < 4; ++qd) mbar_init(res_bar(qd), 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -736,178 +762,264 @@ __global__ void __maxnreg__(128)
         const int row = qd * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
         const uint32_t srow = sum_base + (uint32_t)row * sum_stride;
-        const bool vec_out = (args.c_out & 3) == 0;
-        // Transposed (coalesced) stores for float4 outputs; a SiLU epilogue keeps one row per thread
-        // (inside the UNet its transposed form ran 22 % slower) unless statistics are gathered.
-        const bool transpose = vec_out && (!args.act || GN);
-        int gseg = 0;
-        bool live = true;
-        // Transposed epilogue: lane l owns the float4 column group l % 8 of rows 4i + l / 8 of each
-        // 32 × 32 block. Its bias and GroupNorm-add operands for a block are loaded one block ahead
-        // (the first block's before the accumulator wait), so no block waits out their latency
-        // (loaded per block, that wait cost the short-K 1×1 convs up to 16 %).
-        const int tj = lane & 7;
-        struct BlockIn {
-            float4 bias, gadd;
-        };
-        auto load_block = [&](int64_t t, int n0, int cc, BlockIn& in) {
-            const int col = n0 + cc + 4 * tj;
-            const bool ok = n0 + cc < args.c_out && col < args.c_out;  // c_out % 4 == 0: whole float4s
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            in.bias = args.bias && ok ? __ldg(reinterpret_cast<const float4*>(args.bias + col)) : z;
-            in.gadd = GN && args.gn_add && ok
-                          ? __ldg(reinterpret_cast<const float4*>(args.gn_add + (tile_m0(t) / hw_out) * args.c_out + col))
-                          : z;
-        };
-        for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
-            const int64_t m = tile_m0(t) + row;
-            const int n0 = tile_n0(t);
-            BlockIn cur;
-            for (int seg = 0; seg < nseg; ++seg, ++gseg) {
-                const int b = gseg & 1;
-                const bool last = seg + 1 == nseg;
-                if (last && transpose) load_block(t, n0, 0, cur);
-                if (!mbar_wait(acc_full_bar(b), (gseg >> 1) & 1, args.err, 6, abort_flag, true)) {
+        if (args.tma_out) {
+            // Bulk-store epilogue. This warp's bn/32 blocks of 32 rows × 32 columns sit in the sum
+            // buffer (4 KB each, 128-byte swizzle: float4 v of row r at r·128 + ((v ^ (r & 7))·16),
+            // the layout of a {32, 32} TMA box). A tile's residual blocks are loaded into them by TMA
+            // while the tile accumulates; the drain adds bias and residual while copying its row out
+            // of TMEM, releases the accumulator, and lane 0 stores the blocks with TMA (rows and
+            // columns outside the output are clipped by the tensor map).
+            const int nblk = bn / 32;
+            const uint32_t wreg = sum_base + (uint32_t)(qd * nblk) * 4096u;
+            const uint32_t rbar = res_bar(qd);
+            const uint32_t rrow = (uint32_t)lane * 128u;
+            const int x7 = lane & 7;
+            auto issue_res = [&](int64_t t) {  // lane 0
+                const int64_t m0 = tile_m0(t);
+                const int n0 = tile_n0(t);
+                int live_blocks = 0;
+                for (int cb = 0; cb < nblk; ++cb) live_blocks += n0 + 32 * cb < args.c_out ? 1 : 0;
+                mbar_arrive_expect_tx(rbar, (uint32_t)live_blocks * 4096u);
+                for (int cb = 0; cb < nblk; ++cb)
+                    if (n0 + 32 * cb < args.c_out)
+                        tma_load_2d(wreg + (uint32_t)cb * 4096u, &tmap_res, n0 + 32 * cb, (int)(m0 + 32 * qd), rbar);
+                res_pending = 1;
+            };
+            bool live = true;
+            int tcount = 0;
+            if (args.has_res && lane == 0 && (int64_t)blockIdx.x < tiles) issue_res(blockIdx.x);
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x, ++tcount) {
+                const int64_t m0 = tile_m0(t);
+                const int n0 = tile_n0(t);
+                const int b = tcount & 1;
+                if (!mbar_wait(acc_full_bar(b), (uint32_t)((tcount >> 1) & 1), args.err, 6, abort_flag, true)) {
                     live = false;
                     break;
                 }
                 tc_fence_after();
-                for (int cc = 0; cc < bn; cc += 32) {
+                if (args.has_res) {
+                    // The previous tile's stores finished reading the blocks before this load was issued.
+                    if (!mbar_wait(rbar, res_phase, args.err, 13, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    res_phase ^= 1u;
+                    res_pending = 0;
+                } else {
+                    if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the blocks
+                    __syncwarp();
+                }
+                for (int cb = 0; cb < nblk; ++cb) {
                     float acc[32];
-                    tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
-                    if (seg > 0) {
+                    tmem_ld32(lane_base + (uint32_t)(b * bn + 32 * cb), acc);
+                    const uint32_t blk = wreg + (uint32_t)cb * 4096u + rrow;
+                    const int c0 = n0 + 32 * cb;
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            const float4 r4 = ld_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u);
-                            acc[4 * v] = r4.x + acc[4 * v];
-                            acc[4 * v + 1] = r4.y + acc[4 * v + 1];
-                            acc[4 * v + 2] = r4.z + acc[4 * v + 2];
-                            acc[4 * v + 3] = r4.w + acc[4 * v + 3];
+                    for (int v = 0; v < 8; ++v) {
+                        const uint32_t addr = blk + ((uint32_t)(v ^ x7) << 4);
+                        float4 pre = args.bias && c0 + 4 * v < args.c_out
+                                         ? __ldg(reinterpret_cast<const float4*>(args.bias + c0 + 4 * v))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (args.has_res) {
+                            const float4 r4 = ld_shared_v4(addr);
+                            pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
                         }
-                    }
-                    if (!last || transpose) {
-#pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1],
-                                         acc[4 * v + 2], acc[4 * v + 3]);
-                        continue;
-                    }
-                    if (m >= args.m_total) continue;
-                    const int nb = n0 + cc;
-                    if (nb >= args.c_out) continue;
-                    // One row per thread: float4 stores (SiLU epilogues), or scalar stores for output
-                    // widths that are not a multiple of 4 (the VAE's 3-channel conv_out).
-                    float* dst = args.out + m * args.c_out + nb;
-                    const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
-                    if (vec_out && nb + 32 <= args.c_out) {
-#pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + v)
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (res) {
-                                const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
-                                pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
-                            }
-                            float4 o4 = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1],
-                                                    pre.z + acc[4 * v + 2], pre.w + acc[4 * v + 3]);
-                            if (args.act)
-                                o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
-                            reinterpret_cast<float4*>(dst)[v] = o4;
-                        }
-                    } else {
-                        const int lim = min(32, args.c_out - nb);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (i < lim) {
-                                float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
-                                if (res) pre = __ldg(res + i) + pre;
-                                const float o = pre + acc[i];
-                                dst[i] = args.act ? dev_silu(o) : o;
-                            }
-                        }
+                        st_shared_v4(addr, pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
+                                     pre.w + acc[4 * v + 3]);
                     }
                 }
-                // The accumulator has been read (into registers, or into the sum buffer for folds
-                // and transposed epilogues): the MMA warp may start the segment after next in it
-                // while the stores below run.
                 tc_fence_before();
                 mbar_arrive(acc_empty_bar(b));
-                if (!last || !transpose) continue;
-                __syncwarp();  // the rows written above are read by other lanes below
-                for (int cc = 0; cc < bn; cc += 32) {
-                    // Transposed stores: the warp's 32 × 32 block goes through this row's slot
-                    // of the (segment) sum buffer, so each store instruction writes four
-                    // whole 128-byte row pieces instead of 32 scattered 16-byte ones. The row stride
-                    // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
-                    BlockIn nxt;
-                    if (cc + 32 < bn) load_block(t, n0, cc + 32, nxt);
-                    const int nb = n0 + cc;
-                    if (nb < args.c_out) {
-                        const int col = nb + 4 * tj;
-                        const bool col_ok = col < args.c_out;
-                        const int64_t m_base = tile_m0(t) + qd * 32 + (lane >> 3);
-                        float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs;
-                        // All eight shared loads, then all eight residual loads, then the stores: a
-                        // residual load placed after a store would wait out its whole latency.
-                        float4 a4[8], r4[8];
+                fence_proxy_async_smem();  // the blocks' writes, before the bulk stores read them
+                __syncwarp();
+                if (lane == 0) {
+                    for (int cb = 0; cb < nblk; ++cb)
+                        if (n0 + 32 * cb < args.c_out)
+                            tma_store_2d(&tmap_out, n0 + 32 * cb, (int)(m0 + 32 * qd), wreg + (uint32_t)cb * 4096u);
+                    bulk_commit();
+                    const int64_t tn = t + gridDim.x;
+                    if (args.has_res && tn < tiles) {
+                        bulk_wait_read_all();
+                        issue_res(tn);
+                    }
+                }
+                __syncwarp();
+            }
+            if (lane == 0) bulk_wait_all();
+        } else {
+            const bool vec_out = (args.c_out & 3) == 0;
+            // Transposed (coalesced) stores for float4 outputs; a SiLU epilogue keeps one row per thread
+            // (inside the UNet its transposed form ran 22 % slower) unless statistics are gathered.
+            const bool transpose = vec_out && (!args.act || GN);
+            int gseg = 0;
+            bool live = true;
+            // Transposed epilogue: lane l owns the float4 column group l % 8 of rows 4i + l / 8 of each
+            // 32 × 32 block. Its bias and GroupNorm-add operands for a block are loaded one block ahead
+            // (the first block's before the accumulator wait), so no block waits out their latency
+            // (loaded per block, that wait cost the short-K 1×1 convs up to 16 %).
+            const int tj = lane & 7;
+            struct BlockIn {
+                float4 bias, gadd;
+            };
+            auto load_block = [&](int64_t t, int n0, int cc, BlockIn& in) {
+                const int col = n0 + cc + 4 * tj;
+                const bool ok = n0 + cc < args.c_out && col < args.c_out;  // c_out % 4 == 0: whole float4s
+                const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                in.bias = args.bias && ok ? __ldg(reinterpret_cast<const float4*>(args.bias + col)) : z;
+                in.gadd = GN && args.gn_add && ok
+                              ? __ldg(reinterpret_cast<const float4*>(args.gn_add + (tile_m0(t) / hw_out) * args.c_out + col))
+                              : z;
+            };
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+                const int64_t m = tile_m0(t) + row;
+                const int n0 = tile_n0(t);
+                BlockIn cur;
+                for (int seg = 0; seg < nseg; ++seg, ++gseg) {
+                    const int b = gseg & 1;
+                    const bool last = seg + 1 == nseg;
+                    if (last && transpose) load_block(t, n0, 0, cur);
+                    if (!mbar_wait(acc_full_bar(b), (gseg >> 1) & 1, args.err, 6, abort_flag, true)) {
+                        live = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int cc = 0; cc < bn; cc += 32) {
+                        float acc[32];
+                        tmem_ld32(lane_base + (uint32_t)(b * bn + cc), acc);
+                        if (seg > 0) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
-                                                 (uint32_t)(cc + 4 * tj) * 4u);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int64_t mr = m_base + 4 * i;
-                            r4[i] = args.residual && col_ok && mr < args.m_total
-                                        ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int64_t mr = m_base + 4 * i;
-                            if (mr >= args.m_total || !col_ok) continue;
-                            const float4 a = a4[i];
-                            const float4 pre = make_float4(r4[i].x + cur.bias.x, r4[i].y + cur.bias.y,
-                                                           r4[i].z + cur.bias.z, r4[i].w + cur.bias.w);
-                            float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
-                            // Only statistics-gathering convs reach this path with an activation (see
-                            // `transpose`). A runtime-only test let the compiler predicate the SiLU
-                            // instead of branching: 32 exp/divide pairs per block on every conv.
-                            if (GN && args.act)
-                                o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
-                            *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
-                            if constexpr (GN) {
-                                const float4 g = cur.gadd;
-                                const float4 y = make_float4(o4.x + g.x, o4.y + g.y, o4.z + g.z, o4.w + g.w);
-                                gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
-                                gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
-                                                 fmaf(y.w, y.w, gq.w));
+                            for (int v = 0; v < 8; ++v) {
+                                const float4 r4 = ld_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u);
+                                acc[4 * v] = r4.x + acc[4 * v];
+                                acc[4 * v + 1] = r4.y + acc[4 * v + 1];
+                                acc[4 * v + 2] = r4.z + acc[4 * v + 2];
+                                acc[4 * v + 3] = r4.w + acc[4 * v + 3];
                             }
                         }
-                        if constexpr (GN) {
-                            // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
-                            // order, so results do not depend on timing), then lanes 0-7 write the
-                            // warp's sums for their four channels.
+                        if (!last || transpose) {
 #pragma unroll
-                            for (int o = 8; o <= 16; o <<= 1) {
-                                gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
-                                gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
-                                gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
-                                gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
-                                gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
-                                gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
-                                gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
-                                gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
+                            for (int v = 0; v < 8; ++v)
+                                st_shared_v4(srow + (uint32_t)(cc + 4 * v) * 4u, acc[4 * v], acc[4 * v + 1],
+                                             acc[4 * v + 2], acc[4 * v + 3]);
+                            continue;
+                        }
+                        if (m >= args.m_total) continue;
+                        const int nb = n0 + cc;
+                        if (nb >= args.c_out) continue;
+                        // One row per thread: float4 stores (SiLU epilogues), or scalar stores for output
+                        // widths that are not a multiple of 4 (the VAE's 3-channel conv_out).
+                        float* dst = args.out + m * args.c_out + nb;
+                        const float* res = args.residual ? args.residual + m * args.c_out + nb : nullptr;
+                        if (vec_out && nb + 32 <= args.c_out) {
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                float4 pre = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + nb) + v)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (res) {
+                                    const float4 r4 = __ldg(reinterpret_cast<const float4*>(res) + v);
+                                    pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
+                                }
+                                float4 o4 = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1],
+                                                        pre.z + acc[4 * v + 2], pre.w + acc[4 * v + 3]);
+                                if (args.act)
+                                    o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                                reinterpret_cast<float4*>(dst)[v] = o4;
                             }
-                            if (lane < 8 && col_ok) {
-                                float* dst = args.gn_part + ((tile_m0(t) / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
-                                *reinterpret_cast<float4*>(dst) = gs;
-                                *reinterpret_cast<float4*>(dst + args.c_out) = gq;
+                        } else {
+                            const int lim = min(32, args.c_out - nb);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if (i < lim) {
+                                    float pre = args.bias ? __ldg(args.bias + nb + i) : 0.0f;
+                                    if (res) pre = __ldg(res + i) + pre;
+                                    const float o = pre + acc[i];
+                                    dst[i] = args.act ? dev_silu(o) : o;
+                                }
                             }
                         }
                     }
-                    if (cc + 32 < bn) cur = nxt;
+                    // The accumulator has been read (into registers, or into the sum buffer for folds
+                    // and transposed epilogues): the MMA warp may start the segment after next in it
+                    // while the stores below run.
+                    tc_fence_before();
+                    mbar_arrive(acc_empty_bar(b));
+                    if (!last || !transpose) continue;
+                    __syncwarp();  // the rows written above are read by other lanes below
+                    for (int cc = 0; cc < bn; cc += 32) {
+                        // Transposed stores: the warp's 32 × 32 block goes through this row's slot
+                        // of the (segment) sum buffer, so each store instruction writes four
+                        // whole 128-byte row pieces instead of 32 scattered 16-byte ones. The row stride
+                        // (bn + 4 words, ≡ 4 mod 32) keeps both passes free of bank conflicts.
+                        BlockIn nxt;
+                        if (cc + 32 < bn) load_block(t, n0, cc + 32, nxt);
+                        const int nb = n0 + cc;
+                        if (nb < args.c_out) {
+                            const int col = nb + 4 * tj;
+                            const bool col_ok = col < args.c_out;
+                            const int64_t m_base = tile_m0(t) + qd * 32 + (lane >> 3);
+                            float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs;
+                            // All eight shared loads, then all eight residual loads, then the stores: a
+                            // residual load placed after a store would wait out its whole latency.
+                            float4 a4[8], r4[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                a4[i] = ld_shared_v4(sum_base + (uint32_t)(qd * 32 + 4 * i + (lane >> 3)) * sum_stride +
+                                                     (uint32_t)(cc + 4 * tj) * 4u);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int64_t mr = m_base + 4 * i;
+                                r4[i] = args.residual && col_ok && mr < args.m_total
+                                            ? __ldg(reinterpret_cast<const float4*>(args.residual + mr * args.c_out + col))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int64_t mr = m_base + 4 * i;
+                                if (mr >= args.m_total || !col_ok) continue;
+                                const float4 a = a4[i];
+                                const float4 pre = make_float4(r4[i].x + cur.bias.x, r4[i].y + cur.bias.y,
+                                                               r4[i].z + cur.bias.z, r4[i].w + cur.bias.w);
+                                float4 o4 = make_float4(pre.x + a.x, pre.y + a.y, pre.z + a.z, pre.w + a.w);
+                                // Only statistics-gathering convs reach this path with an activation (see
+                                // `transpose`). A runtime-only test let the compiler predicate the SiLU
+                                // instead of branching: 32 exp/divide pairs per block on every conv.
+                                if (GN && args.act)
+                                    o4 = make_float4(dev_silu(o4.x), dev_silu(o4.y), dev_silu(o4.z), dev_silu(o4.w));
+                                *reinterpret_cast<float4*>(args.out + mr * args.c_out + col) = o4;
+                                if constexpr (GN) {
+                                    const float4 g = cur.gadd;
+                                    const float4 y = make_float4(o4.x + g.x, o4.y + g.y, o4.z + g.z, o4.w + g.w);
+                                    gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
+                                    gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
+                                                     fmaf(y.w, y.w, gq.w));
+                                }
+                            }
+                            if constexpr (GN) {
+                                // Lanes j, j + 8, j + 16, j + 24 hold the same columns: fold them (a fixed
+                                // order, so results do not depend on timing), then lanes 0-7 write the
+                                // warp's sums for their four channels.
+#pragma unroll
+                                for (int o = 8; o <= 16; o <<= 1) {
+                                    gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
+                                    gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
+                                    gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
+                                    gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
+                                    gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
+                                    gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
+                                    gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
+                                    gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
+                                }
+                                if (lane < 8 && col_ok) {
+                                    float* dst = args.gn_part + ((tile_m0(t) / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
+                                    *reinterpret_cast<float4*>(dst) = gs;
+                                    *reinterpret_cast<float4*>(dst + args.c_out) = gq;
+                                }
+                            }
+                        }
+                        if (cc + 32 < bn) cur = nxt;
+                    }
+                    __syncwarp();  // the slots are read before any lane overwrites them
                 }
-                __syncwarp();  // the slots are read before any lane overwrites them
             }
         }
     }
@@ -931,6 +1043,9 @@ __global__ void __maxnreg__(128)
         if (warp == 5 && lane == 1 && args.a_tma)
             for (int i = max(0, a_fills - nstg); i < a_fills; ++i)
                 drain_wait(sfull_bar(i % nstg), (uint32_t)((i / nstg) & 1), deadline, args.err, 11);
+        // A residual load of the bulk-store epilogue still in flight completes its barrier phase.
+        if (warp >= 6 && warp < 10 && lane == 0 && res_pending)
+            drain_wait(res_bar(warp & 3), res_phase, deadline, args.err, 14);
         __syncthreads();
     }
     if (warp == 4) {
@@ -996,7 +1111,8 @@ int stage_count(bool f32w, int bn) {
 }
 
 template <bool F32W, bool VEC4, bool FLAT, bool GN>
-void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtensorMap& tmap_a, int64_t m_tiles) {
+void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtensorMap& tmap_a,
+              const CUtensorMap& tmap_out, const CUtensorMap& tmap_res, int64_t m_tiles) {
     auto kernel = conv_tc_kernel<F32W, VEC4, FLAT, GN>;
     const int stage = (F32W ? 2 : 1) * a.bn * 128;
     const int smem = a.stages * stage + a.stg_slots * (int)A_BYTES + sum_bytes(a.bn) + 1024 + 512;
@@ -1015,7 +1131,8 @@ void run_conv(mbx_ctx* ctx, const mbx_param* p, const ConvArgs& a, const CUtenso
     (void)m_tiles;
     // Persistent: one CTA per SM (the shared-memory footprint allows one), tiles strided over them.
     const int64_t blocks = std::min<int64_t>(a.tiles, (int64_t)ctx->sm_count);
-    kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, tmap_a, a);
+    kernel<<<(unsigned)blocks, kThreads, smem, ctx->stream>>>(p->tmap_hi, F32W ? p->tmap_lo : p->tmap_hi, tmap_a,
+                                                              tmap_out, tmap_res, a);
 }
 
 }  // namespace
@@ -1165,22 +1282,38 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
             encode_a_map(&tmap_a, x, 4, dims, strides, box);
         }
     }
+    // Bulk-store epilogue: one K segment per tile, float4 outputs, no activation, no statistics.
+    CUtensorMap tmap_out = p->tmap_hi, tmap_res = p->tmap_hi;  // unused unless tma_out
+    a.tma_out = 0;
+    a.has_res = 0;
+    const int seg_cap = f32w ? kSegMaxChunksF32 : kSegMaxChunksF16;
+    if ((p->c_out & 3) == 0 && act == 0 && !gn_part && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
+        a.tma_out = 1;
+        cuuint64_t dims[2] = {(cuuint64_t)p->c_out, (cuuint64_t)a.m_total};
+        cuuint64_t strides[1] = {(cuuint64_t)p->c_out * 4};
+        cuuint32_t box[2] = {32, 32};
+        encode_a_map(&tmap_out, out, 2, dims, strides, box);
+        if (residual) {
+            a.has_res = 1;
+            encode_a_map(&tmap_res, residual, 2, dims, strides, box);
+        }
+    }
     auto dispatch = [&](auto gn) {
         constexpr bool G = decltype(gn)::value;
         if (a.flat) {
             if (f32w)
-                vec4 ? run_conv<true, true, true, G>(ctx, p, a, tmap_a, m_tiles)
-                     : run_conv<true, false, true, G>(ctx, p, a, tmap_a, m_tiles);
+                vec4 ? run_conv<true, true, true, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles)
+                     : run_conv<true, false, true, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles);
             else
-                vec4 ? run_conv<false, true, true, G>(ctx, p, a, tmap_a, m_tiles)
-                     : run_conv<false, false, true, G>(ctx, p, a, tmap_a, m_tiles);
+                vec4 ? run_conv<false, true, true, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles)
+                     : run_conv<false, false, true, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles);
         } else {
             if (f32w)
-                vec4 ? run_conv<true, true, false, G>(ctx, p, a, tmap_a, m_tiles)
-                     : run_conv<true, false, false, G>(ctx, p, a, tmap_a, m_tiles);
+                vec4 ? run_conv<true, true, false, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles)
+                     : run_conv<true, false, false, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles);
             else
-                vec4 ? run_conv<false, true, false, G>(ctx, p, a, tmap_a, m_tiles)
-                     : run_conv<false, false, false, G>(ctx, p, a, tmap_a, m_tiles);
+                vec4 ? run_conv<false, true, false, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles)
+                     : run_conv<false, false, false, G>(ctx, p, a, tmap_a, tmap_out, tmap_res, m_tiles);
         }
     };
     if (gn_part)
