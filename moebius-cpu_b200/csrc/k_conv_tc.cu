@@ -792,6 +792,16 @@ __global__ void __maxnreg__(128)
                 const int64_t m0 = tile_m0(t);
                 const int n0 = tile_n0(t);
                 const int b = tcount & 1;
+                // The tile's bias, loaded before the accumulator wait: lane l holds float4 groups l and
+                // l + 32 of the tile's columns (bn ≤ 256); the drain shuffles each out when it is needed.
+                float4 bias_q[2];
+#pragma unroll
+                for (int sq = 0; sq < 2; ++sq) {
+                    const int c = n0 + 4 * (lane + 32 * sq);
+                    bias_q[sq] = args.bias && 4 * (lane + 32 * sq) < bn && c < args.c_out
+                                     ? __ldg(reinterpret_cast<const float4*>(args.bias + c))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
                 if (!mbar_wait(acc_full_bar(b), (uint32_t)((tcount >> 1) & 1), args.err, 6, abort_flag, true)) {
                     live = false;
                     break;
@@ -813,13 +823,13 @@ __global__ void __maxnreg__(128)
                     float acc[32];
                     tmem_ld32(lane_base + (uint32_t)(b * bn + 32 * cb), acc);
                     const uint32_t blk = wreg + (uint32_t)cb * 4096u + rrow;
-                    const int c0 = n0 + 32 * cb;
+                    const float4 bsel = cb < 4 ? bias_q[0] : bias_q[1];  // groups 8·cb … 8·cb + 7
 #pragma unroll
                     for (int v = 0; v < 8; ++v) {
                         const uint32_t addr = blk + ((uint32_t)(v ^ x7) << 4);
-                        float4 pre = args.bias && c0 + 4 * v < args.c_out
-                                         ? __ldg(reinterpret_cast<const float4*>(args.bias + c0 + 4 * v))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const int src = (8 * cb + v) & 31;
+                        float4 pre = make_float4(__shfl_sync(0xffffffffu, bsel.x, src), __shfl_sync(0xffffffffu, bsel.y, src),
+                                                 __shfl_sync(0xffffffffu, bsel.z, src), __shfl_sync(0xffffffffu, bsel.w, src));
                         if (args.has_res) {
                             const float4 r4 = ld_shared_v4(addr);
                             pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
