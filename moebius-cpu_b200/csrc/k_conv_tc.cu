@@ -96,8 +96,8 @@ struct ConvArgs {
     // and tap from a 4-D map [n][h][w][c_in] (3×3, stride 1, no upsample; the box's zero fill
     // outside the map is the padding).
     int a_tma, a_bw;
-    // Epilogue by bulk tensor stores (single-segment tiles, float4 outputs, no activation, no
-    // statistics): the drain adds bias and residual while copying the accumulator into 32 × 32
+    // Epilogue by bulk tensor stores (single-segment tiles, float4 outputs, no statistics): the
+    // drain adds bias and residual (then the activation) while copying the accumulator into 32 × 32
     // swizzled blocks in shared memory, and one lane per warp stores them with TMA; the residual
     // blocks arrive by TMA beforehand (has_res).
     int tma_out, has_res;
@@ -766,9 +766,9 @@ __global__ void __maxnreg__(128)
             // Bulk-store epilogue. This warp's bn/32 blocks of 32 rows × 32 columns sit in the sum
             // buffer (4 KB each, 128-byte swizzle: float4 v of row r at r·128 + ((v ^ (r & 7))·16),
             // the layout of a {32, 32} TMA box). A tile's residual blocks are loaded into them by TMA
-            // while the tile accumulates; the drain adds bias and residual while copying its row out
-            // of TMEM, releases the accumulator, and lane 0 stores the blocks with TMA (rows and
-            // columns outside the output are clipped by the tensor map).
+            // while the tile accumulates; the drain adds bias and residual (then the activation)
+            // while copying its row out of TMEM, releases the accumulator, and lane 0 stores the
+            // blocks with TMA (rows and columns outside the output are clipped by the tensor map).
             const int nblk = bn / 32;
             const uint32_t wreg = sum_base + (uint32_t)(qd * nblk) * 4096u;
             const uint32_t rbar = res_bar(qd);
@@ -819,7 +819,11 @@ __global__ void __maxnreg__(128)
                     if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the blocks
                     __syncwarp();
                 }
-                for (int cb = 0; cb < nblk; ++cb) {
+                // One 32-column block of this thread's row: + bias (+ residual) [→ SiLU] into the block.
+                // The activation is a template argument: a runtime test inside the loop would be
+                // predicated into every block.
+                auto drain_block = [&](auto act_tag, int cb) {
+                    constexpr bool ACT = decltype(act_tag)::value;
                     float acc[32];
                     tmem_ld32(lane_base + (uint32_t)(b * bn + 32 * cb), acc);
                     const uint32_t blk = wreg + (uint32_t)cb * 4096u + rrow;
@@ -834,9 +838,17 @@ __global__ void __maxnreg__(128)
                             const float4 r4 = ld_shared_v4(addr);
                             pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
                         }
-                        st_shared_v4(addr, pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
-                                     pre.w + acc[4 * v + 3]);
+                        float4 o = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
+                                               pre.w + acc[4 * v + 3]);
+                        if constexpr (ACT) o = make_float4(dev_silu(o.x), dev_silu(o.y), dev_silu(o.z), dev_silu(o.w));
+                        st_shared_v4(addr, o.x, o.y, o.z, o.w);
                     }
+                };
+                for (int cb = 0; cb < nblk; ++cb) {
+                    if (args.act)
+                        drain_block(std::true_type{}, cb);
+                    else
+                        drain_block(std::false_type{}, cb);
                 }
                 tc_fence_before();
                 mbar_arrive(acc_empty_bar(b));
@@ -1292,12 +1304,12 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
             encode_a_map(&tmap_a, x, 4, dims, strides, box);
         }
     }
-    // Bulk-store epilogue: one K segment per tile, float4 outputs, no activation, no statistics.
+    // Bulk-store epilogue: one K segment per tile, float4 outputs, no statistics.
     CUtensorMap tmap_out = p->tmap_hi, tmap_res = p->tmap_hi;  // unused unless tma_out
     a.tma_out = 0;
     a.has_res = 0;
     const int seg_cap = f32w ? kSegMaxChunksF32 : kSegMaxChunksF16;
-    if ((p->c_out & 3) == 0 && act == 0 && !gn_part && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
+    if ((p->c_out & 3) == 0 && !gn_part && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
         a.tma_out = 1;
         cuuint64_t dims[2] = {(cuuint64_t)p->c_out, (cuuint64_t)a.m_total};
         cuuint64_t strides[1] = {(cuuint64_t)p->c_out * 4};
