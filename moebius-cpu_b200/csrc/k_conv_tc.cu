@@ -96,8 +96,8 @@ struct ConvArgs {
     // and tap from a 4-D map [n][h][w][c_in] (3×3, stride 1, no upsample; the box's zero fill
     // outside the map is the padding).
     int a_tma, a_bw;
-    // Epilogue by bulk tensor stores (single-segment tiles, float4 outputs, no statistics): the
-    // drain adds bias and residual (then the activation) while copying the accumulator into 32 × 32
+    // Epilogue by bulk tensor stores (single-segment tiles, float4 outputs): the drain adds bias
+    // and residual (then the activation) while copying the accumulator into 32 × 32
     // swizzled blocks in shared memory, and one lane per warp stores them with TMA; the residual
     // blocks arrive by TMA beforehand (has_res).
     int tma_out, has_res;
@@ -794,12 +794,16 @@ __global__ void __maxnreg__(128)
                 const int b = tcount & 1;
                 // The tile's bias, loaded before the accumulator wait: lane l holds float4 groups l and
                 // l + 32 of the tile's columns (bn ≤ 256); the drain shuffles each out when it is needed.
-                float4 bias_q[2];
+                float4 bias_q[2], gadd_q[2];
 #pragma unroll
                 for (int sq = 0; sq < 2; ++sq) {
                     const int c = n0 + 4 * (lane + 32 * sq);
-                    bias_q[sq] = args.bias && 4 * (lane + 32 * sq) < bn && c < args.c_out
-                                     ? __ldg(reinterpret_cast<const float4*>(args.bias + c))
+                    const bool ok = 4 * (lane + 32 * sq) < bn && c < args.c_out;
+                    bias_q[sq] = args.bias && ok ? __ldg(reinterpret_cast<const float4*>(args.bias + c))
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                    // GroupNorm add of the tile's item (its rows all belong to one item).
+                    gadd_q[sq] = GN && args.gn_add && ok
+                                     ? __ldg(reinterpret_cast<const float4*>(args.gn_add + (m0 / hw_out) * args.c_out + c))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
                 if (!mbar_wait(acc_full_bar(b), (uint32_t)((tcount >> 1) & 1), args.err, 6, abort_flag, true)) {
@@ -859,6 +863,51 @@ __global__ void __maxnreg__(128)
                         if (n0 + 32 * cb < args.c_out)
                             tma_store_2d(&tmap_out, n0 + 32 * cb, (int)(m0 + 32 * qd), wreg + (uint32_t)cb * 4096u);
                     bulk_commit();
+                }
+                if constexpr (GN) {
+                    // GroupNorm statistics of y = out + add over this warp's 32 rows, read back from the
+                    // blocks while the stores run: lane l takes float4 group l % 8 of rows 4i + l / 8,
+                    // two shuffles fold the lanes sharing those columns (a fixed order), and lanes 0-7
+                    // write the warp's sums: [M tile][warp][2][c_out]. Fusable shapes have whole M tiles.
+                    const int j = lane & 7;
+                    for (int cb = 0; cb < nblk; ++cb) {
+                        const int col = n0 + 32 * cb + 4 * j;
+                        const float4 gsel = cb < 4 ? gadd_q[0] : gadd_q[1];
+                        const int src = (8 * cb + j) & 31;
+                        const float4 g = make_float4(__shfl_sync(0xffffffffu, gsel.x, src),
+                                                     __shfl_sync(0xffffffffu, gsel.y, src),
+                                                     __shfl_sync(0xffffffffu, gsel.z, src),
+                                                     __shfl_sync(0xffffffffu, gsel.w, src));
+                        float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), gq = gs;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = 4 * i + (lane >> 3);
+                            const float4 o = ld_shared_v4(wreg + (uint32_t)cb * 4096u + (uint32_t)r * 128u +
+                                                          ((uint32_t)(j ^ (r & 7)) << 4));
+                            const float4 y = make_float4(o.x + g.x, o.y + g.y, o.z + g.z, o.w + g.w);
+                            gs = make_float4(gs.x + y.x, gs.y + y.y, gs.z + y.z, gs.w + y.w);
+                            gq = make_float4(fmaf(y.x, y.x, gq.x), fmaf(y.y, y.y, gq.y), fmaf(y.z, y.z, gq.z),
+                                             fmaf(y.w, y.w, gq.w));
+                        }
+#pragma unroll
+                        for (int o = 8; o <= 16; o <<= 1) {
+                            gs.x += __shfl_xor_sync(0xffffffffu, gs.x, o);
+                            gs.y += __shfl_xor_sync(0xffffffffu, gs.y, o);
+                            gs.z += __shfl_xor_sync(0xffffffffu, gs.z, o);
+                            gs.w += __shfl_xor_sync(0xffffffffu, gs.w, o);
+                            gq.x += __shfl_xor_sync(0xffffffffu, gq.x, o);
+                            gq.y += __shfl_xor_sync(0xffffffffu, gq.y, o);
+                            gq.z += __shfl_xor_sync(0xffffffffu, gq.z, o);
+                            gq.w += __shfl_xor_sync(0xffffffffu, gq.w, o);
+                        }
+                        if (lane < 8 && col < args.c_out) {
+                            float* dst = args.gn_part + ((m0 / BM) * 4 + qd) * 2 * (int64_t)args.c_out + col;
+                            *reinterpret_cast<float4*>(dst) = gs;
+                            *reinterpret_cast<float4*>(dst + args.c_out) = gq;
+                        }
+                    }
+                }
+                if (lane == 0) {
                     const int64_t tn = t + gridDim.x;
                     if (args.has_res && tn < tiles) {
                         bulk_wait_read_all();
@@ -1304,12 +1353,12 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
             encode_a_map(&tmap_a, x, 4, dims, strides, box);
         }
     }
-    // Bulk-store epilogue: one K segment per tile, float4 outputs, no statistics.
+    // Bulk-store epilogue: one K segment per tile, float4 outputs.
     CUtensorMap tmap_out = p->tmap_hi, tmap_res = p->tmap_hi;  // unused unless tma_out
     a.tma_out = 0;
     a.has_res = 0;
     const int seg_cap = f32w ? kSegMaxChunksF32 : kSegMaxChunksF16;
-    if ((p->c_out & 3) == 0 && !gn_part && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
+    if ((p->c_out & 3) == 0 && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
         a.tma_out = 1;
         cuuint64_t dims[2] = {(cuuint64_t)p->c_out, (cuuint64_t)a.m_total};
         cuuint64_t strides[1] = {(cuuint64_t)p->c_out * 4};
