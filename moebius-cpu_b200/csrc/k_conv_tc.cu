@@ -786,12 +786,11 @@ __global__ void __maxnreg__(128)
                 res_pending = 1;
             };
             bool live = true;
-            int tcount = 0;
+            int gseg = 0;  // accumulator segments drained so far (the MMA warp's count)
             if (args.has_res && lane == 0 && (int64_t)blockIdx.x < tiles) issue_res(blockIdx.x);
-            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x, ++tcount) {
+            for (int64_t t = blockIdx.x; live && t < tiles; t += gridDim.x) {
                 const int64_t m0 = tile_m0(t);
                 const int n0 = tile_n0(t);
-                const int b = tcount & 1;
                 // The tile's bias, loaded before the accumulator wait: lane l holds float4 groups l and
                 // l + 32 of the tile's columns (bn ≤ 256); the drain shuffles each out when it is needed.
                 float4 bias_q[2], gadd_q[2];
@@ -806,56 +805,86 @@ __global__ void __maxnreg__(128)
                                      ? __ldg(reinterpret_cast<const float4*>(args.gn_add + (m0 / hw_out) * args.c_out + c))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                if (!mbar_wait(acc_full_bar(b), (uint32_t)((tcount >> 1) & 1), args.err, 6, abort_flag, true)) {
+                bool seg_live = true;
+                for (int seg = 0; seg < nseg; ++seg, ++gseg) {
+                    const int b = gseg & 1;
+                    const bool first = seg == 0, last = seg + 1 == nseg;
+                    if (!mbar_wait(acc_full_bar(b), (uint32_t)((gseg >> 1) & 1), args.err, 6, abort_flag, true)) {
+                        seg_live = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (first) {
+                        if (args.has_res) {
+                            // The previous tile's stores finished reading the blocks before this load
+                            // was issued.
+                            if (!mbar_wait(rbar, res_phase, args.err, 13, abort_flag, true)) {
+                                seg_live = false;
+                                break;
+                            }
+                            res_phase ^= 1u;
+                            res_pending = 0;
+                        } else {
+                            if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the blocks
+                            __syncwarp();
+                        }
+                    }
+                    // One 32-column block of this thread's row into the block: the first segment adds
+                    // bias (+ residual) to its sum, later ones fold theirs into the running value, the
+                    // last one then applies the activation. Both choices are template arguments: a
+                    // runtime test inside the loop would be predicated into every block.
+                    auto drain_block = [&](auto first_tag, auto act_tag, int cb) {
+                        constexpr bool FIRST = decltype(first_tag)::value;
+                        constexpr bool ACT = decltype(act_tag)::value;
+                        float acc[32];
+                        tmem_ld32(lane_base + (uint32_t)(b * bn + 32 * cb), acc);
+                        const uint32_t blk = wreg + (uint32_t)cb * 4096u + rrow;
+                        const float4 bsel = cb < 4 ? bias_q[0] : bias_q[1];  // groups 8·cb … 8·cb + 7
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            const uint32_t addr = blk + ((uint32_t)(v ^ x7) << 4);
+                            float4 pre;
+                            if constexpr (FIRST) {
+                                const int src = (8 * cb + v) & 31;
+                                pre = make_float4(__shfl_sync(0xffffffffu, bsel.x, src),
+                                                  __shfl_sync(0xffffffffu, bsel.y, src),
+                                                  __shfl_sync(0xffffffffu, bsel.z, src),
+                                                  __shfl_sync(0xffffffffu, bsel.w, src));
+                                if (args.has_res) {
+                                    const float4 r4 = ld_shared_v4(addr);
+                                    pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
+                                }
+                            } else {
+                                pre = ld_shared_v4(addr);  // the running value
+                            }
+                            float4 o = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
+                                                   pre.w + acc[4 * v + 3]);
+                            if constexpr (ACT)
+                                o = make_float4(dev_silu(o.x), dev_silu(o.y), dev_silu(o.z), dev_silu(o.w));
+                            st_shared_v4(addr, o.x, o.y, o.z, o.w);
+                        }
+                    };
+                    const bool act_now = last && args.act;
+                    for (int cb = 0; cb < nblk; ++cb) {
+                        if (first) {
+                            if (act_now)
+                                drain_block(std::true_type{}, std::true_type{}, cb);
+                            else
+                                drain_block(std::true_type{}, std::false_type{}, cb);
+                        } else {
+                            if (act_now)
+                                drain_block(std::false_type{}, std::true_type{}, cb);
+                            else
+                                drain_block(std::false_type{}, std::false_type{}, cb);
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(acc_empty_bar(b));
+                }
+                if (!seg_live) {
                     live = false;
                     break;
                 }
-                tc_fence_after();
-                if (args.has_res) {
-                    // The previous tile's stores finished reading the blocks before this load was issued.
-                    if (!mbar_wait(rbar, res_phase, args.err, 13, abort_flag, true)) {
-                        live = false;
-                        break;
-                    }
-                    res_phase ^= 1u;
-                    res_pending = 0;
-                } else {
-                    if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the blocks
-                    __syncwarp();
-                }
-                // One 32-column block of this thread's row: + bias (+ residual) [→ SiLU] into the block.
-                // The activation is a template argument: a runtime test inside the loop would be
-                // predicated into every block.
-                auto drain_block = [&](auto act_tag, int cb) {
-                    constexpr bool ACT = decltype(act_tag)::value;
-                    float acc[32];
-                    tmem_ld32(lane_base + (uint32_t)(b * bn + 32 * cb), acc);
-                    const uint32_t blk = wreg + (uint32_t)cb * 4096u + rrow;
-                    const float4 bsel = cb < 4 ? bias_q[0] : bias_q[1];  // groups 8·cb … 8·cb + 7
-#pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        const uint32_t addr = blk + ((uint32_t)(v ^ x7) << 4);
-                        const int src = (8 * cb + v) & 31;
-                        float4 pre = make_float4(__shfl_sync(0xffffffffu, bsel.x, src), __shfl_sync(0xffffffffu, bsel.y, src),
-                                                 __shfl_sync(0xffffffffu, bsel.z, src), __shfl_sync(0xffffffffu, bsel.w, src));
-                        if (args.has_res) {
-                            const float4 r4 = ld_shared_v4(addr);
-                            pre = make_float4(r4.x + pre.x, r4.y + pre.y, r4.z + pre.z, r4.w + pre.w);
-                        }
-                        float4 o = make_float4(pre.x + acc[4 * v], pre.y + acc[4 * v + 1], pre.z + acc[4 * v + 2],
-                                               pre.w + acc[4 * v + 3]);
-                        if constexpr (ACT) o = make_float4(dev_silu(o.x), dev_silu(o.y), dev_silu(o.z), dev_silu(o.w));
-                        st_shared_v4(addr, o.x, o.y, o.z, o.w);
-                    }
-                };
-                for (int cb = 0; cb < nblk; ++cb) {
-                    if (args.act)
-                        drain_block(std::true_type{}, cb);
-                    else
-                        drain_block(std::false_type{}, cb);
-                }
-                tc_fence_before();
-                mbar_arrive(acc_empty_bar(b));
                 fence_proxy_async_smem();  // the blocks' writes, before the bulk stores read them
                 __syncwarp();
                 if (lane == 0) {
@@ -1353,12 +1382,11 @@ void launch_conv_tc(mbx_ctx* ctx, const float* x, const ConvShape& s, const mbx_
             encode_a_map(&tmap_a, x, 4, dims, strides, box);
         }
     }
-    // Bulk-store epilogue: one K segment per tile, float4 outputs.
+    // Bulk-store epilogue: float4 outputs.
     CUtensorMap tmap_out = p->tmap_hi, tmap_res = p->tmap_hi;  // unused unless tma_out
     a.tma_out = 0;
     a.has_res = 0;
-    const int seg_cap = f32w ? kSegMaxChunksF32 : kSegMaxChunksF16;
-    if ((p->c_out & 3) == 0 && a.k_chunks <= seg_cap && a.m_total < (int64_t(1) << 31)) {
+    if ((p->c_out & 3) == 0 && a.m_total < (int64_t(1) << 31)) {
         a.tma_out = 1;
         cuuint64_t dims[2] = {(cuuint64_t)p->c_out, (cuuint64_t)a.m_total};
         cuuint64_t strides[1] = {(cuuint64_t)p->c_out * 4};
