@@ -198,7 +198,9 @@ int32_t mbx_conv1x1(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t 
  * pro_shift[item,c]) (pro_scale/pro_shift [n, c_in] or NULL; reference:
  * GroupNorm::forward feeding the conv, src/unet/transformer.rs:324-325), and an
  * epilogue activation `act` (MBX_ACT_*) after bias and residual (reference:
- * Conv1x1::forward then silu_inplace, src/unet/transformer.rs:351-352). */
+ * Conv1x1::forward then silu_inplace, src/unet/transformer.rs:351-352). With a
+ * prologue the library first writes the normalised input into pool scratch of
+ * x's size (one memory-bound pass), then runs the conv on it. */
 int32_t mbx_conv1x1_fused(mbx_ctx *ctx, const float *x, int64_t n, int64_t h, int64_t w, int64_t c_in,
                           const mbx_param *weight, const float *bias, const float *pro_scale,
                           const float *pro_shift, int32_t pro_silu, const float *residual, int32_t act,
@@ -212,7 +214,8 @@ int32_t mbx_conv3x3_output_hw(int64_t h, int64_t w, int64_t stride, const int64_
  * pad = [top, left, bottom, right], optional nearest-2x upsample of the input
  * read on the fly, optional GroupNorm prologue: the input is read as
  * [SiLU](x*pro_scale[item,c] + pro_shift[item,c]) at in-image taps while padding
- * stays zero (pro_scale/pro_shift [n, c_in] or NULL), bias, optional residual
+ * stays zero (pro_scale/pro_shift [n, c_in] or NULL; applied as one pass into pool
+ * scratch of x's size before the conv), bias, optional residual
  * [n, ho, wo, c_out] added in the epilogue.
  * Reference: Conv3x3::{forward, forward_prologue, forward_im2col},
  * src/engine/conv.rs:83-130 (Winograd for stride 1 / pad 1, src/engine/winograd.rs:48-120).
