@@ -7,7 +7,7 @@ libmoebius_cuda.so.
 A small C host that calls every entry point the way a moebius-cpu host would
 is compiled with gcc against this repository's header and linked to the
 library. Where the reference checkout is available (MOEBIUS_REFERENCE_ROOT,
-default /root/reference), the same host is also compiled against the
+default: a `reference` directory beside this repository), the same host is also compiled against the
 reference's own header, unmodified, and linked to this library, and the
 struct layouts seen through both headers are compared. Without a GPU,
 engine creation must fail with the reference's MOEBIUS_ERR_UNSUPPORTED_CPU
@@ -24,7 +24,7 @@ from conftest import REPO, load_package
 
 LIBDIR = os.path.join(REPO, "moebius-cpu_b200", "lib")
 OUR_INCLUDE = os.path.join(REPO, "include")
-REF_ROOT = os.environ.get("MOEBIUS_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("MOEBIUS_REFERENCE_ROOT", os.path.join(os.path.dirname(REPO), "reference"))
 REF_INCLUDE = os.path.join(REF_ROOT, "include")
 
 HOST_C = r"""
